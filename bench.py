@@ -1,0 +1,508 @@
+#!/usr/bin/env python
+"""Benchmark of the TurboQuant 4bit_nc decode hot path (Stage1 + Stage2).
+
+One JSON line on rank 0.  A "step" is one decode pass of one attention layer
+over the whole batch: Stage1 (split-KV partial attention over the 4-bit
+paged cache) followed by the Stage2 split merge, inputs resident in HBM.
+``value`` is decode tokens/s (sequences decoded per second, summed over all
+ranks) from CUDA events around exactly ``--steps`` steps, max over ranks.
+
+Default workload (``--config c1``): the reference's fixed Qwen3-4B shape,
+B=64, context 4096, 32 Q / 8 KV heads, D=128, block 16, 32 splits, SoA cache
+written by the sm_100a store from seeded N(0,1) keys/values and a seeded
+random rotation, shuffled physical block pool.  Under torchrun each rank
+runs its own copy (data-parallel over batch, weak scaling, no collective on
+the data path).
+
+``--impl reference`` times the reference algorithm on the host CPU (the
+fp32 C restatement in ``oracle/``, all host threads) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "turboquant-cuda-decode_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: (B, seq_len, Hq, Hk, splits)
+    "c1": dict(B=64, L=4096, Hq=32, Hk=8, S=32,
+               workload="Qwen3-4B decode Stage1+Stage2, B64 x 4096 ctx, Hq32/Hk8, D128, bs16, 32 splits"),
+}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--layout", choices=["soa", "aos"], default="soa")
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+
+def orthogonal(seed: int, d: int = 128) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    q, r = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64))
+    return (q * torch.sign(torch.diagonal(r))[None, :]).to(torch.float32)
+
+
+def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
+    """Seeded cache written by the sm_100a store, plus decode inputs."""
+    import tqb
+    from tqb import layout as L
+
+    B, Lc, Hq, Hk, S = cfg["B"], cfg["L"], cfg["Hq"], cfg["Hk"], cfg["S"]
+    pages = math.ceil(Lc / L.BLOCK_SIZE)
+    nblk = B * pages
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    cents = tqb.get_centroids(128, 4).to(dev)
+    mids = tqb.get_midpoints(cents)
+    R = orthogonal(seed + 1).to(dev)
+    perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
+    bt = perm.reshape(B, pages).to(dev)
+    kv = torch.zeros(nblk, L.BLOCK_SIZE, Hk, L.SLOT_SIZE, dtype=torch.uint8, device=dev)
+    chunk = 8192
+    tok_b = torch.arange(Lc, device=dev)
+    for b in range(B):
+        slots_b = (bt[b, tok_b // 16].long() * 16 + tok_b % 16).to(torch.int32)
+        for s0 in range(0, Lc, chunk):
+            n = min(chunk, Lc - s0)
+            key = torch.randn(n, Hk, 128, generator=gen, device=dev)
+            val = torch.randn(n, Hk, 128, generator=gen, device=dev)
+            tqb.triton_turboquant_store(key, val, kv, slots_b[s0:s0 + n], R, mids, 4, 66, 4,
+                                        centroids=cents, norm_correction=(layout == "soa"),
+                                        layout=layout)
+    query = torch.randn(B, Hq, 128, generator=gen, device=dev).to(torch.bfloat16)
+    q_rot = (query.float() @ R).contiguous()
+    seq_lens = torch.full((B,), Lc, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    return dict(kv=kv, bt=bt, seq_lens=seq_lens, cents=cents, R=R, query=query, q_rot=q_rot,
+                B=B, Hq=Hq, Hk=Hk, S=S, L=Lc, layout=layout)
+
+
+def algorithmic_bytes(w) -> int:
+    """Bytes Stage1 must move: the cache slots of every token-head (134 B),
+    the fp32 query, the block-table entries used, seq_lens, the centroid
+    table, and the fp32 mid_o write."""
+    B, Hq, Hk, S, Lc = w["B"], w["Hq"], w["Hk"], w["S"], w["L"]
+    cache = B * Lc * Hk * 134
+    q = B * Hq * 128 * 4
+    bt = B * math.ceil(Lc / 16) * 4
+    mid = B * Hq * S * 129 * 4
+    return cache + q + bt + B * 4 + 16 * 4 + mid
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML)
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, dev: torch.device, period_s: float = 0.002):
+        self.samples = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._t = None
+        self.window = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            try:  # map the CUDA device to its NVML handle by UUID
+                uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+                ids = [int(x) for x in vis.split(",") if x.strip().isdigit()]
+                idx = ids[dev.index] if dev.index < len(ids) else dev.index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:  # pragma: no cover - NVML missing
+            self.nvml = None
+            self.max_mhz = None
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+                reasons = self._reasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nvml is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        inside = [s for s in self.samples if self.window and self.window[0] <= s[0] <= self.window[1]]
+        use = inside if inside else self.samples
+        mask = 0
+        for _, _, r in use:
+            mask |= r
+        reasons = [k for k, bit in self.REASONS.items() if mask & bit]
+        return {"sm_mhz": statistics.median(m for _, m, _ in use), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(use),
+                "window": "timed region" if inside else "warm-up + timed region"}
+
+
+# ---------------------------------------------------------------------------
+# measured numbers committed under profiles/
+# ---------------------------------------------------------------------------
+
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(config: str, layout: str):
+    """DRAM bytes per Stage1 launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"stage1_{layout}_{config}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (reference algorithm on the host cores)
+# ---------------------------------------------------------------------------
+
+
+def cpu_baseline(w, min_seconds=3.0):
+    from oracle import oracle as O
+
+    cores = O.default_threads()
+    q = w["q_rot"].cpu().numpy()
+    kv = w["kv"].cpu().numpy()
+    bt = w["bt"].cpu().numpy()
+    sl = w["seq_lens"].cpu().numpy()
+    cents = w["cents"].cpu().numpy()
+    lay = O.LAYOUT_SOA if w["layout"] == "soa" else O.LAYOUT_AOS
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        mid = O.stage1(q, kv, bt, sl, cents, w["S"], layout=lay, nthreads=cores)
+        O.stage2(mid, sl, nthreads=cores)
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": w["B"] / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"full B{w['B']} x {w['L']} workload, Stage1+Stage2, fp32 C restatement "
+                      f"of reference/soa_decode_v1.py + baseline/stage2.py, {reps} rep(s), "
+                      f"{dt * 1e3:.1f} ms each"}
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+
+def build_workload_cpu(cfg: dict, seed: int, layout: str):
+    """Host-only copy of the workload for the reference arm: seeded numpy
+    keys/values written by the oracle store (reference store semantics)."""
+    from oracle import oracle as O
+    import tqb
+
+    B, Lc, Hq, Hk, S = cfg["B"], cfg["L"], cfg["Hq"], cfg["Hk"], cfg["S"]
+    pages = math.ceil(Lc / 16)
+    nblk = B * pages
+    rng = np.random.default_rng(seed)
+    cents = tqb.get_centroids(128, 4).numpy()
+    mids = tqb.get_midpoints(tqb.get_centroids(128, 4)).numpy()
+    R = orthogonal(seed + 1).numpy()
+    bt = rng.permutation(nblk).astype(np.int32).reshape(B, pages)
+    kv = np.zeros((nblk, 16, Hk, 134), np.uint8)
+    lay = O.LAYOUT_SOA if layout == "soa" else O.LAYOUT_AOS
+    tok = np.arange(Lc)
+    for b in range(B):
+        slots = (bt[b, tok // 16].astype(np.int64) * 16 + tok % 16).astype(np.int32)
+        key = rng.standard_normal((Lc * Hk, 128), dtype=np.float32)
+        val = rng.standard_normal((Lc * Hk, 128), dtype=np.float32)
+        norms = np.linalg.norm(key, axis=1).astype(np.float32)
+        y = ((key / (norms[:, None] + np.float32(1e-8))) @ R).astype(np.float32)
+        O.store(lay, y, norms, val, mids, cents, slots, kv, norm_correction=(layout == "soa"))
+    q = rng.standard_normal((B, Hq, 128), dtype=np.float32)
+    q_rot = (q @ R).astype(np.float32)
+    return dict(q_rot=q_rot, kv=kv, bt=bt, seq_lens=np.full(B, Lc, np.int32), cents=cents,
+                B=B, Hq=Hq, Hk=Hk, S=S, L=Lc, layout=layout)
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference algorithm on the host CPU cores (the
+    fp32 C restatement of reference/soa_decode_v1.py:43-314 and
+    baseline/stage2.py:8-55).  Rank 0 only; other ranks exit without work."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    cfg = CONFIGS[args.config]
+    w = build_workload_cpu(cfg, args.seed, args.layout)
+    cores = O.default_threads()
+    lay = O.LAYOUT_SOA if args.layout == "soa" else O.LAYOUT_AOS
+
+    def step():
+        mid = O.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], w["S"], layout=lay,
+                       nthreads=cores)
+        O.stage2(mid, w["seq_lens"], nthreads=cores)
+
+    step()  # one warm-up pass (a CPU has no JIT or clock ramp to hide)
+    steps = max(1, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    value = w["B"] / dt
+    line = {
+        "impl": "reference", "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["workload"], "layout": args.layout, "per_gpu_batch": w["B"],
+                   "seq_len": w["L"], "num_splits": w["S"]},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"the full B{w['B']} x {w['L']} workload per step, {steps} step(s) "
+                                   f"(capped at 10), fp32 C restatement of the reference Stage1+Stage2, "
+                                   f"{cores} threads"},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_init()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    import tqb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    w = build_workload(cfg, args.seed + 1000 * rank, dev, args.layout)
+    B, Hq, S = w["B"], w["Hq"], w["S"]
+    mid = torch.empty(B, Hq, S, 129, device=dev)
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+
+    def step():
+        tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, layout=args.layout)
+        tqb.stage2(mid, w["seq_lens"], out, lse)
+
+    clocks = ClockSampler(dev)
+    clocks.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    start.record()
+    for i in range(K):
+        ev[i][0].record()
+        tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, layout=args.layout)
+        ev[i][1].record()
+        tqb.stage2(mid, w["seq_lens"], out, lse)
+    end.record()
+    torch.cuda.synchronize(dev)
+    w1 = time.perf_counter()
+    barrier(world)
+    clocks.mark(w0, w1)
+    clocks.stop()
+    total_ms = max_over_ranks(start.elapsed_time(end), world)
+    s1_ms = [a.elapsed_time(b) for a, b in ev]
+    s1_avg_ms = max_over_ranks(statistics.mean(s1_ms), world)
+    ms_per_step = total_ms / K
+    value = world * B / (ms_per_step * 1e-3)
+
+    # -- end to end through the production entry point, host buffers ------
+    e2e = None
+    if args.e2e_steps > 0:
+        hq = w["query"].cpu().pin_memory()
+        hbt = w["bt"].cpu().pin_memory()
+        hsl = w["seq_lens"].cpu().pin_memory()
+        hout = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+        dq, dbt, dsl = torch.empty_like(w["query"]), torch.empty_like(w["bt"]), torch.empty_like(w["seq_lens"])
+        mbuf = torch.empty(B, Hq, S, 129, device=dev)
+        obuf = torch.empty(B, Hq, 128, device=dev)
+        lbuf = torch.empty(B, Hq, device=dev)
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dbt.copy_(hbt, non_blocking=True)
+            dsl.copy_(hsl, non_blocking=True)
+            o = tqb.triton_turboquant_decode_attention(
+                dq, w["kv"], dbt, dsl, w["R"].T, w["cents"], 1.0 / math.sqrt(128), 4, 66, 4,
+                norm_correction=True, PiT=w["R"], mid_o_buf=mbuf, output_buf=obuf, lse_buf=lbuf,
+                max_num_kv_splits=S)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        b_.record()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e2e_ms = max_over_ranks(a.elapsed_time(b_), world) / args.e2e_steps
+        h2d = hq.numel() * hq.element_size() + hbt.numel() * 4 + hsl.numel() * 4
+        d2h = hout.numel() * hout.element_size()
+        e2e = {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "path": "tqb.triton_turboquant_decode_attention (q rotation GEMM + Stage1 + Stage2 + cast), "
+                       "pinned host query/block_table/seq_lens in, bf16 output out"}
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = measured_peak_hbm()
+    alg = algorithmic_bytes(w)
+    achieved = alg / (s1_avg_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(args.config, args.layout)
+    line = {
+        "metric": "decode_tokens_per_s",
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)",
+        "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
+        "config": {"workload": cfg["workload"], "layout": args.layout,
+                   "per_gpu_batch": B, "global_batch": world * B, "seq_len": w["L"],
+                   "num_splits": S, "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (cache %.0f MB per GPU vs 126 MB L2); no flush"
+                         % (w["kv"].numel() / 1e6)},
+        "stage1_us": s1_avg_ms * 1e3,
+        "stage2_us": (ms_per_step - s1_avg_ms) * 1e3,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s",
+                     "algorithmic_bytes_per_launch": alg, "kernel": "tqb stage1_kernel"},
+        "gpu_launches": 2 * K,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(w)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,173 @@
+/*
+ * tqb.h — C ABI of the B200-native TurboQuant `turboquant_4bit_nc` decode path.
+ *
+ * The library (libtqb.so) holds hand-written sm_100a kernels for the decode
+ * Stage1 (split-KV partial attention over the 4-bit paged cache), the Stage2
+ * log-sum-exp merge, the cross-GPU merge of partial results, and the cache
+ * store.  Every entry point:
+ *   - takes plain device pointers, sizes and byte/element strides (no torch
+ *     types), and the CUDA stream to launch on;
+ *   - launches asynchronously and allocates nothing;
+ *   - returns TQB_OK (0) or a negative tqb_status; tqb_strerror() names it
+ *     and tqb_last_error_detail() says which argument was rejected (per
+ *     calling thread).
+ * Thread safety: stateless apart from a per-device attribute cache; calls on
+ * different streams may run concurrently.
+ *
+ * Reference interfaces replaced (paths inside zben777/turboquant-cuda-decode):
+ *   tqb_stage1   <- launch_soa_v1_stage1 / launch_aos_v1_stage1
+ *                   (baseline/triton_v1.py:90-97,145-152),
+ *                   launch_tq4_v2_stage1 (baseline/triton_v2.py:569-577),
+ *                   tq4_cuda_vN pybind entry (cuda/tq4_cuda_v9_bind.cpp:3-8,
+ *                   cuda/tq4_cuda_v9.cu:276-306), and the Stage1 launch inside
+ *                   triton_turboquant_decode_attention
+ *                   (reference/soa_decode_v1.py:563-608)
+ *   tqb_stage2   <- launch_stage2 (baseline/stage2.py:58-81),
+ *                   tq4_cuda_v7_stage2 (cuda/tq4_cuda_v7.cu:56-76)
+ *   tqb_merge_partials  (no counterpart: the reference is single-GPU; this
+ *                   merges per-GPU (O, LSE) partials with the same algebra as
+ *                   baseline/stage2.py:44-55)
+ *   tqb_store    <- triton_turboquant_store kernel launch
+ *                   (reference/soa_store.py:494-524, reference/aos_store.py:420-447)
+ */
+#ifndef TQB_H_
+#define TQB_H_
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TQB_VERSION 1000 /* 1.0.0 */
+
+typedef enum tqb_status {
+    TQB_OK = 0,
+    TQB_ERR_INVALID_ARG = -1,  /* null pointer, bad size or stride */
+    TQB_ERR_UNSUPPORTED = -2,  /* shape outside the kernels' envelope */
+    TQB_ERR_ALIGNMENT = -3,    /* pointer or stride misaligned */
+    TQB_ERR_LAUNCH = -4,       /* cudaGetLastError after the launch */
+    TQB_ERR_CUDA = -5          /* other CUDA runtime failure */
+} tqb_status;
+
+typedef enum tqb_layout {
+    TQB_LAYOUT_SOA = 0, /* block = [16 tok][Hk][K64|V64] + [Hk][3][16] fp16 meta */
+    TQB_LAYOUT_AOS = 1  /* slot  = [K64 | knorm | V64 | vscale | vzero] */
+} tqb_layout;
+
+/*
+ * Stage1: mid_o[b, h, s, 0:D] = softmax-normalised partial output of split s
+ * of sequence b for query head h; mid_o[b, h, s, D] = natural-log LSE.
+ * Split rule (reference/soa_decode_v1.py:104-110): split_len =
+ * ceil(seq_len / n_s), split s covers [s*split_len, min((s+1)*split_len,
+ * seq_len)); empty splits are left unwritten, exactly like the reference.
+ * n_s = num_splits, or num_splits_per_seq[b] when that array is given
+ * (entries s >= n_s are left unwritten too).
+ */
+typedef struct tqb_stage1_args {
+    const float* q_rot;          /* [B, Hq, D] fp32, unit inner stride */
+    int64_t q_stride_b;          /* elements */
+    int64_t q_stride_h;          /* elements */
+    const uint8_t* kv_cache;     /* [num_blocks, block_size, Hk, slot] uint8 */
+    int32_t layout;              /* tqb_layout */
+    int64_t cache_stride_block;  /* bytes between physical blocks */
+    int64_t cache_stride_pos;    /* bytes between tokens (AoS only) */
+    int64_t cache_stride_head;   /* bytes between KV heads (AoS only) */
+    int64_t num_blocks;          /* physical blocks (0: skip the range check) */
+    const int32_t* block_table;  /* [B, max_blocks_per_seq] */
+    int64_t block_table_stride;  /* elements between rows */
+    int32_t max_blocks_per_seq;
+    const int32_t* seq_lens;     /* [B] */
+    const float* centroids;      /* [n_centroids] fp32 Lloyd-Max codebook */
+    int32_t n_centroids;         /* must be 16 */
+    const float* pair_lut;       /* optional [256, 2]; accepted, not needed */
+    const int32_t* num_splits_per_seq; /* optional [B] */
+    float* mid_o;                /* [B, Hq, S, D+1] fp32, unit inner stride */
+    int64_t mid_stride_b;        /* elements */
+    int64_t mid_stride_h;
+    int64_t mid_stride_s;
+    int32_t batch;               /* B */
+    int32_t num_q_heads;         /* Hq */
+    int32_t num_kv_heads;        /* Hk; Hq % Hk == 0, Hq / Hk <= 8 */
+    int32_t head_dim;            /* D, must be 128 */
+    int32_t block_size;          /* must be 16 */
+    int32_t num_splits;          /* S: split count, and the mid_o split extent */
+    float attn_scale;            /* <= 0 selects 1/sqrt(D) */
+} tqb_stage1_args;
+
+int tqb_stage1(const tqb_stage1_args* args, cudaStream_t stream);
+
+/*
+ * Stage2: merge the non-empty splits of mid_o into output[b, h, 0:D] and
+ * lse[b, h] (baseline/stage2.py:33-58).  A sequence with no non-empty split
+ * (seq_len 0) gets output NaN and lse -inf, as in the reference.
+ */
+typedef struct tqb_stage2_args {
+    const float* mid_o;
+    int64_t mid_stride_b, mid_stride_h, mid_stride_s; /* elements */
+    const int32_t* seq_lens;
+    const int32_t* num_splits_per_seq; /* optional [B] */
+    float* output;                     /* [B, Hq, D] */
+    int64_t out_stride_b, out_stride_h;
+    float* lse;                        /* [B, Hq] */
+    int64_t lse_stride_b;
+    int32_t batch, num_q_heads, head_dim, num_splits;
+} tqb_stage2_args;
+
+int tqb_stage2(const tqb_stage2_args* args, cudaStream_t stream);
+
+/*
+ * Cross-GPU merge: partials[g, b, h, 0:D] / partials[g, b, h, D] are the
+ * (O, LSE) of G disjoint KV ranges (one per GPU, already gathered into this
+ * GPU's memory).  Ranges whose LSE is -inf (no tokens) are skipped.
+ */
+typedef struct tqb_merge_args {
+    const float* partials;       /* [G, B, Hq, D+1] contiguous */
+    int32_t num_parts;           /* G */
+    int32_t batch, num_q_heads, head_dim;
+    float* output;               /* [B, Hq, D] contiguous */
+    float* lse;                  /* [B, Hq] contiguous, may be NULL */
+} tqb_merge_args;
+
+int tqb_merge_partials(const tqb_merge_args* args, cudaStream_t stream);
+
+/*
+ * Store: quantise N tokens x H heads into the paged cache
+ * (reference/soa_store.py:223-373, reference/aos_store.py:221-340).
+ * Inputs are the kernel inputs of the reference launcher: y = rotated unit
+ * keys (x / (|x| + 1e-8)) @ PiT, the key norms |x|, and the raw values, all
+ * fp32 [N*H, D].  Bucketising, packing, norm folding (SoA,
+ * norm_correction=1) and value quantisation are bit-exact with the
+ * reference arithmetic.  Negative slot_mapping entries are skipped.
+ */
+typedef struct tqb_store_args {
+    const float* y;              /* [N*H, D] */
+    const float* norms;          /* [N*H] */
+    const float* value;          /* [N*H, D] */
+    const float* midpoints;      /* [n_centroids - 1] */
+    const float* centroids;      /* [n_centroids] */
+    const int32_t* slot_mapping; /* [N] */
+    uint8_t* kv_cache;
+    int32_t layout;              /* tqb_layout */
+    int64_t cache_stride_block, cache_stride_pos, cache_stride_head; /* bytes */
+    int64_t num_blocks;          /* 0: skip the range check */
+    int32_t num_tokens;          /* N */
+    int32_t num_kv_heads;        /* H */
+    int32_t head_dim;            /* 128 */
+    int32_t block_size;          /* 16 */
+    int32_t n_centroids;         /* 16 */
+    int32_t norm_correction;     /* SoA: fold 1/|c| into the stored norm */
+} tqb_store_args;
+
+int tqb_store(const tqb_store_args* args, cudaStream_t stream);
+
+const char* tqb_strerror(int status);
+const char* tqb_last_error_detail(void);
+int tqb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TQB_H_ */

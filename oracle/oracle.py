@@ -1,0 +1,260 @@
+"""CPU oracle for the TurboQuant ``turboquant_4bit_nc`` decode path.
+
+TEST INFRASTRUCTURE ONLY: this module is the checker the CUDA path is compared
+against, and the timed CPU baseline of ``bench.py``.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs import it; the product
+package never does.
+
+Two independent restatements live here:
+
+* ``store``/``stage1``/``stage2`` call ``libtqoracle.so`` (``tq_oracle.c``), an
+  fp32 restatement in the reference's own operation order.  Its parity is
+  pinned against the reference's Triton kernels run under
+  ``TRITON_INTERPRET=1`` (``tests/golden/*.npz``).
+* ``stage1_np``/``stage2_np`` are vectorised float64 numpy restatements of the
+  same algorithm, used to cross-check the C code and for large configs.
+
+Reference citations are paths inside zben777/turboquant-cuda-decode.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libtqoracle.so"
+
+LAYOUT_SOA = 0
+LAYOUT_AOS = 1
+HEAD_DIM = 128
+BLOCK_SIZE = 16
+SLOT_BYTES = 134  # 64 K + 64 V + 3 fp16 metadata
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile ``libtqoracle.so`` with ``oracle/Makefile``."""
+    if force or not LIB_PATH.exists() or (
+        LIB_PATH.stat().st_mtime < (HERE / "tq_oracle.c").stat().st_mtime
+    ):
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        i64, i32, vp, f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+        _lib.tqo_store.argtypes = [i32, vp, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp,
+                                   i64, i64, i64, i32, i32]
+        _lib.tqo_stage1.argtypes = [i32, vp, i64, i64, vp, i64, i64, i64, vp, i64, vp, vp,
+                                    vp, vp, i64, i64, i64, i32, i32, i32, i32, i32, i32,
+                                    f32, i32]
+        _lib.tqo_stage2.argtypes = [vp, i64, i64, i64, vp, vp, vp, i64, i64, vp, i64,
+                                    i32, i32, i32, i32, i32]
+        for f in (_lib.tqo_store, _lib.tqo_stage1, _lib.tqo_stage2):
+            f.restype = ctypes.c_int
+    return _lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ---------------------------------------------------------------------------
+# Layout helpers (baseline/common.py:79-224; reference/soa_decode_v1.py:168-188)
+# ---------------------------------------------------------------------------
+
+
+def block_bytes(hk: int, block_size: int = BLOCK_SIZE) -> int:
+    """Bytes per physical block: [block_size, Hk, 134] uint8."""
+    return block_size * hk * SLOT_BYTES
+
+
+def soa_meta_offset(hk: int, block_size: int = BLOCK_SIZE, d: int = HEAD_DIM) -> int:
+    """Byte offset of the SoA metadata region inside a block."""
+    return block_size * hk * d
+
+
+def split_range(seq_len: int, num_splits: int, s: int) -> tuple[int, int]:
+    """Reference split rule (reference/soa_decode_v1.py:104-107)."""
+    split_len = -(-seq_len // num_splits)
+    start = split_len * s
+    return start, min(start + split_len, seq_len)
+
+
+# ---------------------------------------------------------------------------
+# C restatement
+# ---------------------------------------------------------------------------
+
+
+def store(layout, y, norms, value, midpoints, centroids, slot_mapping, cache,
+          norm_correction=True, bits=4):
+    """In-place store of N*H token-heads (reference/soa_store.py:223-373,
+    reference/aos_store.py:221-340).  ``y``/``norms``/``value`` are the kernel
+    inputs ``[N*H, D]``, ``[N*H]``, ``[N*H, D]`` fp32; ``cache`` is the
+    ``[num_blocks, 16, H, 134]`` uint8 array, modified in place."""
+    assert cache.dtype == np.uint8 and cache.flags.c_contiguous
+    N = slot_mapping.shape[0]
+    H = cache.shape[2]
+    D = y.shape[-1]
+    y, norms, value = _c(y, np.float32), _c(norms, np.float32), _c(value, np.float32)
+    mids, cents = _c(midpoints, np.float32), _c(centroids, np.float32)
+    slots = _c(slot_mapping, np.int32)
+    st = [s * cache.itemsize for s in cache.strides]
+    rc = lib().tqo_store(layout, _ptr(y), _ptr(norms), _ptr(value), N, H, D, _ptr(mids),
+                         _ptr(cents), bits, _ptr(slots), _ptr(cache), st[0], st[1], st[2],
+                         cache.shape[1], int(norm_correction))
+    assert rc == 0
+
+
+def stage1(q_rot, cache, block_table, seq_lens, centroids, num_splits, *,
+           layout=LAYOUT_SOA, num_splits_per_seq=None, mid_o=None, attn_scale=None,
+           nthreads=0):
+    """fp32 Stage1 in the reference's order.  Returns ``mid_o [B,Hq,S,D+1]``;
+    entries of empty splits keep their initial value (NaN when allocated
+    here), as the reference leaves them unwritten."""
+    q = _c(q_rot, np.float32)
+    B, Hq, D = q.shape
+    cache = np.ascontiguousarray(cache)
+    Hk = cache.shape[2]
+    bt = _c(block_table, np.int32)
+    sl = _c(seq_lens, np.int32)
+    cents = _c(centroids, np.float32)
+    nsp = None if num_splits_per_seq is None else _c(num_splits_per_seq, np.int32)
+    if mid_o is None:
+        mid_o = np.full((B, Hq, num_splits, D + 1), np.nan, dtype=np.float32)
+    assert mid_o.dtype == np.float32 and mid_o.flags.c_contiguous
+    scale = np.float32(1.0 / np.sqrt(D)) if attn_scale is None else np.float32(attn_scale)
+    rc = lib().tqo_stage1(layout, _ptr(q), q.strides[0] // 4, q.strides[1] // 4, _ptr(cache),
+                          cache.strides[0], cache.strides[1], cache.strides[2], _ptr(bt),
+                          bt.strides[0] // 4, _ptr(sl), _ptr(nsp), _ptr(cents), _ptr(mid_o),
+                          mid_o.strides[0] // 4, mid_o.strides[1] // 4, mid_o.strides[2] // 4,
+                          B, Hq, Hk, D, cache.shape[1], num_splits, float(scale), nthreads)
+    assert rc == 0
+    return mid_o
+
+
+def stage2(mid_o, seq_lens, num_splits_per_seq=None, nthreads=0):
+    """LSE merge over non-empty splits (baseline/stage2.py:8-55).
+    Returns ``(output [B,Hq,D], lse [B,Hq])``."""
+    mid = _c(mid_o, np.float32)
+    B, Hq, S, D1 = mid.shape
+    D = D1 - 1
+    sl = _c(seq_lens, np.int32)
+    nsp = None if num_splits_per_seq is None else _c(num_splits_per_seq, np.int32)
+    out = np.empty((B, Hq, D), np.float32)
+    lse = np.empty((B, Hq), np.float32)
+    rc = lib().tqo_stage2(_ptr(mid), mid.strides[0] // 4, mid.strides[1] // 4,
+                          mid.strides[2] // 4, _ptr(sl), _ptr(nsp), _ptr(out),
+                          out.strides[0] // 4, out.strides[1] // 4, _ptr(lse),
+                          lse.strides[0] // 4, B, Hq, S, D, nthreads)
+    assert rc == 0
+    return out, lse
+
+
+# ---------------------------------------------------------------------------
+# Independent float64 numpy restatement
+# ---------------------------------------------------------------------------
+
+
+def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
+    """Dequantise tokens (block_ids[i], offs[i]) of KV head ``kvh``.
+    Returns ``K [n, D]`` (centroid*norm, norm correction applied for AoS) and
+    ``V [n, D]`` in float64."""
+    nb, bs, Hk, slot = cache.shape
+    D = HEAD_DIM
+    flat = cache.reshape(nb, bs * Hk * slot)
+    c = np.asarray(centroids, np.float64)
+    if layout == LAYOUT_SOA:
+        dps = D  # 64 K + 64 V bytes
+        base = offs * Hk * dps + kvh * dps
+        kb = flat[block_ids[:, None], base[:, None] + np.arange(D // 2)]
+        vb = flat[block_ids[:, None], base[:, None] + D // 2 + np.arange(D // 2)]
+        meta = flat[:, soa_meta_offset(Hk, bs, D):].view(np.float16).reshape(nb, Hk, 3, bs)
+        knorm = meta[block_ids, kvh, 0, offs].astype(np.float64)
+        vsc = meta[block_ids, kvh, 1, offs].astype(np.float64)
+        vz = meta[block_ids, kvh, 2, offs].astype(np.float64)
+    else:
+        slots = cache[block_ids, offs, kvh]  # [n, 134]
+        kb = slots[:, : D // 2]
+        knorm = slots[:, D // 2 : D // 2 + 2].copy().view(np.float16)[:, 0].astype(np.float64)
+        vb = slots[:, D // 2 + 2 : D + 2]
+        vsc = slots[:, D + 2 : D + 4].copy().view(np.float16)[:, 0].astype(np.float64)
+        vz = slots[:, D + 4 : D + 6].copy().view(np.float16)[:, 0].astype(np.float64)
+    kidx = np.stack([kb & 0xF, kb >> 4], -1).reshape(-1, D)
+    vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
+    kc = c[kidx]
+    if layout == LAYOUT_AOS:
+        kc = kc / np.sqrt((kc * kc).sum(-1, keepdims=True) + 1e-16)
+    K = kc * knorm[:, None]
+    V = vidx * vsc[:, None] + vz[:, None]
+    return K, V
+
+
+def stage1_np(q_rot, cache, block_table, seq_lens, centroids, num_splits, *,
+              layout=LAYOUT_SOA, num_splits_per_seq=None, attn_scale=None):
+    """float64 restatement of Stage1 (two-pass softmax per split)."""
+    q = np.asarray(q_rot, np.float64)
+    B, Hq, D = q.shape
+    Hk = cache.shape[2]
+    G = Hq // Hk
+    bs = cache.shape[1]
+    scale = 1.0 / np.sqrt(D) if attn_scale is None else attn_scale
+    mid = np.full((B, Hq, num_splits, D + 1), np.nan, np.float64)
+    for b in range(B):
+        nsp = num_splits if num_splits_per_seq is None else int(num_splits_per_seq[b])
+        L = int(seq_lens[b])
+        for kvh in range(Hk):
+            for s in range(nsp):
+                t0, t1 = split_range(L, nsp, s)
+                if t0 >= t1:
+                    continue
+                toks = np.arange(t0, t1)
+                blk = np.asarray(block_table[b])[toks // bs].astype(np.int64)
+                K, V = decode_kv_np(cache, blk, toks % bs, kvh, centroids, layout)
+                qs = q[b, kvh * G : (kvh + 1) * G]  # [G, D]
+                sc = qs @ K.T * scale  # [G, n]
+                m = sc.max(-1, keepdims=True)
+                p = np.exp(sc - m)
+                l = p.sum(-1, keepdims=True)
+                mid[b, kvh * G : (kvh + 1) * G, s, :D] = (p @ V) / l
+                mid[b, kvh * G : (kvh + 1) * G, s, D] = (m + np.log(l))[:, 0]
+    return mid
+
+
+def stage2_np(mid_o, seq_lens, num_splits_per_seq=None):
+    mid = np.asarray(mid_o, np.float64)
+    B, Hq, S, D1 = mid.shape
+    out = np.empty((B, Hq, D1 - 1))
+    lse = np.empty((B, Hq))
+    for b in range(B):
+        nsp = S if num_splits_per_seq is None else int(num_splits_per_seq[b])
+        keep = [s for s in range(nsp) if split_range(int(seq_lens[b]), nsp, s)[0]
+                < split_range(int(seq_lens[b]), nsp, s)[1]]
+        if not keep:
+            out[b] = np.nan
+            lse[b] = -np.inf
+            continue
+        ls = mid[b][:, keep, D1 - 1]  # [Hq, k]
+        m = ls.max(-1, keepdims=True)
+        w = np.exp(ls - m)
+        out[b] = (w[..., None] * mid[b][:, keep, : D1 - 1]).sum(1) / w.sum(-1, keepdims=True)
+        lse[b] = (m + np.log(w.sum(-1, keepdims=True)))[:, 0]
+    return out, lse
+
+
+def default_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

@@ -1,0 +1,68 @@
+"""Shared fixtures.  GPU tests carry ``@pytest.mark.gpu``; everything else runs
+on a CPU-only host."""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / "turboquant-cuda-decode_b200"
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+for p in (str(ROOT), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+GOLDEN_CASES = ["c0", "ragged_gqa4", "ragged_gqa8_hk1", "ragged_gqa8_hk2"]
+
+# Parity bar of the decode path: |got - ref| <= ATOL + RTOL * |ref|
+# (1e-4 absolute, 2e-3 relative) on Stage1 O and LSE and on Stage2.
+ATOL = 1e-4
+RTOL = 2e-3
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+    config.addinivalue_line("markers", "multigpu: needs two or more CUDA GPUs")
+
+
+def load_golden(name: str) -> dict:
+    with np.load(GOLDEN / f"{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def golden():
+    return {name: load_golden(name) for name in GOLDEN_CASES}
+
+
+@pytest.fixture(scope="session")
+def golden_store():
+    return load_golden("store_small")
+
+
+def assert_close(got, ref, atol=ATOL, rtol=RTOL, what=""):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (what, got.shape, ref.shape)
+    both_nan = np.isnan(got) & np.isnan(ref)
+    err = np.abs(got - ref)
+    bad = ~both_nan & ~(err <= atol + rtol * np.abs(ref))
+    if bad.any():
+        i = np.argwhere(bad)[0]
+        raise AssertionError(
+            f"{what}: {int(bad.sum())}/{bad.size} elements outside {atol}+{rtol}*|ref|; "
+            f"max err {np.nanmax(err):.3e}; first bad {tuple(i)} got {got[tuple(i)]} ref {ref[tuple(i)]}")
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")

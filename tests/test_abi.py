@@ -1,0 +1,117 @@
+"""The C ABI library (CPU only: no kernel is launched here).
+
+Checks that libtqb.so is built for sm_100a, loads, exports every function
+declared in include/tqb.h, and that the ctypes argument structs have the
+exact layout of the C structs (compiled with gcc against the header).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+import tempfile
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT
+from tqb import _build, _lib
+
+HEADER = ROOT / "include" / "tqb.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    _build.build()
+    return _lib.load()
+
+
+def header_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(tqb_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert header_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_header_symbol(lib):
+    for name in header_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (tqb_\w+)", out))
+    assert set(header_functions()) <= exported
+
+
+def test_library_holds_sm100a_code():
+    out = subprocess.run(["cuobjdump", "--list-elf", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    assert "sm_100a" in out.stdout
+
+
+def test_host_only_entry_points(lib):
+    assert lib.tqb_version() == 1000
+    assert _lib.version() == 1000
+    assert lib.tqb_strerror(0) == b"ok"
+    assert lib.tqb_strerror(_lib.TQB_ERR_UNSUPPORTED) == b"unsupported shape or configuration"
+    assert lib.tqb_strerror(-99) == b"unknown tqb status"
+
+
+def test_argument_validation_without_launch(lib):
+    """Rejections happen on the host before any device call."""
+    a = _lib.Stage1Args()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.num_splits = 1, 32, 8, 4
+    a.head_dim, a.block_size, a.n_centroids = 64, 16, 16
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.tqb_last_error_detail()
+    a.head_dim = 128
+    a.num_q_heads = 30  # not a multiple of Hk
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    a.num_q_heads, a.num_kv_heads = 64, 4  # GQA 16
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_UNSUPPORTED
+    a.num_kv_heads = 8
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG  # NULL pointers
+    assert lib.tqb_stage1(None, None) == _lib.TQB_ERR_INVALID_ARG
+    s = _lib.StoreArgs()
+    s.num_tokens, s.num_kv_heads, s.head_dim, s.block_size, s.n_centroids = 1, 8, 128, 16, 8
+    assert lib.tqb_store(ctypes.byref(s), None) == _lib.TQB_ERR_UNSUPPORTED
+    # Empty batches are valid no-ops.
+    a = _lib.Stage1Args()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.num_splits = 0, 32, 8, 32
+    a.head_dim, a.block_size, a.n_centroids = 128, 16, 16
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_OK
+
+
+C_LAYOUT_PROBE = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "tqb.h"
+#define F(T, f) printf("%s.%s %zu\n", #T, #f, offsetof(T, f));
+int main(void) {
+  printf("tqb_stage1_args %zu\n", sizeof(tqb_stage1_args));
+  printf("tqb_stage2_args %zu\n", sizeof(tqb_stage2_args));
+  printf("tqb_merge_args %zu\n", sizeof(tqb_merge_args));
+  printf("tqb_store_args %zu\n", sizeof(tqb_store_args));
+  %FIELDS%
+  return 0;
+}
+"""
+
+
+def test_ctypes_structs_match_c_layout(tmp_path: Path):
+    structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
+               "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs}
+    fields = "\n".join(f"F({c}, {f})" for c, py in structs.items() for f, _ in py._fields_)
+    src = tmp_path / "probe.c"
+    src.write_text(C_LAYOUT_PROBE.replace("%FIELDS%", fields))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
+                    str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run(
+        [str(exe)], capture_output=True, text=True, check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"

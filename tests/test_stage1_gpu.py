@@ -1,0 +1,181 @@
+"""Stage1 parity of the sm_100a kernel (GPU).
+
+Bar: |got - ref| <= 1e-4 + 2e-3 |ref| on every written O and LSE element
+(conftest.ATOL/RTOL), against (a) the reference's own SoA/AoS V1 outputs
+stored in the golden fixtures and (b) the CPU oracle on fresh seeded inputs.
+Empty splits must stay unwritten, exactly as in the reference.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, assert_close
+from oracle import oracle as O
+import tqb
+from tqb import layout as L
+
+pytestmark = pytest.mark.gpu
+
+SENTINEL = -12345.0
+
+
+def _to(dev, z, key, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(z[key]))
+    return t.to(dev) if dtype is None else t.to(dev, dtype)
+
+
+def _run(dev, z, cache_key="kv_cache", layout="soa", nsp=None, S=None):
+    S = int(z["num_splits"]) if S is None else S
+    q = _to(dev, z, "q_rot")
+    mid = torch.full((q.shape[0], q.shape[1], S, q.shape[2] + 1), SENTINEL, device=dev)
+    tqb.stage1(q, _to(dev, z, cache_key), _to(dev, z, "block_table"), _to(dev, z, "seq_lens"),
+               _to(dev, z, "centroids"), mid, layout=layout,
+               num_splits_per_seq=None if nsp is None else torch.tensor(nsp, dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    return mid.cpu().numpy()
+
+
+def _check(got, ref, what):
+    written = ~np.isnan(ref[..., 0])
+    # unwritten in the reference -> untouched here
+    assert np.all(got[~written] == SENTINEL), f"{what}: wrote into an empty split"
+    assert_close(got[written], ref[written], what=what)
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_soa_vs_reference_golden(cuda_device, golden, name):
+    z = golden[name]
+    _check(_run(cuda_device, z), z["mid_o_soa_v1"], f"{name} SoA")
+
+
+@pytest.mark.parametrize("name", [n for n in GOLDEN_CASES if n != "ragged_gqa8_hk2"])
+def test_aos_vs_reference_golden(cuda_device, golden, name):
+    z = golden[name]
+    _check(_run(cuda_device, z, "kv_cache_aos", "aos"), z["mid_o_aos_v1"], f"{name} AoS")
+
+
+def test_compat_launchers(cuda_device, golden):
+    z = golden["c0"]
+    dev = cuda_device
+    q, kv, bt, sl, c = (_to(dev, z, k) for k in ("q_rot", "kv_cache", "block_table", "seq_lens", "centroids"))
+    mid = torch.full((2, 32, 4, 129), SENTINEL, device=dev)
+    tqb.launch_soa_v1_stage1(q, kv, bt, sl, c, mid)
+    lut = tqb.build_pair_lut(c)
+    mid2 = tqb.launch_tq4_v2_stage1(q, kv, bt, sl, c, lut, num_splits=4)
+    out = torch.empty(2, 32, 128, device=dev)
+    lse = torch.empty(2, 32, device=dev)
+    tqb.launch_stage2(mid, sl, out, lse)
+    torch.cuda.synchronize()
+    _check(mid.cpu().numpy(), z["mid_o_soa_v1"], "launch_soa_v1_stage1")
+    assert_close(mid2.cpu().numpy(), z["mid_o_soa_v1"], what="launch_tq4_v2_stage1")
+    assert_close(out.cpu().numpy(), z["out_stage2"], what="launch_stage2 out")
+    assert_close(lse.cpu().numpy(), z["lse_stage2"], what="launch_stage2 lse")
+
+
+def _random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0, dev="cuda"):
+    """Seeded cache written by the CPU oracle store (reference semantics),
+    shuffled block pool, random garbage in unused slots."""
+    rng = np.random.default_rng(seed)
+    pages = [max(1, math.ceil(n / 16)) for n in seq_lens]
+    nblk = sum(pages) + pool_extra
+    slot = L.SLOT_SIZE
+    cache = rng.integers(0, 256, size=(nblk, 16, Hk, slot), dtype=np.uint8)
+    perm = rng.permutation(nblk)
+    bt = np.zeros((B, max(pages)), np.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]]
+        k += pages[b]
+    cents = tqb.get_centroids(128, 4).numpy()
+    mids = tqb.get_midpoints(tqb.get_centroids(128, 4)).numpy()
+    ntok = int(sum(seq_lens))
+    slots = np.concatenate([bt[b, np.arange(n) // 16] * 16 + np.arange(n) % 16 for b, n in enumerate(seq_lens)]).astype(np.int32)
+    key = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
+    norms = np.linalg.norm(key, axis=1).astype(np.float32)
+    R = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    y = ((key / (norms[:, None] + 1e-8)) @ R).astype(np.float32)
+    val = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
+    O.store(O.LAYOUT_SOA, y, norms, val, mids, cents, slots, cache, norm_correction=True)
+    q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
+    return dict(q_rot=q, kv_cache=cache, block_table=bt, seq_lens=np.asarray(seq_lens, np.int32),
+                centroids=cents)
+
+
+@pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8), (8, 1), (16, 2), (24, 8), (6, 2), (4, 4)])
+def test_gqa_shapes_vs_oracle(cuda_device, hq, hk):
+    z = _random_case(hq * 100 + hk, 3, hq, hk, [300, 17, 1024])
+    S = 5
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S)
+    _check(_run(cuda_device, z, S=S), ref, f"GQA {hq}/{hk}")
+
+
+def test_ragged_per_sequence_splits(cuda_device):
+    lens = [512, 1, 16, 17, 4000, 777, 33, 1500]
+    z = _random_case(5, len(lens), 32, 8, lens)
+    nsp = L.splits_per_sequence(lens, 512, 32)
+    nsp[3] = 4  # 17 tokens in 4 splits of 5: the last split holds 2 tokens
+    S = 32
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                   num_splits_per_seq=np.asarray(nsp, np.int32))
+    _check(_run(cuda_device, z, nsp=nsp, S=S), ref, "per-seq splits")
+
+
+def test_long_split_reloads_block_ids(cuda_device):
+    """A split spanning > 32 pages exercises the block-id window refill."""
+    lens = [16 * 70 + 5, 16 * 33]
+    z = _random_case(9, 2, 32, 8, lens)
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], 1)
+    _check(_run(cuda_device, z, S=1), ref, "long split")
+
+
+def test_strided_views(cuda_device):
+    """Non-contiguous q/mid_o views and a block stride larger than the block
+    (a cache carved out of a bigger allocation)."""
+    z = _random_case(3, 2, 32, 8, [200, 70])
+    dev = cuda_device
+    nb = z["kv_cache"].shape[0]
+    big = torch.zeros(nb, 17152 + 256, dtype=torch.uint8, device=dev)
+    big[:, :17152] = torch.from_numpy(z["kv_cache"].reshape(nb, -1)).to(dev)
+    kv = torch.as_strided(big, (nb, 16, 8, 134), (17152 + 256, 8 * 134, 134, 1))
+    qbig = torch.zeros(2, 40, 128, device=dev)
+    qbig[:, :32] = torch.from_numpy(z["q_rot"]).to(dev)
+    q = qbig[:, :32]
+    midbig = torch.full((2, 32, 6, 140), SENTINEL, device=dev)
+    mid = midbig[:, :, :4, :129]
+    tqb.stage1(q, kv, torch.from_numpy(z["block_table"]).to(dev), torch.from_numpy(z["seq_lens"]).to(dev),
+               torch.from_numpy(z["centroids"]).to(dev), mid)
+    torch.cuda.synchronize()
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], 4)
+    _check(mid.cpu().numpy(), ref, "strided")
+    assert torch.all(midbig[:, :, 4:] == SENTINEL) and torch.all(midbig[..., 129:] == SENTINEL)
+
+
+def test_large_magnitudes(cuda_device):
+    """Query magnitudes far from 1 (power-of-two scaling keeps the fp16
+    operand split exact) and large V scales."""
+    z = _random_case(21, 2, 32, 8, [256, 100])
+    S = 4
+    for scale in (1e-3, 30.0):
+        z2 = dict(z, q_rot=(z["q_rot"] * scale).astype(np.float32))
+        ref = O.stage1(z2["q_rot"], z2["kv_cache"], z2["block_table"], z2["seq_lens"], z2["centroids"], S)
+        _check(_run(cuda_device, z2, S=S), ref, f"q scale {scale}")
+
+
+def test_errors_raise(cuda_device, golden):
+    z = golden["c0"]
+    dev = cuda_device
+    q = _to(dev, z, "q_rot")
+    kv = _to(dev, z, "kv_cache")
+    bt, sl, c = _to(dev, z, "block_table"), _to(dev, z, "seq_lens"), _to(dev, z, "centroids")
+    mid = torch.empty(2, 32, 4, 129, device=dev)
+    with pytest.raises(tqb.TqbError):
+        tqb.stage1(q.double(), kv, bt, sl, c, mid)
+    with pytest.raises(tqb.TqbError):
+        tqb.stage1(q, kv, bt, sl, c, torch.empty(2, 32, 4, 128, device=dev))
+    with pytest.raises(tqb.TqbError):
+        tqb.stage1(q[:, :30], kv, bt, sl, c, torch.empty(2, 30, 4, 129, device=dev))

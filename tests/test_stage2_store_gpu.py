@@ -1,0 +1,106 @@
+"""Stage2 merge, cross-GPU partial merge and the store kernel (GPU)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, assert_close
+from oracle import oracle as O
+import tqb
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_stage2_vs_reference_golden(cuda_device, golden, name):
+    z = golden[name]
+    dev = cuda_device
+    mid = torch.from_numpy(z["mid_o_soa_v1"]).to(dev)  # NaN in empty splits: must be skipped
+    sl = torch.from_numpy(z["seq_lens"]).to(dev)
+    B, Hq, S, D1 = mid.shape
+    out = torch.empty(B, Hq, D1 - 1, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, sl, out, lse)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), z["out_stage2"], what="stage2 out")
+    assert_close(lse.cpu().numpy(), z["lse_stage2"], what="stage2 lse")
+
+
+def test_stage2_empty_sequence_and_per_seq_splits(cuda_device):
+    rng = np.random.default_rng(0)
+    B, Hq, S = 4, 8, 6
+    lens = np.array([0, 5, 100, 64], np.int32)
+    nsp = np.array([3, 6, 4, 6], np.int32)
+    mid = rng.standard_normal((B, Hq, S, 129)).astype(np.float32)
+    dev = cuda_device
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.stage2(torch.from_numpy(mid).to(dev), torch.from_numpy(lens).to(dev), out, lse,
+               num_splits_per_seq=torch.from_numpy(nsp).to(dev))
+    torch.cuda.synchronize()
+    ro, rl = O.stage2(mid, lens, nsp)
+    assert_close(out.cpu().numpy(), ro, what="out")
+    assert_close(lse.cpu().numpy(), rl, what="lse")
+    assert np.isnan(out.cpu().numpy()[0]).all() and np.isneginf(lse.cpu().numpy()[0]).all()
+
+
+def test_merge_partials_equals_single_pass(cuda_device):
+    """Merging per-range (O, LSE) partials equals merging all splits at once
+    (the identity behind the sequence-parallel path)."""
+    rng = np.random.default_rng(1)
+    G, B, Hq = 4, 3, 16
+    parts = rng.standard_normal((G, B, Hq, 129)).astype(np.float32)
+    parts[2, 1, :, 128] = -np.inf  # an empty range
+    parts[2, 1, :, :128] = np.nan
+    dev = cuda_device
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.merge_partials(torch.from_numpy(parts).to(dev), out, lse)
+    torch.cuda.synchronize()
+    lse_p = parts[..., 128]
+    m = np.max(np.where(np.isneginf(lse_p), -np.inf, lse_p), axis=0)
+    w = np.where(np.isneginf(lse_p), 0.0, np.exp(lse_p - m))
+    ref = np.nansum(w[..., None] * np.nan_to_num(parts[..., :128]), axis=0) / w.sum(0)[..., None]
+    assert_close(out.cpu().numpy(), ref, what="merge out")
+    assert_close(lse.cpu().numpy(), m + np.log(w.sum(0)), what="merge lse")
+
+
+@pytest.mark.parametrize("layout,key", [("soa", "kv_cache_soa"), ("aos", "kv_cache_aos")])
+def test_store_bit_exact_vs_reference(cuda_device, golden_store, layout, key):
+    z = golden_store
+    dev = cuda_device
+    cache = torch.from_numpy(z["cache_before"].copy()).to(dev)
+    tqb.store(torch.from_numpy(z["y"]).to(dev), torch.from_numpy(z["norms"]).to(dev),
+              torch.from_numpy(z["value"].reshape(-1, 128).copy()).to(dev), cache,
+              torch.from_numpy(z["slot_mapping"]).to(dev), torch.from_numpy(z["midpoints"]).to(dev),
+              torch.from_numpy(z["centroids"]).to(dev), layout=layout, norm_correction=(layout == "soa"))
+    torch.cuda.synchronize()
+    got = cache.cpu().numpy()
+    assert np.array_equal(got, z[key]), f"{(got != z[key]).sum()} bytes differ"
+
+
+def test_store_bit_exact_vs_oracle_large(cuda_device):
+    """Thousands of random token-heads, including near-midpoint values."""
+    rng = np.random.default_rng(7)
+    N, H, nb = 2000, 8, 160
+    cents = tqb.get_centroids(128, 4)
+    mids = tqb.get_midpoints(cents).numpy()
+    y = rng.standard_normal((N * H, 128)).astype(np.float32) * np.float32(0.09)
+    pick = rng.random(y.shape) < 0.05  # land exactly on a midpoint: `>=` goes right
+    y[pick] = mids[rng.integers(0, 15, pick.sum())]
+    norms = np.abs(rng.standard_normal(N * H)).astype(np.float32) * 11
+    val = rng.standard_normal((N * H, 128)).astype(np.float32) * rng.uniform(0.01, 50, (N * H, 1)).astype(np.float32)
+    slots = rng.permutation(nb * 16)[:N].astype(np.int32)
+    slots[::97] = -1
+    base = rng.integers(0, 256, (nb, 16, H, 134), dtype=np.uint8)
+    ref = base.copy()
+    O.store(O.LAYOUT_SOA, y, norms, val, mids, cents.numpy(), slots, ref, norm_correction=True)
+    dev = cuda_device
+    cache = torch.from_numpy(base).to(dev)
+    tqb.store(*(torch.from_numpy(a).to(dev) for a in (y, norms, val)), cache,
+              torch.from_numpy(slots).to(dev), torch.from_numpy(mids).to(dev), cents.to(dev))
+    torch.cuda.synchronize()
+    got = cache.cpu().numpy()
+    assert np.array_equal(got, ref), f"{(got != ref).sum()} bytes differ"

@@ -1,0 +1,276 @@
+// tqb_api.cu — the C ABI (include/tqb.h): argument validation, error
+// reporting and dispatch to the kernels.  No allocation happens here or in
+// any kernel; every buffer is owned by the caller.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "tqb_common.cuh"
+#include "tqb_internal.h"
+
+namespace {
+
+thread_local char g_detail[256] = "";
+
+int fail(int code, const char* fmt, const char* what) {
+    snprintf(g_detail, sizeof(g_detail), fmt, what);
+    return code;
+}
+
+#define TQB_REQUIRE(cond, code, msg)                   \
+    do {                                               \
+        if (!(cond)) return fail((code), "%s", (msg)); \
+    } while (0)
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {0};
+
+// Makes the device that owns `ptr` current for the duration of a call (the
+// library may run beside another CUDA runtime instance, e.g. torch's, whose
+// notion of the current device it must not depend on).
+struct DeviceGuard {
+    int prev = -1, dev = -1;
+    bool ok = true;
+    explicit DeviceGuard(const void* ptr) {
+        cudaPointerAttributes attr{};
+        if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+            cudaGetLastError();  // clear the sticky-free error of a failed query
+            ok = (cudaGetDevice(&dev) == cudaSuccess);
+            return;
+        }
+        dev = attr.device;
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+};
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return -1;
+    if (dev < kMaxDevices && g_sm_count[dev] > 0) return g_sm_count[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return -1;
+    if (dev < kMaxDevices) g_sm_count[dev] = n;
+    return n;
+}
+
+}  // namespace
+
+namespace tqb {
+int report_launch(cudaError_t e) {
+    if (e == cudaSuccess) return TQB_OK;
+    snprintf(g_detail, sizeof(g_detail), "kernel launch: %s", cudaGetErrorString(e));
+    return TQB_ERR_LAUNCH;
+}
+}  // namespace tqb
+
+extern "C" {
+
+int tqb_version(void) { return TQB_VERSION; }
+
+const char* tqb_strerror(int status) {
+    switch (status) {
+        case TQB_OK: return "ok";
+        case TQB_ERR_INVALID_ARG: return "invalid argument";
+        case TQB_ERR_UNSUPPORTED: return "unsupported shape or configuration";
+        case TQB_ERR_ALIGNMENT: return "misaligned pointer or stride";
+        case TQB_ERR_LAUNCH: return "kernel launch failed";
+        case TQB_ERR_CUDA: return "CUDA runtime error";
+        default: return "unknown tqb status";
+    }
+}
+
+const char* tqb_last_error_detail(void) { return g_detail; }
+
+int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 && a->num_splits > 0,
+                TQB_ERR_INVALID_ARG, "batch/heads/num_splits must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
+    TQB_REQUIRE(a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED,
+                "n_centroids must be 16 (4-bit keys)");
+    TQB_REQUIRE(a->num_q_heads % a->num_kv_heads == 0, TQB_ERR_INVALID_ARG,
+                "num_q_heads must be a multiple of num_kv_heads");
+    const int G = a->num_q_heads / a->num_kv_heads;
+    TQB_REQUIRE(G <= 8, TQB_ERR_UNSUPPORTED, "GQA group size must be <= 8");
+    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS, TQB_ERR_INVALID_ARG,
+                "layout must be TQB_LAYOUT_SOA or TQB_LAYOUT_AOS");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens && a->centroids && a->mid_o,
+                TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->q_rot, 16) && a->q_stride_b % 4 == 0 && a->q_stride_h % 4 == 0,
+                TQB_ERR_ALIGNMENT, "q_rot must be 16-byte aligned with strides multiple of 4");
+    TQB_REQUIRE(aligned(a->mid_o, 4), TQB_ERR_ALIGNMENT, "mid_o must be 4-byte aligned");
+    TQB_REQUIRE(a->mid_stride_s >= tqb::kHeadDim + 1 && a->mid_stride_h >= 0 && a->mid_stride_b >= 0,
+                TQB_ERR_INVALID_ARG, "mid_o split stride must be >= head_dim + 1");
+    TQB_REQUIRE(a->max_blocks_per_seq > 0 && a->block_table_stride >= a->max_blocks_per_seq,
+                TQB_ERR_INVALID_ARG, "block_table row stride must be >= max_blocks_per_seq");
+    const int64_t hk = a->num_kv_heads;
+    if (a->layout == TQB_LAYOUT_SOA) {
+        TQB_REQUIRE(aligned(a->kv_cache, 16), TQB_ERR_ALIGNMENT, "SoA kv_cache must be 16-byte aligned");
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes &&
+                        a->cache_stride_block % 16 == 0,
+                    TQB_ERR_ALIGNMENT, "SoA block stride must be >= 16*Hk*134 bytes and a multiple of 16");
+    } else {
+        TQB_REQUIRE(aligned(a->kv_cache, 2) && a->cache_stride_block % 2 == 0 &&
+                        a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0,
+                    TQB_ERR_ALIGNMENT, "AoS cache pointer and strides must be even");
+        TQB_REQUIRE(a->cache_stride_head >= tqb::kSlotBytes &&
+                        a->cache_stride_pos >= hk * a->cache_stride_head &&
+                        a->cache_stride_block >= tqb::kBlockSize * a->cache_stride_pos,
+                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134]");
+    }
+    DeviceGuard guard(a->mid_o);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
+    const int nsm = sm_count();
+    TQB_REQUIRE(nsm > 0, TQB_ERR_CUDA, "cannot query the current CUDA device");
+
+    tqb::Stage1Params p{};
+    p.q = a->q_rot;
+    p.qsb = a->q_stride_b;
+    p.qsh = a->q_stride_h;
+    p.cache = a->kv_cache;
+    p.block_bytes = a->cache_stride_block;
+    p.pos_stride = a->cache_stride_pos;
+    p.head_stride = a->cache_stride_head;
+    p.layout = a->layout;
+    p.bt = a->block_table;
+    p.bt_stride = a->block_table_stride;
+    p.max_blocks = a->max_blocks_per_seq;
+    p.num_blocks = a->num_blocks;
+    p.seq_lens = a->seq_lens;
+    p.nsplits = a->num_splits_per_seq;
+    p.cents = a->centroids;
+    p.mid = a->mid_o;
+    p.msb = a->mid_stride_b;
+    p.msh = a->mid_stride_h;
+    p.mss = a->mid_stride_s;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    p.Hk = a->num_kv_heads;
+    p.G = G;
+    p.S = a->num_splits;
+    p.attn_scale = a->attn_scale > 0.0f ? a->attn_scale : 1.0f / sqrtf((float)tqb::kHeadDim);
+    p.num_items = (int64_t)a->batch * a->num_splits * a->num_kv_heads;
+    const int rc = tqb::launch_stage1(p, stream, nsm);
+    if (rc != TQB_OK) return rc;
+    return TQB_OK;
+}
+
+int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0 && a->num_splits > 0, TQB_ERR_INVALID_ARG,
+                "batch/heads/num_splits must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->mid_o && a->seq_lens && a->output && a->lse, TQB_ERR_INVALID_ARG,
+                "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->mid_o, 4) && aligned(a->output, 4) && aligned(a->lse, 4),
+                TQB_ERR_ALIGNMENT, "buffers must be 4-byte aligned");
+    DeviceGuard guard(a->output);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning output");
+    tqb::Stage2Params p{};
+    p.mid = a->mid_o;
+    p.msb = a->mid_stride_b;
+    p.msh = a->mid_stride_h;
+    p.mss = a->mid_stride_s;
+    p.seq_lens = a->seq_lens;
+    p.nsplits = a->num_splits_per_seq;
+    p.out = a->output;
+    p.osb = a->out_stride_b;
+    p.osh = a->out_stride_h;
+    p.lse = a->lse;
+    p.lsb = a->lse_stride_b;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    p.S = a->num_splits;
+    const int rc = tqb::launch_stage2(p, stream);
+    if (rc != TQB_OK) return rc;
+    return TQB_OK;
+}
+
+int tqb_merge_partials(const tqb_merge_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->num_parts > 0 && a->batch >= 0 && a->num_q_heads > 0, TQB_ERR_INVALID_ARG,
+                "num_parts/batch/heads must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->partials && a->output, TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->partials, 4) && aligned(a->output, 4) && aligned(a->lse, 4),
+                TQB_ERR_ALIGNMENT, "buffers must be 4-byte aligned");
+    DeviceGuard guard(a->output);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning output");
+    tqb::MergeParams p{};
+    p.partials = a->partials;
+    p.G = a->num_parts;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    p.out = a->output;
+    p.lse = a->lse;
+    const int rc = tqb::launch_merge(p, stream);
+    if (rc != TQB_OK) return rc;
+    return TQB_OK;
+}
+
+int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->num_tokens >= 0 && a->num_kv_heads > 0, TQB_ERR_INVALID_ARG,
+                "num_tokens must be >= 0 and num_kv_heads > 0");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
+    TQB_REQUIRE(a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED, "n_centroids must be 16");
+    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS, TQB_ERR_INVALID_ARG,
+                "layout must be TQB_LAYOUT_SOA or TQB_LAYOUT_AOS");
+    if (a->num_tokens == 0) return TQB_OK;
+    TQB_REQUIRE(a->y && a->norms && a->value && a->midpoints && a->slot_mapping && a->kv_cache,
+                TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(!a->norm_correction || a->centroids, TQB_ERR_INVALID_ARG,
+                "norm_correction requires centroids");
+    TQB_REQUIRE(aligned(a->y, 16) && aligned(a->value, 16), TQB_ERR_ALIGNMENT,
+                "y and value must be 16-byte aligned");
+    TQB_REQUIRE(aligned(a->kv_cache, 2) && a->cache_stride_block % 2 == 0, TQB_ERR_ALIGNMENT,
+                "kv_cache and its block stride must be even");
+    const int64_t hk = a->num_kv_heads;
+    if (a->layout == TQB_LAYOUT_SOA) {
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes,
+                    TQB_ERR_INVALID_ARG, "SoA block stride must be >= 16*Hk*134 bytes");
+    } else {
+        TQB_REQUIRE(a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0 &&
+                        a->cache_stride_head >= tqb::kSlotBytes,
+                    TQB_ERR_ALIGNMENT, "AoS strides must be even and describe >=134-byte slots");
+    }
+    DeviceGuard guard(a->kv_cache);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning kv_cache");
+    tqb::StoreParams p{};
+    p.y = a->y;
+    p.norms = a->norms;
+    p.value = a->value;
+    p.mids = a->midpoints;
+    p.cents = a->centroids;
+    p.slots = a->slot_mapping;
+    p.cache = a->kv_cache;
+    p.layout = a->layout;
+    p.block_bytes = a->cache_stride_block;
+    p.pos_stride = a->cache_stride_pos;
+    p.head_stride = a->cache_stride_head;
+    p.N = a->num_tokens;
+    p.H = a->num_kv_heads;
+    p.norm_correction = a->norm_correction;
+    const int rc = tqb::launch_store(p, stream);
+    if (rc != TQB_OK) return rc;
+    return TQB_OK;
+}
+
+}  // extern "C"

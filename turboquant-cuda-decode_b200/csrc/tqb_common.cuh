@@ -1,0 +1,89 @@
+// tqb_common.cuh — shared device helpers for the sm_100a TurboQuant kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace tqb {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlockSize = 16;        // tokens per physical page
+constexpr int kKBytes = kHeadDim / 2; // packed 4-bit K codes per token-head
+constexpr int kVBytes = kHeadDim / 2; // packed 4-bit V codes per token-head
+constexpr int kDataBytes = kKBytes + kVBytes;
+constexpr int kSlotBytes = kDataBytes + 6; // + knorm, vscale, vzero (fp16)
+constexpr int kNumCentroids = 16;
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// Tensor-core MMA: D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col).
+// Fragment ownership (lane = 4*g + c): A {a0a1: row g, cols 2c..2c+1;
+// a2a3: row g+8; a4a5: row g, cols 2c+8..; a6a7: row g+8, cols 2c+8..},
+// B {b0b1: rows 2c..2c+1, col g; b2b3: rows 2c+8.., col g},
+// D {d0d1: row g, cols 2c..2c+1; d2d3: row g+8}.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                          uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// (x & m) | o in one LOP3.
+__device__ __forceinline__ uint32_t and_or(uint32_t x, uint32_t m, uint32_t o) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(x), "r"(m), "r"(o));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
+    return *reinterpret_cast<__half2*>(&u);
+}
+
+// Exact fp16 integers from nibbles: (x & mask) | 0x6400 per half gives
+// 1024 + n (low nibble) or 1024 + 16 n (high nibble); subtracting 1024 is
+// exact.
+__device__ __forceinline__ uint32_t nib_to_h2(uint32_t x, uint32_t mask) {
+    const uint32_t magic = 0x64006400u;
+    __half2 v = u32_as_h2(and_or(x, mask, magic));
+    return h2_as_u32(__hsub2(v, u32_as_h2(magic)));
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
+}
+
+__device__ __forceinline__ float warp_max_xor(float v, int from, int to) {
+    for (int o = from; o <= to; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum_xor(float v, int from, int to) {
+    for (int o = from; o <= to; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Power-of-two exponent e such that max_abs * 2^e lies in [2^14, 2^15):
+// scaling fp16 operands this way keeps hi/lo splits away from both overflow
+// and the subnormal range.  Returns 0 for 0/non-finite inputs.
+__device__ __forceinline__ int fp16_scale_exp(float max_abs) {
+    if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
+    int e;
+    frexpf(max_abs, &e);  // max_abs = m * 2^e, m in [0.5, 1)
+    return 15 - e;
+}
+
+}  // namespace tqb

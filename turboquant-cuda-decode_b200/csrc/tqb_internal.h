@@ -1,0 +1,74 @@
+// tqb_internal.h — kernel parameter blocks shared by the launchers and the
+// C-ABI front end (tqb_api.cu).  Not part of the public interface.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tqb.h"
+
+namespace tqb {
+
+struct Stage1Params {
+    const float* q;
+    int64_t qsb, qsh;
+    const uint8_t* cache;
+    int64_t block_bytes, pos_stride, head_stride;
+    int layout;
+    const int32_t* bt;
+    int64_t bt_stride;
+    int max_blocks;      // entries per block-table row
+    int64_t num_blocks;  // physical blocks (0: unchecked)
+    const int32_t* seq_lens;
+    const int32_t* nsplits;
+    const float* cents;
+    float* mid;
+    int64_t msb, msh, mss;
+    int B, Hq, Hk, G, S;
+    float attn_scale;
+    int64_t num_items;  // B * S * Hk work items, KV head fastest
+};
+
+struct Stage2Params {
+    const float* mid;
+    int64_t msb, msh, mss;
+    const int32_t* seq_lens;
+    const int32_t* nsplits;
+    float* out;
+    int64_t osb, osh;
+    float* lse;
+    int64_t lsb;
+    int B, Hq, S;
+};
+
+struct MergeParams {
+    const float* partials;
+    int G, B, Hq;
+    float* out;
+    float* lse;
+};
+
+struct StoreParams {
+    const float* y;
+    const float* norms;
+    const float* value;
+    const float* mids;
+    const float* cents;
+    const int32_t* slots;
+    uint8_t* cache;
+    int layout;
+    int64_t block_bytes, pos_stride, head_stride;
+    int N, H;
+    int norm_correction;
+};
+
+// Records the CUDA error text for tqb_last_error_detail(); returns
+// TQB_OK or TQB_ERR_LAUNCH.
+int report_launch(cudaError_t e);
+
+int launch_stage1(const Stage1Params& p, cudaStream_t stream, int num_sms);
+int launch_stage2(const Stage2Params& p, cudaStream_t stream);
+int launch_merge(const MergeParams& p, cudaStream_t stream);
+int launch_store(const StoreParams& p, cudaStream_t stream);
+
+}  // namespace tqb

@@ -1,0 +1,449 @@
+// tqb_stage1.cu — sm_100a Stage1 of the TurboQuant 4bit_nc decode.
+//
+// What it computes (reference: reference/soa_decode_v1.py:43-314 for the SoA
+// cache, reference/aos_decode.py:43-313 for the AoS cache): for every
+// (sequence b, query head h, KV split s) the softmax-normalised partial
+// output over the split's tokens and its natural-log LSE,
+//     score_t = knorm_t * (q_rot[b,h] . c[idx_t]) * attn_scale
+//     O       = sum_t exp(score_t - m) * V_t / sum_t exp(score_t - m)
+//     LSE     = m + ln(sum_t exp(score_t - m))
+// with K_t = centroids[idx_t] * knorm_t and V_t = vidx_t * vscale_t + vzero_t.
+//
+// How (B200 design, not a translation of the reference kernels):
+//  * One warp owns one work item (b, KV head, split) and serves all Hq/Hk
+//    query heads of its GQA group; 8 warps per CTA, persistent grid.  With
+//    the KV head as the fastest item index, the 8 warps of a CTA read the 8
+//    interleaved 128-byte head slices of the same 16-token pages, so each
+//    17 KB page streams from HBM as one contiguous run.
+//  * The warp walks the split one 16-token page at a time with 128/64/32-bit
+//    streaming loads, prefetching the next page into registers while the
+//    current one is computed.
+//  * Q.K runs on the tensor cores as D[token, n] = K[token, :] . Qpack[:, n]
+//    (mma.m16n8k16, tokens as M).  The 8 N columns are 4 query heads x
+//    {Q_hi, Q_lo} (fp16 split of the power-of-two scaled fp32 query), and K
+//    is fed twice, as C_hi and C_lo (fp16 split of the scaled centroid).  The
+//    four partial products sum to the fp32-accurate dot product (the single
+//    fp16 MMA of the reference's V2 kernel does not meet 1e-4).  A byte of
+//    packed K (two 4-bit codes) maps to {C_hi pair, C_lo pair} through a
+//    256-entry table replicated 16x in shared memory (bank-conflict free).
+//  * Softmax runs in the exp2 domain on the MMA accumulators; each lane owns
+//    one query head and two tokens of the page, so the row max is three
+//    shuffles.
+//  * P.V runs on the tensor cores as D[dim, n] = Vq[dim, token] . W[token, n]
+//    with dims as M.  Vq are the raw 4-bit codes turned into exact fp16
+//    integers (magic-number OR + subtract), and W = p * vscale split into
+//    fp16 hi/lo across the N columns, so the product is fp32-accurate; the
+//    vzero term sum_t p_t * vzero_t is added per head in fp32.
+#include <cuda_runtime.h>
+
+#include "tqb_common.cuh"
+#include "tqb_internal.h"
+
+namespace tqb {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kLutCopies = 16;
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint4 ld_stream_v4(const uint8_t* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const uint8_t* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const uint8_t* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(r) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ld_stream_u16(const uint8_t* p) {
+    unsigned short r;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
+    return r;
+}
+
+// Registers holding one page's worth of a lane's operands.
+struct PageRegs {
+    uint4 k0, k1;      // K bytes [16c, 16c+16) of tokens 2g and 2g+1
+    uint2 v[4];        // V bytes [8g, 8g+8) of tokens 4c .. 4c+3
+    uint32_t kn, vs, vz;  // fp16 pairs (tokens 2g, 2g+1): knorm, vscale, vzero
+};
+
+// AoS slots are only 2-byte aligned: gather with 16-bit loads.
+__device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
+    return ld_stream_u16(p) | (ld_stream_u16(p + 2) << 16);
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_page(PageRegs& r, const Stage1Params& P,
+                                          int64_t blk, int kvh, int g, int c) {
+    const uint8_t* base = P.cache + blk * P.block_bytes;
+    if (LAYOUT == TQB_LAYOUT_SOA) {
+        const int64_t tok = (int64_t)P.Hk * kDataBytes;  // bytes per token row
+        const uint8_t* head = base + (int64_t)kvh * kDataBytes;
+        r.k0 = ld_stream_v4(head + (2 * g) * tok + 16 * c);
+        r.k1 = ld_stream_v4(head + (2 * g + 1) * tok + 16 * c);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            r.v[j] = ld_stream_v2(head + (4 * c + j) * tok + kKBytes + 8 * g);
+        const uint8_t* meta = base + kBlockSize * tok + (int64_t)kvh * (3 * kBlockSize * 2) + 4 * g;
+        r.kn = ld_stream_u32(meta);
+        r.vs = ld_stream_u32(meta + 2 * kBlockSize);
+        r.vz = ld_stream_u32(meta + 4 * kBlockSize);
+    } else {
+        const uint8_t* s0 = base + (2 * g) * P.pos_stride + (int64_t)kvh * P.head_stride;
+        const uint8_t* s1 = s0 + P.pos_stride;
+        r.k0 = make_uint4(ld2x16(s0 + 16 * c), ld2x16(s0 + 16 * c + 4),
+                          ld2x16(s0 + 16 * c + 8), ld2x16(s0 + 16 * c + 12));
+        r.k1 = make_uint4(ld2x16(s1 + 16 * c), ld2x16(s1 + 16 * c + 4),
+                          ld2x16(s1 + 16 * c + 8), ld2x16(s1 + 16 * c + 12));
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint8_t* sv = base + (4 * c + j) * P.pos_stride +
+                                (int64_t)kvh * P.head_stride + kKBytes + 2 + 8 * g;
+            r.v[j] = make_uint2(ld2x16(sv), ld2x16(sv + 4));
+        }
+        r.kn = ld_stream_u16(s0 + kKBytes) | (ld_stream_u16(s1 + kKBytes) << 16);
+        r.vs = ld_stream_u16(s0 + kKBytes + 2 + kVBytes) |
+               (ld_stream_u16(s1 + kKBytes + 2 + kVBytes) << 16);
+        r.vz = ld_stream_u16(s0 + kKBytes + 4 + kVBytes) |
+               (ld_stream_u16(s1 + kKBytes + 4 + kVBytes) << 16);
+    }
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+template <int NT, int LAYOUT>
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
+    stage1_kernel(const Stage1Params P) {
+    // Shared memory: the replicated K table, then one output staging row
+    // set per warp.  SoA entries are {C_hi pair, C_lo pair}; AoS entries add
+    // the squared centroid sum of the byte for the in-kernel norm correction.
+    constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* stage_all = reinterpret_cast<float*>(smem + 256 * kLutCopies * kEntry);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+
+    // ---- centroid table -------------------------------------------------
+    float cmax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
+    const int ec = fp16_scale_exp(cmax);
+    const float cscale = ldexpf(1.0f, ec);
+    for (int e = tid; e < 256 * kLutCopies; e += kThreads) {
+        const int byte = e / kLutCopies;
+        const float clo = __ldg(P.cents + (byte & 15)) * cscale;
+        const float chi = __ldg(P.cents + (byte >> 4)) * cscale;
+        const __half2 h = __floats2half2_rn(clo, chi);
+        const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
+        uint8_t* dst = smem + (size_t)e * kEntry;
+        if (LAYOUT == TQB_LAYOUT_SOA) {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
+        } else {
+            const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
+            *reinterpret_cast<uint4*>(dst) =
+                make_uint4(h2_as_u32(h), h2_as_u32(l), __float_as_uint(a * a + b * b), 0u);
+        }
+    }
+    __syncthreads();
+
+    const uint32_t lut_lane =
+        static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + (lane & (kLutCopies - 1)) * kEntry;
+    float* stage = stage_all + warp * (NT * 4 * (kHeadDim + 1));
+    const float ln2 = kLn2;
+
+    for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < P.num_items;
+         item += (int64_t)gridDim.x * kWarps) {
+        const int kvh = (int)(item % P.Hk);
+        const int64_t rest = item / P.Hk;
+        const int s = (int)(rest % P.S);
+        const int b = (int)(rest / P.S);
+        const int nsp = P.nsplits ? min(__ldg(P.nsplits + b), P.S) : P.S;
+        if (s >= nsp) continue;
+        // Tokens past the block-table row are outside the sequence's pages.
+        const int L = min(__ldg(P.seq_lens + b), P.max_blocks * kBlockSize);
+        const int split_len = (L + nsp - 1) / nsp;
+        const int start = split_len * s;
+        const int end = min(start + split_len, L);
+        if (start >= end) continue;  // empty split: left unwritten
+
+        // ---- query fragments (B operand of Q.K) --------------------------
+        // Lane (g, c) supplies column n = g (head g>>1 of the n-tile, part
+        // g&1) for dims 32c .. 32c+31, in k order 32c + 4ks + {0,1 | 2,3}.
+        uint32_t qf[NT][16];
+        float kfac[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int hl = (g >> 1) + 4 * nt;
+            float qv[32];
+            float amax = 0.0f;
+            if (hl < P.G) {
+                const float* qp = P.q + (int64_t)b * P.qsb + (int64_t)(kvh * P.G + hl) * P.qsh + 32 * c;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(qp) + j);
+                    qv[4 * j] = v.x; qv[4 * j + 1] = v.y; qv[4 * j + 2] = v.z; qv[4 * j + 3] = v.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(qv[j]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) qv[j] = 0.0f;
+            }
+            amax = warp_max_xor(amax, 1, 2);
+            const int eq = fp16_scale_exp(amax);
+            const float qscale = ldexpf(1.0f, eq);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
+                const __half2 h = __floats2half2_rn(x0, x1);
+                const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+                qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
+            }
+            // Score factor of this lane's softmax head (c + 4 nt), whose
+            // scale exponent lives on lane 8c.
+            const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
+            kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
+        }
+
+        float m_run[NT], l_part[NT], z_part[NT];
+        float acc[NT][8][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            m_run[nt] = -INFINITY;
+            l_part[nt] = 0.0f;
+            z_part[nt] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) acc[nt][i][k] = 0.0f;
+        }
+
+        // ---- page loop -----------------------------------------------------
+        const int p_first = start / kBlockSize, p_last = (end - 1) / kBlockSize;
+        const int32_t* bt_row = P.bt + (int64_t)b * P.bt_stride;
+        int blk_reg = (p_first + lane <= p_last) ? __ldg(bt_row + p_first + lane) : 0;
+        // Block ids outside [0, num_blocks) mask their page and read block 0.
+        auto valid_blk = [&](int id) { return id >= 0 && (P.num_blocks == 0 || id < P.num_blocks); };
+        int blk = __shfl_sync(0xffffffffu, blk_reg, 0);
+        bool nxt_ok = valid_blk(blk);
+        PageRegs nxt;
+        load_page<LAYOUT>(nxt, P, nxt_ok ? blk : 0, kvh, g, c);
+
+        for (int p = p_first; p <= p_last; p++) {
+            const PageRegs cur = nxt;
+            const bool page_ok = nxt_ok;
+            if (p < p_last) {
+                const int rel = p + 1 - p_first;
+                if ((rel & 31) == 0)
+                    blk_reg = (p + 1 + lane <= p_last) ? __ldg(bt_row + p + 1 + lane) : 0;
+                blk = __shfl_sync(0xffffffffu, blk_reg, rel & 31);
+                nxt_ok = valid_blk(blk);
+                load_page<LAYOUT>(nxt, P, nxt_ok ? blk : 0, kvh, g, c);
+            }
+            const int t0 = p * kBlockSize + 2 * g;  // tokens t0 (row g), t0+1 (row g+8)
+            const bool va = page_ok && t0 >= start && t0 < end;
+            const bool vb = page_ok && t0 + 1 >= start && t0 + 1 < end;
+
+            // -- Q.K on the tensor cores --
+            float dq[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) dq[nt][k] = 0.0f;
+            float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
+#pragma unroll
+            for (int ks = 0; ks < 8; ks++) {
+                const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
+                const int sh = 16 * (ks & 1);
+                const uint32_t ia = ((w0 >> sh) & 0xFFu) * (kLutCopies * kEntry);
+                const uint32_t ib = ((w0 >> (sh + 8)) & 0xFFu) * (kLutCopies * kEntry);
+                const uint32_t ic = ((w1 >> sh) & 0xFFu) * (kLutCopies * kEntry);
+                const uint32_t id = ((w1 >> (sh + 8)) & 0xFFu) * (kLutCopies * kEntry);
+                uint32_t e0x, e0y, e1x, e1y, e2x, e2y, e3x, e3y;
+                if (LAYOUT == TQB_LAYOUT_SOA) {
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e0x), "=r"(e0y) : "r"(lut_lane + ia));
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e1x), "=r"(e1y) : "r"(lut_lane + ic));
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e2x), "=r"(e2y) : "r"(lut_lane + ib));
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e3x), "=r"(e3y) : "r"(lut_lane + id));
+                } else {
+                    uint32_t q0, q1, q2, q3;
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                                 : "=r"(e0x), "=r"(e0y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ia));
+                    csq0 += __uint_as_float(q0);
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                                 : "=r"(e1x), "=r"(e1y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ic));
+                    csq1 += __uint_as_float(q0);
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                                 : "=r"(e2x), "=r"(e2y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ib));
+                    csq0 += __uint_as_float(q0);
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                                 : "=r"(e3x), "=r"(e3y), "=r"(q2), "=r"(q3) : "r"(lut_lane + id));
+                    csq1 += __uint_as_float(q2);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    mma_16816(dq[nt], e0x, e1x, e2x, e3x, qf[nt][2 * ks], qf[nt][2 * ks + 1]);
+                    mma_16816(dq[nt], e0y, e1y, e2y, e3y, qf[nt][2 * ks], qf[nt][2 * ks + 1]);
+                }
+            }
+            float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
+            if (LAYOUT == TQB_LAYOUT_AOS) {
+                // Norm correction c / |c| (reference/aos_decode.py:199-206).
+                csq0 = warp_sum_xor(csq0, 1, 2);
+                csq1 = warp_sum_xor(csq1, 1, 2);
+                kn0 = kn0 / sqrtf(csq0 + 1e-16f);
+                kn1 = kn1 / sqrtf(csq1 + 1e-16f);
+            }
+            const float vs0 = va ? half_bits_to_float(cur.vs) : 0.0f;
+            const float vs1 = vb ? half_bits_to_float(cur.vs >> 16) : 0.0f;
+            const float vz0 = va ? half_bits_to_float(cur.vz) : 0.0f;
+            const float vz1 = vb ? half_bits_to_float(cur.vz >> 16) : 0.0f;
+
+            // -- online softmax (exp2 domain), exact rescale --
+            uint32_t bw0[NT], bw1[NT];
+            float alpha[NT];
+            bool rescale = false;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float s0 = (dq[nt][0] + dq[nt][1]) * kn0 * kfac[nt];
+                float s1 = (dq[nt][2] + dq[nt][3]) * kn1 * kfac[nt];
+                s0 = va ? s0 : -INFINITY;
+                s1 = vb ? s1 : -INFINITY;
+                const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
+                const float mnew = fmaxf(m_run[nt], tmax);
+                // A page with no valid token keeps the state (-inf - -inf guard).
+                const float mref = mnew == -INFINITY ? 0.0f : mnew;
+                alpha[nt] = ex2(m_run[nt] - mref);
+                rescale |= alpha[nt] != 1.0f;
+                const float p0 = ex2(s0 - mref), p1 = ex2(s1 - mref);
+                l_part[nt] = l_part[nt] * alpha[nt] + (p0 + p1);
+                z_part[nt] = z_part[nt] * alpha[nt] + (p0 * vz0 + p1 * vz1);
+                m_run[nt] = mnew;
+                const float w0 = p0 * vs0, w1 = p1 * vs1;
+                const __half2 wh = __floats2half2_rn(w0, w1);
+                const __half2 wl = __floats2half2_rn(w0 - __low2float(wh), w1 - __high2float(wh));
+                // Transpose W into the B fragment of P.V: lane (g, c) takes
+                // tokens {4c, 4c+1} from lane 8c + (g>>1) and {4c+2, 4c+3}
+                // from lane 8c + 4 + (g>>1), part g&1.
+                const int srcA = 8 * c + (g >> 1);
+                const uint32_t hA = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA);
+                const uint32_t lA = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA);
+                const uint32_t hB = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA + 4);
+                const uint32_t lB = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA + 4);
+                bw0[nt] = (g & 1) ? lA : hA;
+                bw1[nt] = (g & 1) ? lB : hB;
+            }
+            if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++) acc[nt][i][k] *= alpha[nt];
+            }
+
+            // -- P.V on the tensor cores --
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int wi = i >> 2, bi = i & 3;
+                const uint32_t sel = (uint32_t)(bi | (bi << 4) | ((4 + bi) << 8) | ((4 + bi) << 12));
+                const uint32_t x0 = wi ? cur.v[0].y : cur.v[0].x;
+                const uint32_t x1 = wi ? cur.v[1].y : cur.v[1].x;
+                const uint32_t x2 = wi ? cur.v[2].y : cur.v[2].x;
+                const uint32_t x3 = wi ? cur.v[3].y : cur.v[3].x;
+                const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
+                const uint32_t a0 = nib_to_h2(p01, 0x000F000Fu);
+                const uint32_t a1 = nib_to_h2(p01, 0x00F000F0u);
+                const uint32_t a2 = nib_to_h2(p23, 0x000F000Fu);
+                const uint32_t a3 = nib_to_h2(p23, 0x00F000F0u);
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) mma_16816(acc[nt][i], a0, a1, a2, a3, bw0[nt], bw1[nt]);
+            }
+        }
+
+        // ---- epilogue: normalise, stage, coalesced write -------------------
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            float l = warp_sum_xor(l_part[nt], 4, 16);
+            l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
+            const float z = warp_sum_xor(z_part[nt], 4, 16);
+            const int hl = c + 4 * nt;
+            float* row = stage + (c + 4 * nt) * (kHeadDim + 1);
+            if (hl < P.G) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float lo = acc[nt][i][0] + acc[nt][i][1] + z;
+                    const float hi = (acc[nt][i][2] + acc[nt][i][3]) * 0.0625f + z;
+                    row[16 * g + 2 * i] = __fdiv_rn(lo, l);
+                    row[16 * g + 2 * i + 1] = __fdiv_rn(hi, l);
+                }
+                if (g == 0) row[kHeadDim] = m_run[nt] * ln2 + logf(l);
+            }
+        }
+        __syncwarp();
+        const int nheads = min(P.G, NT * 4);
+        for (int hl = 0; hl < nheads; hl++) {
+            float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + hl) * P.msh + (int64_t)s * P.mss;
+            const float* src = stage + hl * (kHeadDim + 1);
+            for (int j = lane; j <= kHeadDim; j += 32) dst[j] = src[j];
+        }
+        __syncwarp();
+    }
+}
+
+template <int NT, int LAYOUT>
+int launch_t(const Stage1Params& P, cudaStream_t stream, int num_sms) {
+    constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
+    const size_t smem = 256 * kLutCopies * kEntry + (size_t)kWarps * NT * 4 * (kHeadDim + 1) * sizeof(float);
+    auto kern = stage1_kernel<NT, LAYOUT>;
+    static thread_local int configured_dev = -1;  // per template instance
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return TQB_ERR_CUDA;
+        configured_dev = dev;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const int64_t need = (P.num_items + kWarps - 1) / kWarps;
+    const int64_t grid = need < (int64_t)num_sms * per_sm ? need : (int64_t)num_sms * per_sm;
+    if (grid <= 0) return TQB_OK;
+    kern<<<(unsigned)grid, kThreads, smem, stream>>>(P);
+    return report_launch(cudaGetLastError());
+}
+
+}  // namespace
+
+int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
+    const bool soa = P.layout == TQB_LAYOUT_SOA;
+    if (P.G <= 4) return soa ? launch_t<1, TQB_LAYOUT_SOA>(P, stream, num_sms)
+                             : launch_t<1, TQB_LAYOUT_AOS>(P, stream, num_sms);
+    return soa ? launch_t<2, TQB_LAYOUT_SOA>(P, stream, num_sms)
+               : launch_t<2, TQB_LAYOUT_AOS>(P, stream, num_sms);
+}
+
+}  // namespace tqb
