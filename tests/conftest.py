@@ -49,9 +49,10 @@ def assert_close(got, ref, atol=ATOL, rtol=RTOL, what=""):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     assert got.shape == ref.shape, (what, got.shape, ref.shape)
-    both_nan = np.isnan(got) & np.isnan(ref)
-    err = np.abs(got - ref)
-    bad = ~both_nan & ~(err <= atol + rtol * np.abs(ref))
+    same_special = (np.isnan(got) & np.isnan(ref)) | (np.isinf(ref) & (got == ref))
+    with np.errstate(invalid="ignore"):
+        err = np.abs(got - ref)
+        bad = ~same_special & ~(err <= atol + rtol * np.abs(ref))
     if bad.any():
         i = np.argwhere(bad)[0]
         raise AssertionError(

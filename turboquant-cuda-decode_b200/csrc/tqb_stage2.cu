@@ -18,6 +18,11 @@ namespace {
 
 constexpr int kWarpsPerCta = 8;
 
+// Two passes per (b, h) so that every load is independent of the previous
+// split's result: (1) lane s of a 32-split chunk reads LSE_s, the warp forms
+// the max and the weights w_s = exp(LSE_s - max); (2) every lane reads its 4
+// dims of all splits (unrolled, loads in flight together) and accumulates
+// w_s * O_s.  Same algebra as the reference's running merge.
 __global__ void __launch_bounds__(kWarpsPerCta * 32) stage2_kernel(const Stage2Params P) {
     const int lane = threadIdx.x & 31;
     const int64_t item = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
@@ -27,29 +32,38 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) stage2_kernel(const Stage2P
     const int L = __ldg(P.seq_lens + b);
     const int split_len = nsp > 0 ? (L + nsp - 1) / nsp : 0;
     const float* row0 = P.mid + (int64_t)b * P.msb + (int64_t)h * P.msh;
+    auto nonempty = [&](int s) { return s < nsp && split_len * s < min(split_len * (s + 1), L); };
+
+    float gmax = -INFINITY;
+    for (int s0 = 0; s0 < nsp; s0 += 32) {
+        const int s = s0 + lane;
+        const float l = nonempty(s) ? __ldg(row0 + (int64_t)s * P.mss + kHeadDim) : -INFINITY;
+        gmax = fmaxf(gmax, warp_max_xor(l, 1, 16));
+    }
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float rmax = -INFINITY, rsum = 0.0f;
-    for (int s = 0; s < nsp; s++) {
-        const int start = split_len * s;
-        const int end = min(start + split_len, L);
-        if (end <= start) continue;  // empty split (baseline/stage2.py:37-40)
-        const float* row = row0 + (int64_t)s * P.mss;
-        const float slse = __ldg(row + kHeadDim);
-        float v[4];
+    float wsum = 0.0f;
+    for (int s0 = 0; s0 < nsp; s0 += 32) {
+        const int s = s0 + lane;
+        const bool ok = nonempty(s);
+        const float l = ok ? __ldg(row0 + (int64_t)s * P.mss + kHeadDim) : -INFINITY;
+        const float wl = ok ? expf(l - gmax) : 0.0f;
+        wsum += warp_sum_xor(wl, 1, 16);
+        const int n = min(32, nsp - s0);
+#pragma unroll 8
+        for (int k = 0; k < n; k++) {
+            const float w = __shfl_sync(0xffffffffu, wl, k);
+            const float* row = row0 + (int64_t)(s0 + k) * P.mss;
 #pragma unroll
-        for (int j = 0; j < 4; j++) v[j] = __ldg(row + lane + 32 * j);
-        const float nmax = fmaxf(rmax, slse);
-        const float old_scale = expf(rmax - nmax);
-        const float w = expf(slse - nmax);
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[j] = acc[j] * old_scale + w * v[j];
-        rsum = rsum * old_scale + w;
-        rmax = nmax;
+            for (int j = 0; j < 4; j++) {
+                const float v = __ldg(row + lane + 32 * j);
+                acc[j] += w * (w != 0.0f ? v : 0.0f);
+            }
+        }
     }
     float* out = P.out + (int64_t)b * P.osb + (int64_t)h * P.osh;
 #pragma unroll
-    for (int j = 0; j < 4; j++) out[lane + 32 * j] = __fdiv_rn(acc[j], rsum);
-    if (lane == 0) P.lse[(int64_t)b * P.lsb + h] = rmax + logf(rsum);
+    for (int j = 0; j < 4; j++) out[lane + 32 * j] = __fdiv_rn(acc[j], wsum);
+    if (lane == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
 }
 
 // Cross-GPU merge of G (O, LSE) partials laid out [G, B, Hq, D+1]; parts
