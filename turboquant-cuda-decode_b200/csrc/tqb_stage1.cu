@@ -16,8 +16,9 @@
 //    interleaved 128-byte head slices of the same 16-token pages, so each
 //    17 KB page streams from HBM as one contiguous run.
 //  * The warp walks the split one 16-token page at a time with 128/64/32-bit
-//    streaming loads, prefetching the next page into registers while the
-//    current one is computed.
+//    streaming loads into a two-page register ring, and asks L2 for the page
+//    after that (prefetch.global.L2), so DRAM latency is covered without
+//    spending registers on a deeper ring.
 //  * Q.K runs on the tensor cores as D[token, n] = K[token, :] . Qpack[:, n]
 //    (mma.m16n8k16, tokens as M).  The 8 N columns are 4 query heads x
 //    {Q_hi, Q_lo} (fp16 split of the power-of-two scaled fp32 query), and K
@@ -25,13 +26,15 @@
 //    four partial products sum to the fp32-accurate dot product (the single
 //    fp16 MMA of the reference's V2 kernel does not meet 1e-4).  A byte of
 //    packed K (two 4-bit codes) maps to {C_hi pair, C_lo pair} through a
-//    256-entry table replicated 16x in shared memory (bank-conflict free).
+//    256-entry table with one copy per lane in shared memory (bank-conflict
+//    free); one PRMT forms the table offset from the byte and the lane.
 //  * Softmax runs in the exp2 domain on the MMA accumulators; each lane owns
 //    one query head and two tokens of the page, so the row max is three
 //    shuffles.
 //  * P.V runs on the tensor cores as D[dim, n] = Vq[dim, token] . W[token, n]
-//    with dims as M.  Vq are the raw 4-bit codes turned into exact fp16
-//    integers (magic-number OR + subtract), and W = p * vscale split into
+//    with dims as M.  The raw 4-bit codes are used as fp16 subnormals
+//    (code * 2^-24, or code * 2^-20 for the high nibble) with one AND, so the
+//    operand is exact and costs no conversion; W = p * vscale is split into
 //    fp16 hi/lo across the N columns, so the product is fp32-accurate; the
 //    vzero term sum_t p_t * vzero_t is added per head in fp32.
 #include <cuda_runtime.h>
@@ -45,7 +48,8 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kLutCopies = 16;
+constexpr int kLutStride = 256;              // bytes per table entry (all copies)
+constexpr int kLutBytes = 256 * kLutStride;  // 64 KB
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -77,13 +81,66 @@ __device__ __forceinline__ uint32_t ld_stream_u16(const uint8_t* p) {
     asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
     return r;
 }
+__device__ __forceinline__ void prefetch_l2(const uint8_t* p) {
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(addr));
+    return r;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(addr));
+    return r;
+}
 
-// Registers holding one page's worth of a lane's operands.
+// One page's worth of a lane's operands.
 struct PageRegs {
-    uint4 k0, k1;      // K bytes [16c, 16c+16) of tokens 2g and 2g+1
-    uint2 v[4];        // V bytes [8g, 8g+8) of tokens 4c .. 4c+3
+    uint4 k0, k1;         // K bytes [16c, 16c+16) of tokens 2g and 2g+1
+    uint2 v[4];           // V bytes [8g, 8g+8) of tokens 4c .. 4c+3
     uint32_t kn, vs, vz;  // fp16 pairs (tokens 2g, 2g+1): knorm, vscale, vzero
 };
+
+// Byte offsets, inside one physical block, of a lane's operands for KV head
+// kvh (fixed for a work item).  Token rows are `row` bytes apart.
+struct LaneOffsets {
+    uint32_t k0;    // K bytes of token 2g (token 2g+1: + row)
+    uint32_t v0;    // V bytes of token 4c (token 4c+j: + j * row)
+    uint32_t meta;  // SoA: knorm pair; AoS: slot metadata of token 2g
+    uint32_t pf;    // L2 prefetch target of this lane
+    uint32_t row;   // bytes between consecutive tokens of a page
+};
+
+template <int LAYOUT>
+__device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int kvh, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    LaneOffsets o;
+    if (LAYOUT == TQB_LAYOUT_SOA) {
+        const uint32_t tok = (uint32_t)P.Hk * kDataBytes;
+        const uint32_t head = (uint32_t)kvh * kDataBytes;
+        o.row = tok;
+        o.k0 = (2 * g) * tok + head + 16 * c;
+        o.v0 = (4 * c) * tok + head + kKBytes + 8 * g;
+        o.meta = kBlockSize * tok + (uint32_t)kvh * (3 * kBlockSize * 2) + 4 * g;
+        // lanes 0-15: first byte of token row `lane`; lanes 16-30: last byte
+        // of a row (a row may straddle two lines); lane 31: the metadata
+        // strip of the head (96 bytes from a 32-byte boundary).
+        const uint32_t r = (uint32_t)(lane & 15) * tok + head;
+        o.pf = lane < 16 ? r : (lane == 31 ? kBlockSize * tok + (uint32_t)kvh * 96 : r + kDataBytes - 1);
+    } else {
+        const uint32_t pos = (uint32_t)P.pos_stride, hs = (uint32_t)P.head_stride * kvh;
+        o.row = pos;
+        o.k0 = (2 * g) * pos + hs + 16 * c;
+        o.v0 = (4 * c) * pos + hs + kKBytes + 2 + 8 * g;
+        o.meta = (2 * g) * pos + hs + kKBytes;
+        const uint32_t r = (uint32_t)(lane & 15) * pos + hs;
+        o.pf = lane < 16 ? r : r + kSlotBytes - 1;
+    }
+    return o;
+}
 
 // AoS slots are only 2-byte aligned: gather with 16-bit loads.
 __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
@@ -91,39 +148,33 @@ __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
 }
 
 template <int LAYOUT>
-__device__ __forceinline__ void load_page(PageRegs& r, const Stage1Params& P,
-                                          int64_t blk, int kvh, int g, int c) {
-    const uint8_t* base = P.cache + blk * P.block_bytes;
+__device__ __forceinline__ void load_page(PageRegs& r, const uint8_t* base, const LaneOffsets& o) {
     if (LAYOUT == TQB_LAYOUT_SOA) {
-        const int64_t tok = (int64_t)P.Hk * kDataBytes;  // bytes per token row
-        const uint8_t* head = base + (int64_t)kvh * kDataBytes;
-        r.k0 = ld_stream_v4(head + (2 * g) * tok + 16 * c);
-        r.k1 = ld_stream_v4(head + (2 * g + 1) * tok + 16 * c);
+        const uint8_t* k = base + o.k0;
+        const uint8_t* v = base + o.v0;
+        const uint8_t* m = base + o.meta;
+        r.k0 = ld_stream_v4(k);
+        r.k1 = ld_stream_v4(k + o.row);
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            r.v[j] = ld_stream_v2(head + (4 * c + j) * tok + kKBytes + 8 * g);
-        const uint8_t* meta = base + kBlockSize * tok + (int64_t)kvh * (3 * kBlockSize * 2) + 4 * g;
-        r.kn = ld_stream_u32(meta);
-        r.vs = ld_stream_u32(meta + 2 * kBlockSize);
-        r.vz = ld_stream_u32(meta + 4 * kBlockSize);
+        for (int j = 0; j < 4; j++) r.v[j] = ld_stream_v2(v + j * o.row);
+        r.kn = ld_stream_u32(m);
+        r.vs = ld_stream_u32(m + 2 * kBlockSize);
+        r.vz = ld_stream_u32(m + 4 * kBlockSize);
     } else {
-        const uint8_t* s0 = base + (2 * g) * P.pos_stride + (int64_t)kvh * P.head_stride;
-        const uint8_t* s1 = s0 + P.pos_stride;
-        r.k0 = make_uint4(ld2x16(s0 + 16 * c), ld2x16(s0 + 16 * c + 4),
-                          ld2x16(s0 + 16 * c + 8), ld2x16(s0 + 16 * c + 12));
-        r.k1 = make_uint4(ld2x16(s1 + 16 * c), ld2x16(s1 + 16 * c + 4),
-                          ld2x16(s1 + 16 * c + 8), ld2x16(s1 + 16 * c + 12));
+        const uint8_t* s0 = base + o.k0;
+        const uint8_t* s1 = s0 + o.row;
+        r.k0 = make_uint4(ld2x16(s0), ld2x16(s0 + 4), ld2x16(s0 + 8), ld2x16(s0 + 12));
+        r.k1 = make_uint4(ld2x16(s1), ld2x16(s1 + 4), ld2x16(s1 + 8), ld2x16(s1 + 12));
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint8_t* sv = base + (4 * c + j) * P.pos_stride +
-                                (int64_t)kvh * P.head_stride + kKBytes + 2 + 8 * g;
+            const uint8_t* sv = base + o.v0 + j * o.row;
             r.v[j] = make_uint2(ld2x16(sv), ld2x16(sv + 4));
         }
-        r.kn = ld_stream_u16(s0 + kKBytes) | (ld_stream_u16(s1 + kKBytes) << 16);
-        r.vs = ld_stream_u16(s0 + kKBytes + 2 + kVBytes) |
-               (ld_stream_u16(s1 + kKBytes + 2 + kVBytes) << 16);
-        r.vz = ld_stream_u16(s0 + kKBytes + 4 + kVBytes) |
-               (ld_stream_u16(s1 + kKBytes + 4 + kVBytes) << 16);
+        const uint8_t* m0 = base + o.meta;
+        const uint8_t* m1 = m0 + o.row;
+        r.kn = ld_stream_u16(m0) | (ld_stream_u16(m1) << 16);
+        r.vs = ld_stream_u16(m0 + 2 + kVBytes) | (ld_stream_u16(m1 + 2 + kVBytes) << 16);
+        r.vz = ld_stream_u16(m0 + 4 + kVBytes) | (ld_stream_u16(m1 + 4 + kVBytes) << 16);
     }
 }
 
@@ -131,15 +182,149 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
+// Running softmax / output state of one lane for one work item.
+template <int NT>
+struct ItemState {
+    uint32_t qf[NT][16];  // Q.K B fragments
+    float kfac[NT];       // score factor of this lane's head
+    float m_run[NT], l_part[NT], z_part[NT];
+    float acc[NT][8][4];  // P.V accumulators (rows scaled by 2^-24 / 2^-20)
+};
+
+// One 16-token page of one work item.
+template <int NT, int LAYOUT>
+__device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& cur, bool page_ok,
+                                             int tok0, int start, int end, uint32_t lut_base,
+                                             uint32_t lut_sel_src, int g, int c) {
+    const bool va = page_ok && tok0 >= start && tok0 < end;
+    const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
+
+    // -- Q.K on the tensor cores --
+    float dq[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) dq[nt][k] = 0.0f;
+    float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+        const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
+        const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
+        // (byte << 8) | this lane's copy offset, in one PRMT
+        const uint32_t ia = prmt(w0, lut_sel_src, 0x5504u | (jA << 4));
+        const uint32_t ic = prmt(w1, lut_sel_src, 0x5504u | (jA << 4));
+        const uint32_t ib = prmt(w0, lut_sel_src, 0x5504u | (jB << 4));
+        const uint32_t id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
+        uint2 e0, e1, e2, e3;
+        if (LAYOUT == TQB_LAYOUT_SOA) {
+            e0 = lds_v2(lut_base + ia);
+            e1 = lds_v2(lut_base + ic);
+            e2 = lds_v2(lut_base + ib);
+            e3 = lds_v2(lut_base + id);
+        } else {
+            const uint4 f0 = lds_v4(lut_base + ia), f1 = lds_v4(lut_base + ic);
+            const uint4 f2 = lds_v4(lut_base + ib), f3 = lds_v4(lut_base + id);
+            e0 = make_uint2(f0.x, f0.y);
+            e1 = make_uint2(f1.x, f1.y);
+            e2 = make_uint2(f2.x, f2.y);
+            e3 = make_uint2(f3.x, f3.y);
+            csq0 += __uint_as_float(f0.z) + __uint_as_float(f2.z);
+            csq1 += __uint_as_float(f1.z) + __uint_as_float(f3.z);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            mma_16816(dq[nt], e0.x, e1.x, e2.x, e3.x, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+            mma_16816(dq[nt], e0.y, e1.y, e2.y, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+        }
+    }
+    float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
+    if (LAYOUT == TQB_LAYOUT_AOS) {
+        // Norm correction c / |c| (reference/aos_decode.py:199-206).
+        csq0 = warp_sum_xor(csq0, 1, 2);
+        csq1 = warp_sum_xor(csq1, 1, 2);
+        kn0 = kn0 * rsqrtf(csq0 + 1e-16f);
+        kn1 = kn1 * rsqrtf(csq1 + 1e-16f);
+    }
+    const float vs0 = va ? half_bits_to_float(cur.vs) : 0.0f;
+    const float vs1 = vb ? half_bits_to_float(cur.vs >> 16) : 0.0f;
+    const float vz0 = va ? half_bits_to_float(cur.vz) : 0.0f;
+    const float vz1 = vb ? half_bits_to_float(cur.vz >> 16) : 0.0f;
+
+    // -- online softmax (exp2 domain), exact rescale --
+    uint32_t bw0[NT], bw1[NT];
+    float alpha[NT];
+    bool rescale = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        float s0 = (dq[nt][0] + dq[nt][1]) * kn0 * st.kfac[nt];
+        float s1 = (dq[nt][2] + dq[nt][3]) * kn1 * st.kfac[nt];
+        s0 = va ? s0 : -INFINITY;
+        s1 = vb ? s1 : -INFINITY;
+        const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
+        const float mold = st.m_run[nt];
+        const float mnew = fmaxf(mold, tmax);
+        // A page with no valid token keeps the state (-inf - -inf guard).
+        const float mref = mnew == -INFINITY ? 0.0f : mnew;
+        alpha[nt] = ex2(mold - mref);
+        // The first page of an item has nothing to rescale.
+        rescale |= (alpha[nt] != 1.0f) && (mold != -INFINITY);
+        const float p0 = ex2(s0 - mref), p1 = ex2(s1 - mref);
+        st.l_part[nt] = st.l_part[nt] * alpha[nt] + (p0 + p1);
+        st.z_part[nt] = st.z_part[nt] * alpha[nt] + (p0 * vz0 + p1 * vz1);
+        st.m_run[nt] = mnew;
+        const float w0 = p0 * vs0, w1 = p1 * vs1;
+        const __half2 wh = __floats2half2_rn(w0, w1);
+        const __half2 wl = __floats2half2_rn(w0 - __low2float(wh), w1 - __high2float(wh));
+        // Transpose W into the B fragment of P.V: lane (g, c) takes tokens
+        // {4c, 4c+1} from lane 8c + (g>>1) and {4c+2, 4c+3} from lane
+        // 8c + 4 + (g>>1), part g&1.
+        const int srcA = 8 * c + (g >> 1);
+        const uint32_t hA = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA);
+        const uint32_t lA = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA);
+        const uint32_t hB = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA + 4);
+        const uint32_t lB = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA + 4);
+        bw0[nt] = (g & 1) ? lA : hA;
+        bw1[nt] = (g & 1) ? lB : hB;
+    }
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) st.acc[nt][i][k] *= alpha[nt];
+    }
+
+    // -- P.V on the tensor cores; codes enter as exact fp16 subnormals --
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int wi = i >> 2, bi = i & 3;
+        const uint32_t sel = (uint32_t)(bi | (bi << 4) | ((4 + bi) << 8) | ((4 + bi) << 12));
+        const uint32_t x0 = wi ? cur.v[0].y : cur.v[0].x;
+        const uint32_t x1 = wi ? cur.v[1].y : cur.v[1].x;
+        const uint32_t x2 = wi ? cur.v[2].y : cur.v[2].x;
+        const uint32_t x3 = wi ? cur.v[3].y : cur.v[3].x;
+        const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
+        const uint32_t a0 = p01 & 0x000F000Fu;  // row g:   code * 2^-24
+        const uint32_t a1 = p01 & 0x00F000F0u;  // row g+8: code * 2^-20
+        const uint32_t a2 = p23 & 0x000F000Fu;
+        const uint32_t a3 = p23 & 0x00F000F0u;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) mma_16816(st.acc[nt][i], a0, a1, a2, a3, bw0[nt], bw1[nt]);
+    }
+}
+
 template <int NT, int LAYOUT>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     stage1_kernel(const Stage1Params P) {
-    // Shared memory: the replicated K table, then one output staging row
-    // set per warp.  SoA entries are {C_hi pair, C_lo pair}; AoS entries add
-    // the squared centroid sum of the byte for the in-kernel norm correction.
+    // Shared memory: the K table (256 entries x 256 bytes: SoA keeps 32 lane
+    // copies of {C_hi pair, C_lo pair}; AoS keeps 16 copies that also carry
+    // the byte's squared centroid sum for the in-kernel norm correction),
+    // then one output staging row set per warp.
     constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
-    extern __shared__ __align__(16) uint8_t smem[];
-    float* stage_all = reinterpret_cast<float*>(smem + 256 * kLutCopies * kEntry);
+    constexpr int kCopies = kLutStride / kEntry;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* stage_all = reinterpret_cast<float*>(smem + kLutBytes);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -151,27 +336,26 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     const int ec = fp16_scale_exp(cmax);
     const float cscale = ldexpf(1.0f, ec);
-    for (int e = tid; e < 256 * kLutCopies; e += kThreads) {
-        const int byte = e / kLutCopies;
-        const float clo = __ldg(P.cents + (byte & 15)) * cscale;
-        const float chi = __ldg(P.cents + (byte >> 4)) * cscale;
+    for (int e = tid; e < 256 * kCopies; e += kThreads) {
+        const int byte = e / kCopies;
+        const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
+        const float clo = a * cscale, chi = b * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
         uint8_t* dst = smem + (size_t)e * kEntry;
         if (LAYOUT == TQB_LAYOUT_SOA) {
             *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
         } else {
-            const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
             *reinterpret_cast<uint4*>(dst) =
                 make_uint4(h2_as_u32(h), h2_as_u32(l), __float_as_uint(a * a + b * b), 0u);
         }
     }
     __syncthreads();
 
-    const uint32_t lut_lane =
-        static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + (lane & (kLutCopies - 1)) * kEntry;
+    const uint32_t lut_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    // PRMT source: byte 0 = this lane's copy offset inside an entry, byte 1 = 0.
+    const uint32_t lut_sel_src = (uint32_t)(lane % kCopies) * kEntry;
     float* stage = stage_all + warp * (NT * 4 * (kHeadDim + 1));
-    const float ln2 = kLn2;
 
     for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < P.num_items;
          item += (int64_t)gridDim.x * kWarps) {
@@ -188,11 +372,33 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         const int end = min(start + split_len, L);
         if (start >= end) continue;  // empty split: left unwritten
 
+        const int p_first = start / kBlockSize, p_last = (end - 1) / kBlockSize;
+        const int32_t* bt_row = P.bt + (int64_t)b * P.bt_stride;
+        // Block ids of pages [w0, w0 + 32), one per lane.
+        int w0 = p_first;
+        int blk_reg = (p_first + lane <= p_last) ? __ldg(bt_row + p_first + lane) : 0;
+        const LaneOffsets off = lane_offsets<LAYOUT>(P, kvh, lane);
+        auto valid_blk = [&](int id) { return id >= 0 && (P.num_blocks == 0 || id < P.num_blocks); };
+        // Block id of page pp (pp in [w0, w0 + 32)).
+        auto blk_of = [&](int pp) { return __shfl_sync(0xffffffffu, blk_reg, pp - w0); };
+
+        // Start the first page's loads before the query prologue.
+        PageRegs ra, rb;
+        bool ok_a, ok_b = false;
+        {
+            const int id = blk_of(p_first);
+            ok_a = valid_blk(id);
+            load_page<LAYOUT>(ra, P.cache + (int64_t)(ok_a ? id : 0) * P.block_bytes, off);
+            if (p_first + 1 <= p_last) {
+                const int nb = blk_of(p_first + 1);
+                if (valid_blk(nb)) prefetch_l2(P.cache + (int64_t)nb * P.block_bytes + off.pf);
+            }
+        }
+
         // ---- query fragments (B operand of Q.K) --------------------------
         // Lane (g, c) supplies column n = g (head g>>1 of the n-tile, part
         // g&1) for dims 32c .. 32c+31, in k order 32c + 4ks + {0,1 | 2,3}.
-        uint32_t qf[NT][16];
-        float kfac[NT];
+        ItemState<NT> st;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             const int hl = (g >> 1) + 4 * nt;
@@ -219,187 +425,66 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
                 const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
                 const __half2 h = __floats2half2_rn(x0, x1);
                 const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-                qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
+                st.qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
             }
             // Score factor of this lane's softmax head (c + 4 nt), whose
             // scale exponent lives on lane 8c.
             const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
-            kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
-        }
-
-        float m_run[NT], l_part[NT], z_part[NT];
-        float acc[NT][8][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            m_run[nt] = -INFINITY;
-            l_part[nt] = 0.0f;
-            z_part[nt] = 0.0f;
+            st.kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
+            st.m_run[nt] = -INFINITY;
+            st.l_part[nt] = 0.0f;
+            st.z_part[nt] = 0.0f;
 #pragma unroll
             for (int i = 0; i < 8; i++)
 #pragma unroll
-                for (int k = 0; k < 4; k++) acc[nt][i][k] = 0.0f;
+                for (int k = 0; k < 4; k++) st.acc[nt][i][k] = 0.0f;
         }
 
-        // ---- page loop -----------------------------------------------------
-        const int p_first = start / kBlockSize, p_last = (end - 1) / kBlockSize;
-        const int32_t* bt_row = P.bt + (int64_t)b * P.bt_stride;
-        int blk_reg = (p_first + lane <= p_last) ? __ldg(bt_row + p_first + lane) : 0;
-        // Block ids outside [0, num_blocks) mask their page and read block 0.
-        auto valid_blk = [&](int id) { return id >= 0 && (P.num_blocks == 0 || id < P.num_blocks); };
-        int blk = __shfl_sync(0xffffffffu, blk_reg, 0);
-        bool nxt_ok = valid_blk(blk);
-        PageRegs nxt;
-        load_page<LAYOUT>(nxt, P, nxt_ok ? blk : 0, kvh, g, c);
-
-        for (int p = p_first; p <= p_last; p++) {
-            const PageRegs cur = nxt;
-            const bool page_ok = nxt_ok;
-            if (p < p_last) {
-                const int rel = p + 1 - p_first;
-                if ((rel & 31) == 0)
-                    blk_reg = (p + 1 + lane <= p_last) ? __ldg(bt_row + p + 1 + lane) : 0;
-                blk = __shfl_sync(0xffffffffu, blk_reg, rel & 31);
-                nxt_ok = valid_blk(blk);
-                load_page<LAYOUT>(nxt, P, nxt_ok ? blk : 0, kvh, g, c);
+        // ---- page loop: two-page register ring, L2 prefetch one further ----
+        // Issues the loads of page pp into `r` and the L2 prefetch of pp + 1.
+        auto stage_page = [&](PageRegs& r, bool& ok, int pp) {
+            if (pp + 1 - w0 >= 32) {  // refill the block-id window
+                w0 = pp;
+                blk_reg = (pp + lane <= p_last) ? __ldg(bt_row + pp + lane) : 0;
             }
-            const int t0 = p * kBlockSize + 2 * g;  // tokens t0 (row g), t0+1 (row g+8)
-            const bool va = page_ok && t0 >= start && t0 < end;
-            const bool vb = page_ok && t0 + 1 >= start && t0 + 1 < end;
-
-            // -- Q.K on the tensor cores --
-            float dq[NT][4];
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                for (int k = 0; k < 4; k++) dq[nt][k] = 0.0f;
-            float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
-#pragma unroll
-            for (int ks = 0; ks < 8; ks++) {
-                const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
-                const int sh = 16 * (ks & 1);
-                const uint32_t ia = ((w0 >> sh) & 0xFFu) * (kLutCopies * kEntry);
-                const uint32_t ib = ((w0 >> (sh + 8)) & 0xFFu) * (kLutCopies * kEntry);
-                const uint32_t ic = ((w1 >> sh) & 0xFFu) * (kLutCopies * kEntry);
-                const uint32_t id = ((w1 >> (sh + 8)) & 0xFFu) * (kLutCopies * kEntry);
-                uint32_t e0x, e0y, e1x, e1y, e2x, e2y, e3x, e3y;
-                if (LAYOUT == TQB_LAYOUT_SOA) {
-                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e0x), "=r"(e0y) : "r"(lut_lane + ia));
-                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e1x), "=r"(e1y) : "r"(lut_lane + ic));
-                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e2x), "=r"(e2y) : "r"(lut_lane + ib));
-                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(e3x), "=r"(e3y) : "r"(lut_lane + id));
-                } else {
-                    uint32_t q0, q1, q2, q3;
-                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                                 : "=r"(e0x), "=r"(e0y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ia));
-                    csq0 += __uint_as_float(q0);
-                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                                 : "=r"(e1x), "=r"(e1y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ic));
-                    csq1 += __uint_as_float(q0);
-                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                                 : "=r"(e2x), "=r"(e2y), "=r"(q0), "=r"(q1) : "r"(lut_lane + ib));
-                    csq0 += __uint_as_float(q0);
-                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                                 : "=r"(e3x), "=r"(e3y), "=r"(q2), "=r"(q3) : "r"(lut_lane + id));
-                    csq1 += __uint_as_float(q2);
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    mma_16816(dq[nt], e0x, e1x, e2x, e3x, qf[nt][2 * ks], qf[nt][2 * ks + 1]);
-                    mma_16816(dq[nt], e0y, e1y, e2y, e3y, qf[nt][2 * ks], qf[nt][2 * ks + 1]);
-                }
+            const int id = blk_of(pp);
+            ok = valid_blk(id);
+            load_page<LAYOUT>(r, P.cache + (int64_t)(ok ? id : 0) * P.block_bytes, off);
+            if (pp + 1 <= p_last) {
+                const int nb = blk_of(pp + 1);
+                if (valid_blk(nb)) prefetch_l2(P.cache + (int64_t)nb * P.block_bytes + off.pf);
             }
-            float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
-            if (LAYOUT == TQB_LAYOUT_AOS) {
-                // Norm correction c / |c| (reference/aos_decode.py:199-206).
-                csq0 = warp_sum_xor(csq0, 1, 2);
-                csq1 = warp_sum_xor(csq1, 1, 2);
-                kn0 = kn0 / sqrtf(csq0 + 1e-16f);
-                kn1 = kn1 / sqrtf(csq1 + 1e-16f);
-            }
-            const float vs0 = va ? half_bits_to_float(cur.vs) : 0.0f;
-            const float vs1 = vb ? half_bits_to_float(cur.vs >> 16) : 0.0f;
-            const float vz0 = va ? half_bits_to_float(cur.vz) : 0.0f;
-            const float vz1 = vb ? half_bits_to_float(cur.vz >> 16) : 0.0f;
-
-            // -- online softmax (exp2 domain), exact rescale --
-            uint32_t bw0[NT], bw1[NT];
-            float alpha[NT];
-            bool rescale = false;
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                float s0 = (dq[nt][0] + dq[nt][1]) * kn0 * kfac[nt];
-                float s1 = (dq[nt][2] + dq[nt][3]) * kn1 * kfac[nt];
-                s0 = va ? s0 : -INFINITY;
-                s1 = vb ? s1 : -INFINITY;
-                const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
-                const float mnew = fmaxf(m_run[nt], tmax);
-                // A page with no valid token keeps the state (-inf - -inf guard).
-                const float mref = mnew == -INFINITY ? 0.0f : mnew;
-                alpha[nt] = ex2(m_run[nt] - mref);
-                rescale |= alpha[nt] != 1.0f;
-                const float p0 = ex2(s0 - mref), p1 = ex2(s1 - mref);
-                l_part[nt] = l_part[nt] * alpha[nt] + (p0 + p1);
-                z_part[nt] = z_part[nt] * alpha[nt] + (p0 * vz0 + p1 * vz1);
-                m_run[nt] = mnew;
-                const float w0 = p0 * vs0, w1 = p1 * vs1;
-                const __half2 wh = __floats2half2_rn(w0, w1);
-                const __half2 wl = __floats2half2_rn(w0 - __low2float(wh), w1 - __high2float(wh));
-                // Transpose W into the B fragment of P.V: lane (g, c) takes
-                // tokens {4c, 4c+1} from lane 8c + (g>>1) and {4c+2, 4c+3}
-                // from lane 8c + 4 + (g>>1), part g&1.
-                const int srcA = 8 * c + (g >> 1);
-                const uint32_t hA = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA);
-                const uint32_t lA = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA);
-                const uint32_t hB = __shfl_sync(0xffffffffu, h2_as_u32(wh), srcA + 4);
-                const uint32_t lB = __shfl_sync(0xffffffffu, h2_as_u32(wl), srcA + 4);
-                bw0[nt] = (g & 1) ? lA : hA;
-                bw1[nt] = (g & 1) ? lB : hB;
-            }
-            if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                    for (int i = 0; i < 8; i++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++) acc[nt][i][k] *= alpha[nt];
-            }
-
-            // -- P.V on the tensor cores --
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int wi = i >> 2, bi = i & 3;
-                const uint32_t sel = (uint32_t)(bi | (bi << 4) | ((4 + bi) << 8) | ((4 + bi) << 12));
-                const uint32_t x0 = wi ? cur.v[0].y : cur.v[0].x;
-                const uint32_t x1 = wi ? cur.v[1].y : cur.v[1].x;
-                const uint32_t x2 = wi ? cur.v[2].y : cur.v[2].x;
-                const uint32_t x3 = wi ? cur.v[3].y : cur.v[3].x;
-                const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
-                const uint32_t a0 = nib_to_h2(p01, 0x000F000Fu);
-                const uint32_t a1 = nib_to_h2(p01, 0x00F000F0u);
-                const uint32_t a2 = nib_to_h2(p23, 0x000F000Fu);
-                const uint32_t a3 = nib_to_h2(p23, 0x00F000F0u);
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) mma_16816(acc[nt][i], a0, a1, a2, a3, bw0[nt], bw1[nt]);
-            }
+        };
+        for (int p = p_first; p <= p_last; p += 2) {
+            if (p + 1 <= p_last) stage_page(rb, ok_b, p + 1);
+            process_page<NT, LAYOUT>(st, ra, ok_a, p * kBlockSize + 2 * g, start, end, lut_base,
+                                     lut_sel_src, g, c);
+            if (p + 1 > p_last) break;
+            if (p + 2 <= p_last) stage_page(ra, ok_a, p + 2);
+            process_page<NT, LAYOUT>(st, rb, ok_b, (p + 1) * kBlockSize + 2 * g, start, end, lut_base,
+                                     lut_sel_src, g, c);
         }
 
         // ---- epilogue: normalise, stage, coalesced write -------------------
+        constexpr float kLoScale = 16777216.0f;  // 2^24: undo the subnormal code scale
+        constexpr float kHiScale = 1048576.0f;   // 2^20 for high-nibble rows
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            float l = warp_sum_xor(l_part[nt], 4, 16);
+            float l = warp_sum_xor(st.l_part[nt], 4, 16);
             l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
-            const float z = warp_sum_xor(z_part[nt], 4, 16);
+            const float z = warp_sum_xor(st.z_part[nt], 4, 16);
+            const float inv = __frcp_rn(l);
             const int hl = c + 4 * nt;
-            float* row = stage + (c + 4 * nt) * (kHeadDim + 1);
+            float* row = stage + hl * (kHeadDim + 1);
             if (hl < P.G) {
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const float lo = acc[nt][i][0] + acc[nt][i][1] + z;
-                    const float hi = (acc[nt][i][2] + acc[nt][i][3]) * 0.0625f + z;
-                    row[16 * g + 2 * i] = __fdiv_rn(lo, l);
-                    row[16 * g + 2 * i + 1] = __fdiv_rn(hi, l);
+                    const float lo = (st.acc[nt][i][0] + st.acc[nt][i][1]) * kLoScale + z;
+                    const float hi = (st.acc[nt][i][2] + st.acc[nt][i][3]) * kHiScale + z;
+                    row[16 * g + 2 * i] = lo * inv;
+                    row[16 * g + 2 * i + 1] = hi * inv;
                 }
-                if (g == 0) row[kHeadDim] = m_run[nt] * ln2 + logf(l);
+                if (g == 0) row[kHeadDim] = st.m_run[nt] * kLn2 + logf(l);
             }
         }
         __syncwarp();
@@ -415,15 +500,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
 template <int NT, int LAYOUT>
 int launch_t(const Stage1Params& P, cudaStream_t stream, int num_sms) {
-    constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
-    const size_t smem = 256 * kLutCopies * kEntry + (size_t)kWarps * NT * 4 * (kHeadDim + 1) * sizeof(float);
+    const size_t smem = kLutBytes + (size_t)kWarps * NT * 4 * (kHeadDim + 1) * sizeof(float);
     auto kern = stage1_kernel<NT, LAYOUT>;
     static thread_local int configured_dev = -1;  // per template instance
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return TQB_ERR_CUDA;
+            return report_launch(cudaGetLastError());
         configured_dev = dev;
     }
     int per_sm = 0;
