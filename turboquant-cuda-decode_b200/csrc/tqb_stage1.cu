@@ -19,24 +19,26 @@
 //    streaming loads into a two-page register ring, and asks L2 for the page
 //    after that (prefetch.global.L2), so DRAM latency is covered without
 //    spending registers on a deeper ring.
-//  * Q.K runs on the tensor cores as D[token, n] = K[token, :] . Qpack[:, n]
-//    (mma.m16n8k16, tokens as M).  The 8 N columns are 4 query heads x
-//    {Q_hi, Q_lo} (fp16 split of the power-of-two scaled fp32 query), and K
-//    is fed twice, as C_hi and C_lo (fp16 split of the scaled centroid).  The
-//    four partial products sum to the fp32-accurate dot product (the single
-//    fp16 MMA of the reference's V2 kernel does not meet 1e-4).  A byte of
-//    packed K (two 4-bit codes) maps to {C_hi pair, C_lo pair} through a
-//    256-entry table with one copy per lane in shared memory (bank-conflict
-//    free); one PRMT forms the table offset from the byte and the lane.
+//  * Q.K runs on the tensor cores as D[row, n] = K[row, :] . Qpack[:, n]
+//    (mma.m16n8k16).  The 8 N columns are 4 query heads x {Q_hi, Q_lo}
+//    (fp16 split of the power-of-two scaled fp32 query); the 16 M rows are 8
+//    tokens x {C_hi, C_lo} (fp16 split of the scaled centroid).  The four
+//    partial products add up, per lane, to the fp32-accurate dot product
+//    (the single fp16 MMA of the reference's V2 kernel does not meet 1e-4).
+//    A byte of packed K (two 4-bit codes) maps to {C_hi pair, C_lo pair}
+//    through a 256-entry table with one copy per lane in shared memory
+//    (bank-conflict free); one PRMT forms the table offset from the byte and
+//    the lane, and each table load is exactly half of an A fragment.
 //  * Softmax runs in the exp2 domain on the MMA accumulators; each lane owns
 //    one query head and two tokens of the page, so the row max is three
 //    shuffles.
 //  * P.V runs on the tensor cores as D[dim, n] = Vq[dim, token] . W[token, n]
 //    with dims as M.  The raw 4-bit codes are used as fp16 subnormals
-//    (code * 2^-24, or code * 2^-20 for the high nibble) with one AND, so the
-//    operand is exact and costs no conversion; W = p * vscale is split into
-//    fp16 hi/lo across the N columns, so the product is fp32-accurate; the
-//    vzero term sum_t p_t * vzero_t is added per head in fp32.
+//    (code * 2^-20, mantissa bits 4-7) with one AND (plus a shift for the
+//    low nibble), so the operand is exact and costs no conversion;
+//    W = p * vscale is split into fp16 hi/lo across the N columns, so the
+//    product is fp32-accurate; the vzero term sum_t p_t * vzero_t is added
+//    per head in fp32.
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -188,7 +190,7 @@ struct ItemState {
     uint32_t qf[NT][16];  // Q.K B fragments
     float kfac[NT];       // score factor of this lane's head
     float m_run[NT], l_part[NT], z_part[NT];
-    float acc[NT][8][4];  // P.V accumulators (rows scaled by 2^-24 / 2^-20)
+    float acc[NT][8][4];  // P.V accumulators (codes scaled by 2^-20)
 };
 
 // One 16-token page of one work item.
@@ -200,41 +202,50 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
 
     // -- Q.K on the tensor cores --
-    float dq[NT][4];
+    // Two M tiles per page: tile 0 = tokens 2g (even), tile 1 = tokens 2g+1.
+    // Inside a tile, row g carries the C_hi part of the token and row g+8 its
+    // C_lo part, so one LUT load ({C_hi pair, C_lo pair} of a byte) is
+    // exactly half of an A fragment and the two parts add up per lane
+    // afterwards.  The two tiles are independent accumulator chains.
+    float dq[NT][2][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int k = 0; k < 4; k++) dq[nt][k] = 0.0f;
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
     float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // (byte << 8) | this lane's copy offset, in one PRMT
-        const uint32_t ia = prmt(w0, lut_sel_src, 0x5504u | (jA << 4));
-        const uint32_t ic = prmt(w1, lut_sel_src, 0x5504u | (jA << 4));
-        const uint32_t ib = prmt(w0, lut_sel_src, 0x5504u | (jB << 4));
+        const uint32_t ia = prmt(w0, lut_sel_src, 0x5504u | (jA << 4));  // token 2g, dims k-lo
+        const uint32_t ib = prmt(w0, lut_sel_src, 0x5504u | (jB << 4));  // token 2g, dims k-hi
+        const uint32_t ic = prmt(w1, lut_sel_src, 0x5504u | (jA << 4));  // token 2g+1
         const uint32_t id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
         uint2 e0, e1, e2, e3;
         if (LAYOUT == TQB_LAYOUT_SOA) {
             e0 = lds_v2(lut_base + ia);
-            e1 = lds_v2(lut_base + ic);
-            e2 = lds_v2(lut_base + ib);
+            e1 = lds_v2(lut_base + ib);
+            e2 = lds_v2(lut_base + ic);
             e3 = lds_v2(lut_base + id);
         } else {
-            const uint4 f0 = lds_v4(lut_base + ia), f1 = lds_v4(lut_base + ic);
-            const uint4 f2 = lds_v4(lut_base + ib), f3 = lds_v4(lut_base + id);
+            const uint4 f0 = lds_v4(lut_base + ia), f1 = lds_v4(lut_base + ib);
+            const uint4 f2 = lds_v4(lut_base + ic), f3 = lds_v4(lut_base + id);
             e0 = make_uint2(f0.x, f0.y);
             e1 = make_uint2(f1.x, f1.y);
             e2 = make_uint2(f2.x, f2.y);
             e3 = make_uint2(f3.x, f3.y);
-            csq0 += __uint_as_float(f0.z) + __uint_as_float(f2.z);
-            csq1 += __uint_as_float(f1.z) + __uint_as_float(f3.z);
+            csq0 += __uint_as_float(f0.z) + __uint_as_float(f1.z);
+            csq1 += __uint_as_float(f2.z) + __uint_as_float(f3.z);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            mma_16816(dq[nt], e0.x, e1.x, e2.x, e3.x, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
-            mma_16816(dq[nt], e0.y, e1.y, e2.y, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+            // A = {C_hi kA, C_lo kA, C_hi kB, C_lo kB}; B = Q columns of dims
+            // 32c + 4ks + {0,1 | 2,3}
+            mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+            mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
     }
     float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
@@ -256,8 +267,10 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
     bool rescale = false;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        float s0 = (dq[nt][0] + dq[nt][1]) * kn0 * st.kfac[nt];
-        float s1 = (dq[nt][2] + dq[nt][3]) * kn1 * st.kfac[nt];
+        // columns 2c / 2c+1: Q_hi / Q_lo parts of head c; rows g / g+8:
+        // C_hi / C_lo parts of the token
+        float s0 = ((dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3])) * kn0 * st.kfac[nt];
+        float s1 = ((dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3])) * kn1 * st.kfac[nt];
         s0 = va ? s0 : -INFINITY;
         s1 = vb ? s1 : -INFINITY;
         const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
@@ -305,9 +318,12 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         const uint32_t x2 = wi ? cur.v[2].y : cur.v[2].x;
         const uint32_t x3 = wi ? cur.v[3].y : cur.v[3].x;
         const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
-        const uint32_t a0 = p01 & 0x000F000Fu;  // row g:   code * 2^-24
-        const uint32_t a1 = p01 & 0x00F000F0u;  // row g+8: code * 2^-20
-        const uint32_t a2 = p23 & 0x000F000Fu;
+        // Both nibbles enter as code * 2^-20 (mantissa bits 4-7): the
+        // tensor cores keep these subnormals exact, while codes at 2^-24
+        // lose bits.
+        const uint32_t a0 = (p01 << 4) & 0x00F000F0u;  // row g:   low nibble
+        const uint32_t a1 = p01 & 0x00F000F0u;         // row g+8: high nibble
+        const uint32_t a2 = (p23 << 4) & 0x00F000F0u;
         const uint32_t a3 = p23 & 0x00F000F0u;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) mma_16816(st.acc[nt][i], a0, a1, a2, a3, bw0[nt], bw1[nt]);
@@ -374,13 +390,19 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
         const int p_first = start / kBlockSize, p_last = (end - 1) / kBlockSize;
         const int32_t* bt_row = P.bt + (int64_t)b * P.bt_stride;
-        // Block ids of pages [w0, w0 + 32), one per lane.
+        const LaneOffsets off = lane_offsets<LAYOUT>(P, kvh, lane);
+        const uint8_t* cache = P.cache;
+        const uint32_t block_bytes = (uint32_t)P.block_bytes;
+        const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
+        // Block ids of pages [w0, w0 + 32), one per lane; an id outside
+        // [0, num_blocks) masks its page, whose loads then read block 0.
         int w0 = p_first;
         int blk_reg = (p_first + lane <= p_last) ? __ldg(bt_row + p_first + lane) : 0;
-        const LaneOffsets off = lane_offsets<LAYOUT>(P, kvh, lane);
-        auto valid_blk = [&](int id) { return id >= 0 && (P.num_blocks == 0 || id < P.num_blocks); };
-        // Block id of page pp (pp in [w0, w0 + 32)).
+        auto valid_blk = [&](int id) { return (uint32_t)id < nblocks; };
         auto blk_of = [&](int pp) { return __shfl_sync(0xffffffffu, blk_reg, pp - w0); };
+        auto block_ptr = [&](int id) {
+            return cache + (uint64_t)(valid_blk(id) ? (uint32_t)id : 0u) * block_bytes;
+        };
 
         // Start the first page's loads before the query prologue.
         PageRegs ra, rb;
@@ -388,11 +410,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         {
             const int id = blk_of(p_first);
             ok_a = valid_blk(id);
-            load_page<LAYOUT>(ra, P.cache + (int64_t)(ok_a ? id : 0) * P.block_bytes, off);
-            if (p_first + 1 <= p_last) {
-                const int nb = blk_of(p_first + 1);
-                if (valid_blk(nb)) prefetch_l2(P.cache + (int64_t)nb * P.block_bytes + off.pf);
-            }
+            load_page<LAYOUT>(ra, block_ptr(id), off);
+            prefetch_l2(block_ptr(blk_of(min(p_first + 1, p_last))) + off.pf);
         }
 
         // ---- query fragments (B operand of Q.K) --------------------------
@@ -443,17 +462,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         // ---- page loop: two-page register ring, L2 prefetch one further ----
         // Issues the loads of page pp into `r` and the L2 prefetch of pp + 1.
         auto stage_page = [&](PageRegs& r, bool& ok, int pp) {
-            if (pp + 1 - w0 >= 32) {  // refill the block-id window
+            if (pp + 1 - w0 >= 32) {  // refill the block-id window (warp-uniform)
                 w0 = pp;
                 blk_reg = (pp + lane <= p_last) ? __ldg(bt_row + pp + lane) : 0;
             }
             const int id = blk_of(pp);
             ok = valid_blk(id);
-            load_page<LAYOUT>(r, P.cache + (int64_t)(ok ? id : 0) * P.block_bytes, off);
-            if (pp + 1 <= p_last) {
-                const int nb = blk_of(pp + 1);
-                if (valid_blk(nb)) prefetch_l2(P.cache + (int64_t)nb * P.block_bytes + off.pf);
-            }
+            load_page<LAYOUT>(r, block_ptr(id), off);
+            prefetch_l2(block_ptr(blk_of(min(pp + 1, p_last))) + off.pf);
         };
         for (int p = p_first; p <= p_last; p += 2) {
             if (p + 1 <= p_last) stage_page(rb, ok_b, p + 1);
@@ -466,8 +482,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         }
 
         // ---- epilogue: normalise, stage, coalesced write -------------------
-        constexpr float kLoScale = 16777216.0f;  // 2^24: undo the subnormal code scale
-        constexpr float kHiScale = 1048576.0f;   // 2^20 for high-nibble rows
+        constexpr float kCodeScale = 1048576.0f;  // 2^20: undo the subnormal code scale
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             float l = warp_sum_xor(st.l_part[nt], 4, 16);
@@ -479,8 +494,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
             if (hl < P.G) {
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const float lo = (st.acc[nt][i][0] + st.acc[nt][i][1]) * kLoScale + z;
-                    const float hi = (st.acc[nt][i][2] + st.acc[nt][i][3]) * kHiScale + z;
+                    const float lo = (st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale + z;
+                    const float hi = (st.acc[nt][i][2] + st.acc[nt][i][3]) * kCodeScale + z;
                     row[16 * g + 2 * i] = lo * inv;
                     row[16 * g + 2 * i + 1] = hi * inv;
                 }
