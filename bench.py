@@ -258,7 +258,7 @@ def ncu_traffic(config: str, layout: str):
 # ---------------------------------------------------------------------------
 
 
-def cpu_baseline(w, min_seconds=3.0):
+def cpu_baseline(w, min_seconds=10.0):
     from oracle import oracle as O
 
     cores = O.default_threads()

@@ -161,6 +161,10 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
     p.S = a->num_splits;
     p.attn_scale = a->attn_scale > 0.0f ? a->attn_scale : 1.0f / sqrtf((float)tqb::kHeadDim);
     p.num_items = (int64_t)a->batch * a->num_splits * a->num_kv_heads;
+    TQB_REQUIRE(p.num_items < (int64_t(1) << 31), TQB_ERR_UNSUPPORTED,
+                "batch * num_splits * num_kv_heads must be < 2^31");
+    p.div_hk = tqb::FastDiv((uint32_t)a->num_kv_heads);
+    p.div_s = tqb::FastDiv((uint32_t)a->num_splits);
     const int rc = tqb::launch_stage1(p, stream, nsm);
     if (rc != TQB_OK) return rc;
     return TQB_OK;

@@ -9,6 +9,23 @@
 
 namespace tqb {
 
+// Division of 32-bit unsigned n < 2^31 by a fixed divisor d >= 1 with a
+// multiply-high and a shift (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", 1994): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l.
+struct FastDiv {
+    uint32_t d, m, l;
+    FastDiv() : d(1), m(0), l(0) {}
+    explicit FastDiv(uint32_t div) : d(div) {
+        l = 0;
+        while ((1ull << l) < div) l++;
+        m = (uint32_t)((((1ull << l) - div) << 32) / div + 1);
+    }
+#ifdef __CUDACC__
+    __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+#endif
+};
+
 struct Stage1Params {
     const float* q;
     int64_t qsb, qsh;
@@ -26,7 +43,8 @@ struct Stage1Params {
     int64_t msb, msh, mss;
     int B, Hq, Hk, G, S;
     float attn_scale;
-    int64_t num_items;  // B * S * Hk work items, KV head fastest
+    int64_t num_items;  // B * S * Hk work items, KV head fastest (< 2^31)
+    FastDiv div_hk, div_s;
 };
 
 struct Stage2Params {

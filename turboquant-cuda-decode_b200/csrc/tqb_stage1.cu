@@ -16,11 +16,15 @@
 //    interleaved 128-byte head slices of the same 16-token pages, so each
 //    17 KB page streams from HBM as one contiguous run.
 //  * The warp walks the split one 16-token page at a time with 128/64/32-bit
-//    streaming loads into a two-page register ring, and asks L2 for the page
-//    after that (prefetch.global.L2), so DRAM latency is covered without
-//    spending registers on a deeper ring.
+//    streaming loads into a two-page register ring.  One lane per CTA asks
+//    L2 for whole blocks kPrefetchPages ahead (cp.async.bulk.prefetch.L2,
+//    one request per 17 KB block), so DRAM latency is covered without
+//    spending registers on a deeper ring; the first pages of a warp's next
+//    item are requested while it finishes the current one.
 //  * Q.K runs on the tensor cores as D[row, n] = K[row, :] . Qpack[:, n]
-//    (mma.m16n8k16).  The 8 N columns are 4 query heads x {Q_hi, Q_lo}
+//    (mma.m16n8k16; the contraction is 8 columns wide per token, so the
+//    register-operand MMA is used rather than tcgen05, whose smem operands
+//    would have to hold the dequantised K).  The 8 N columns are 4 query heads x {Q_hi, Q_lo}
 //    (fp16 split of the power-of-two scaled fp32 query); the 16 M rows are 8
 //    tokens x {C_hi, C_lo} (fp16 split of the scaled centroid).  The four
 //    partial products add up, per lane, to the fp32-accurate dot product
@@ -51,7 +55,11 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kLutStride = 256;              // bytes per table entry (all copies)
+constexpr float kLazy = 8.0f;                // lazy-rescale slack (log2 units)
+constexpr float kWMax = 32768.0f;            // largest W kept on the lazy path
 constexpr int kLutBytes = 256 * kLutStride;  // 64 KB
+constexpr int kPrefetchPages = 3;            // L2 prefetch distance in pages
+constexpr int kMinBlocksNT1 = 2;             // CTAs per SM for one n-tile
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -83,13 +91,10 @@ __device__ __forceinline__ uint32_t ld_stream_u16(const uint8_t* p) {
     asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
     return r;
 }
-__device__ __forceinline__ void prefetch_l2(const uint8_t* p) {
-    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
-}
-__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
-    uint2 r;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(addr));
-    return r;
+// L2 prefetch of `bytes` (multiple of 16) from a 16-byte aligned address,
+// one bulk request.
+__device__ __forceinline__ void prefetch_l2_bulk(const uint8_t* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
     uint4 r;
@@ -112,7 +117,6 @@ struct LaneOffsets {
     uint32_t k0;    // K bytes of token 2g (token 2g+1: + row)
     uint32_t v0;    // V bytes of token 4c (token 4c+j: + j * row)
     uint32_t meta;  // SoA: knorm pair; AoS: slot metadata of token 2g
-    uint32_t pf;    // L2 prefetch target of this lane
     uint32_t row;   // bytes between consecutive tokens of a page
 };
 
@@ -127,21 +131,20 @@ __device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int k
         o.k0 = (2 * g) * tok + head + 16 * c;
         o.v0 = (4 * c) * tok + head + kKBytes + 8 * g;
         o.meta = kBlockSize * tok + (uint32_t)kvh * (3 * kBlockSize * 2) + 4 * g;
-        // lanes 0-15: first byte of token row `lane`; lanes 16-30: last byte
-        // of a row (a row may straddle two lines); lane 31: the metadata
-        // strip of the head (96 bytes from a 32-byte boundary).
-        const uint32_t r = (uint32_t)(lane & 15) * tok + head;
-        o.pf = lane < 16 ? r : (lane == 31 ? kBlockSize * tok + (uint32_t)kvh * 96 : r + kDataBytes - 1);
     } else {
         const uint32_t pos = (uint32_t)P.pos_stride, hs = (uint32_t)P.head_stride * kvh;
         o.row = pos;
         o.k0 = (2 * g) * pos + hs + 16 * c;
         o.v0 = (4 * c) * pos + hs + kKBytes + 2 + 8 * g;
         o.meta = (2 * g) * pos + hs + kKBytes;
-        const uint32_t r = (uint32_t)(lane & 15) * pos + hs;
-        o.pf = lane < 16 ? r : r + kSlotBytes - 1;
     }
     return o;
+}
+
+// Whole physical block into L2 with one bulk request (lane 0 of the warp
+// that serves KV head 0, whose block holds every head of the page).
+__device__ __forceinline__ void prefetch_block(const uint8_t* block, uint32_t bytes, bool leader) {
+    if (leader) prefetch_l2_bulk(block, bytes);
 }
 
 // AoS slots are only 2-byte aligned: gather with 16-bit loads.
@@ -193,18 +196,23 @@ struct ItemState {
     float acc[NT][8][4];  // P.V accumulators (codes scaled by 2^-20)
 };
 
+// Table entry load at byte offset `off` from the table start.
+__device__ __forceinline__ uint2 lut_v2(const uint8_t* lut, uint32_t off) {
+    return *reinterpret_cast<const uint2*>(lut + off);
+}
+
 // One 16-token page of one work item.
 template <int NT, int LAYOUT>
 __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& cur, bool page_ok,
-                                             int tok0, int start, int end, uint32_t lut_base,
-                                             uint32_t lut_sel_src, int g, int c) {
+                                             int tok0, int start, int end, const uint8_t* lut,
+                                             uint32_t lut_base, uint32_t lut_sel_src, int g, int c) {
     const bool va = page_ok && tok0 >= start && tok0 < end;
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
 
     // -- Q.K on the tensor cores --
     // Two M tiles per page: tile 0 = tokens 2g (even), tile 1 = tokens 2g+1.
     // Inside a tile, row g carries the C_hi part of the token and row g+8 its
-    // C_lo part, so one LUT load ({C_hi pair, C_lo pair} of a byte) is
+    // C_lo part, so one table load ({C_hi pair, C_lo pair} of a byte) is
     // exactly half of an A fragment and the two parts add up per lane
     // afterwards.  The two tiles are independent accumulator chains.
     float dq[NT][2][4];
@@ -226,10 +234,10 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         const uint32_t id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
         uint2 e0, e1, e2, e3;
         if (LAYOUT == TQB_LAYOUT_SOA) {
-            e0 = lds_v2(lut_base + ia);
-            e1 = lds_v2(lut_base + ib);
-            e2 = lds_v2(lut_base + ic);
-            e3 = lds_v2(lut_base + id);
+            e0 = lut_v2(lut, ia);
+            e1 = lut_v2(lut, ib);
+            e2 = lut_v2(lut, ic);
+            e3 = lut_v2(lut, id);
         } else {
             const uint4 f0 = lds_v4(lut_base + ia), f1 = lds_v4(lut_base + ib);
             const uint4 f2 = lds_v4(lut_base + ic), f3 = lds_v4(lut_base + id);
@@ -269,23 +277,35 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
     for (int nt = 0; nt < NT; nt++) {
         // columns 2c / 2c+1: Q_hi / Q_lo parts of head c; rows g / g+8:
         // C_hi / C_lo parts of the token
-        float s0 = ((dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3])) * kn0 * st.kfac[nt];
-        float s1 = ((dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3])) * kn1 * st.kfac[nt];
+        const float d0 = (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
+        const float d1 = (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
+        float s0 = d0 * kn0 * st.kfac[nt];
+        float s1 = d1 * kn1 * st.kfac[nt];
         s0 = va ? s0 : -INFINITY;
         s1 = vb ? s1 : -INFINITY;
         const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
         const float mold = st.m_run[nt];
-        const float mnew = fmaxf(mold, tmax);
-        // A page with no valid token keeps the state (-inf - -inf guard).
-        const float mref = mnew == -INFINITY ? 0.0f : mnew;
-        alpha[nt] = ex2(mold - mref);
-        // The first page of an item has nothing to rescale.
-        rescale |= (alpha[nt] != 1.0f) && (mold != -INFINITY);
-        const float p0 = ex2(s0 - mref), p1 = ex2(s1 - mref);
+        // Lazy reference max: it only moves when a score exceeds it by more
+        // than kLazy (log2 units), so most pages need no rescale; p <= 2^kLazy.
+        float mref = tmax > mold + kLazy ? tmax : mold;
+        float mref_e = mref == -INFINITY ? 0.0f : mref;  // page with no valid token
+        float p0 = ex2(s0 - mref_e), p1 = ex2(s1 - mref_e);
+        float w0 = p0 * vs0, w1 = p1 * vs1;
+        // W must stay inside fp16: a huge V scale falls back to the exact max.
+        if (__any_sync(0xffffffffu, fmaxf(w0, w1) > kWMax)) {
+            mref = fmaxf(mold, tmax);
+            mref_e = mref == -INFINITY ? 0.0f : mref;
+            p0 = ex2(s0 - mref_e);
+            p1 = ex2(s1 - mref_e);
+            w0 = p0 * vs0;
+            w1 = p1 * vs1;
+        }
+        // The first page has nothing to rescale (accumulators are 0).
+        alpha[nt] = (mold == -INFINITY || mref == mold) ? 1.0f : ex2(mold - mref);
+        rescale |= alpha[nt] != 1.0f;
         st.l_part[nt] = st.l_part[nt] * alpha[nt] + (p0 + p1);
         st.z_part[nt] = st.z_part[nt] * alpha[nt] + (p0 * vz0 + p1 * vz1);
-        st.m_run[nt] = mnew;
-        const float w0 = p0 * vs0, w1 = p1 * vs1;
+        st.m_run[nt] = mref;
         const __half2 wh = __floats2half2_rn(w0, w1);
         const __half2 wl = __floats2half2_rn(w0 - __low2float(wh), w1 - __high2float(wh));
         // Transpose W into the B fragment of P.V: lane (g, c) takes tokens
@@ -331,7 +351,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
 }
 
 template <int NT, int LAYOUT>
-__global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     stage1_kernel(const Stage1Params P) {
     // Shared memory: the K table (256 entries x 256 bytes: SoA keeps 32 lane
     // copies of {C_hi pair, C_lo pair}; AoS keeps 16 copies that also carry
@@ -373,27 +393,59 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     const uint32_t lut_sel_src = (uint32_t)(lane % kCopies) * kEntry;
     float* stage = stage_all + warp * (NT * 4 * (kHeadDim + 1));
 
-    for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < P.num_items;
-         item += (int64_t)gridDim.x * kWarps) {
-        const int kvh = (int)(item % P.Hk);
-        const int64_t rest = item / P.Hk;
-        const int s = (int)(rest % P.S);
-        const int b = (int)(rest / P.S);
-        const int nsp = P.nsplits ? min(__ldg(P.nsplits + b), P.S) : P.S;
-        if (s >= nsp) continue;
+    // Work item -> (b, s, kvh) and its token range; false for an empty split.
+    struct ItemRange { int b, s, kvh, start, end; };
+    auto decode_item = [&](uint32_t item, ItemRange& r) {
+        const uint32_t rest = P.div_hk.div(item);
+        r.kvh = (int)(item - rest * (uint32_t)P.Hk);
+        const uint32_t bq = P.div_s.div(rest);
+        r.s = (int)(rest - bq * (uint32_t)P.S);
+        r.b = (int)bq;
+        const int nsp = P.nsplits ? min(__ldg(P.nsplits + r.b), P.S) : P.S;
+        if (r.s >= nsp) return false;
         // Tokens past the block-table row are outside the sequence's pages.
-        const int L = min(__ldg(P.seq_lens + b), P.max_blocks * kBlockSize);
+        const int L = min(__ldg(P.seq_lens + r.b), P.max_blocks * kBlockSize);
         const int split_len = (L + nsp - 1) / nsp;
-        const int start = split_len * s;
-        const int end = min(start + split_len, L);
-        if (start >= end) continue;  // empty split: left unwritten
+        r.start = split_len * r.s;
+        r.end = min(r.start + split_len, L);
+        return r.start < r.end;
+    };
+    const uint32_t nblocks_all = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
+    const uint32_t item_stride = gridDim.x * kWarps;
+
+    for (uint32_t item = blockIdx.x * kWarps + warp; item < (uint32_t)P.num_items; item += item_stride) {
+        ItemRange ir;
+        if (!decode_item(item, ir)) continue;  // empty split: left unwritten
+        const int b = ir.b, s = ir.s, kvh = ir.kvh, start = ir.start, end = ir.end;
+        // Ask L2 for the first two pages of this warp's next item now, so
+        // the item boundary does not stall on DRAM.
+        {
+            ItemRange nx;
+            const uint32_t nitem = item + item_stride;
+            if (nitem < (uint32_t)P.num_items && decode_item(nitem, nx)) {
+                const int np0 = nx.start / kBlockSize, np1 = min(np0 + 1, (nx.end - 1) / kBlockSize);
+                const int32_t* nrow = P.bt + (int64_t)nx.b * P.bt_stride;
+                const int id0 = __ldg(nrow + np0), id1 = __ldg(nrow + np1);
+                const uint32_t bb = (uint32_t)P.block_bytes;
+                const bool nlead = lane == 0 && nx.kvh == 0 &&
+                                   ((reinterpret_cast<uintptr_t>(P.cache) | bb) & 15) == 0;
+                if ((uint32_t)id0 < nblocks_all) prefetch_block(P.cache + (uint64_t)(uint32_t)id0 * bb, bb, nlead);
+                if ((uint32_t)id1 < nblocks_all && np1 != np0)
+                    prefetch_block(P.cache + (uint64_t)(uint32_t)id1 * bb, bb, nlead);
+            }
+        }
 
         const int p_first = start / kBlockSize, p_last = (end - 1) / kBlockSize;
         const int32_t* bt_row = P.bt + (int64_t)b * P.bt_stride;
         const LaneOffsets off = lane_offsets<LAYOUT>(P, kvh, lane);
         const uint8_t* cache = P.cache;
         const uint32_t block_bytes = (uint32_t)P.block_bytes;
-        const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
+        const uint32_t nblocks = nblocks_all;
+        // One lane per page prefetches whole blocks: lane 0 of the warp of KV
+        // head 0 (the warps of a CTA share the (b, s) of their items).  The
+        // bulk form needs a 16-byte aligned block.
+        const bool pf_leader = lane == 0 && kvh == 0 &&
+                               ((reinterpret_cast<uintptr_t>(cache) | block_bytes) & 15) == 0;
         // Block ids of pages [w0, w0 + 32), one per lane; an id outside
         // [0, num_blocks) masks its page, whose loads then read block 0.
         int w0 = p_first;
@@ -411,7 +463,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
             const int id = blk_of(p_first);
             ok_a = valid_blk(id);
             load_page<LAYOUT>(ra, block_ptr(id), off);
-            prefetch_l2(block_ptr(blk_of(min(p_first + 1, p_last))) + off.pf);
+#pragma unroll
+            for (int d = 1; d <= kPrefetchPages; d++)
+                if (p_first + d <= p_last) prefetch_block(block_ptr(blk_of(p_first + d)), block_bytes, pf_leader);
         }
 
         // ---- query fragments (B operand of Q.K) --------------------------
@@ -459,25 +513,27 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
                 for (int k = 0; k < 4; k++) st.acc[nt][i][k] = 0.0f;
         }
 
-        // ---- page loop: two-page register ring, L2 prefetch one further ----
-        // Issues the loads of page pp into `r` and the L2 prefetch of pp + 1.
+        // ---- page loop: two-page register ring, L2 prefetch further on ----
+        // Issues the loads of page pp into `r` and the L2 prefetch of page
+        // pp + kPrefetchPages.
         auto stage_page = [&](PageRegs& r, bool& ok, int pp) {
-            if (pp + 1 - w0 >= 32) {  // refill the block-id window (warp-uniform)
+            if (pp + kPrefetchPages - w0 >= 32) {  // refill the block-id window
                 w0 = pp;
                 blk_reg = (pp + lane <= p_last) ? __ldg(bt_row + pp + lane) : 0;
             }
             const int id = blk_of(pp);
             ok = valid_blk(id);
             load_page<LAYOUT>(r, block_ptr(id), off);
-            prefetch_l2(block_ptr(blk_of(min(pp + 1, p_last))) + off.pf);
+            if (pp + kPrefetchPages <= p_last)
+                prefetch_block(block_ptr(blk_of(pp + kPrefetchPages)), block_bytes, pf_leader);
         };
         for (int p = p_first; p <= p_last; p += 2) {
             if (p + 1 <= p_last) stage_page(rb, ok_b, p + 1);
-            process_page<NT, LAYOUT>(st, ra, ok_a, p * kBlockSize + 2 * g, start, end, lut_base,
+            process_page<NT, LAYOUT>(st, ra, ok_a, p * kBlockSize + 2 * g, start, end, smem, lut_base,
                                      lut_sel_src, g, c);
             if (p + 1 > p_last) break;
             if (p + 2 <= p_last) stage_page(ra, ok_a, p + 2);
-            process_page<NT, LAYOUT>(st, rb, ok_b, (p + 1) * kBlockSize + 2 * g, start, end, lut_base,
+            process_page<NT, LAYOUT>(st, rb, ok_b, (p + 1) * kBlockSize + 2 * g, start, end, smem, lut_base,
                                      lut_sel_src, g, c);
         }
 
