@@ -166,6 +166,14 @@ const char* tqb_strerror(int status);
 const char* tqb_last_error_detail(void);
 int tqb_version(void);
 
+/* Diagnostics (no reference counterpart).  The SoA Stage1 kernel paces its
+ * TMA page ring with mbarrier waits that give up after about a second; each
+ * wait that gives up adds one to a per-device counter (the kernel then ends
+ * early and its mid_o is not valid).  Copies the counter of the current
+ * device into *count and clears it when `reset` is non-zero.  Synchronous:
+ * waits for the device's outstanding work. */
+int tqb_wait_timeouts(unsigned int* count, int reset);
+
 #ifdef __cplusplus
 }
 #endif

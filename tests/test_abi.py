@@ -8,6 +8,7 @@ exact layout of the C structs (compiled with gcc against the header).
 from __future__ import annotations
 
 import ctypes
+import os
 import re
 import subprocess
 import tempfile
@@ -15,7 +16,7 @@ from pathlib import Path
 
 import pytest
 
-from conftest import ROOT
+from conftest import PKG, ROOT
 from tqb import _build, _lib
 
 HEADER = ROOT / "include" / "tqb.h"
@@ -115,3 +116,23 @@ def test_ctypes_structs_match_c_layout(tmp_path: Path):
         assert int(got[cname]) == ctypes.sizeof(py), cname
         for f, _ in py._fields_:
             assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"
+
+
+def test_missing_library_raises_promptly(tmp_path: Path):
+    """A library path that does not exist gives TqbError at once (the error
+    text must not need the library it reports as missing)."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from tqb import _lib\n"
+            "try:\n    _lib.load()\nexcept _lib.TqbError as e:\n    print('raised', e.status, e)\n") % str(PKG)
+    env = dict(os.environ, TQB_LIBRARY=str(tmp_path / "absent.so"))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    assert "raised -5" in out.stdout and "absent.so" in out.stdout
+
+
+def test_status_text_matches_library(lib):
+    for status, text in _lib.STATUS_TEXT.items():
+        assert lib.tqb_strerror(status).decode() == text

@@ -4,11 +4,17 @@ Bar: |got - ref| <= 1e-4 + 2e-3 |ref| on every written O and LSE element
 (conftest.ATOL/RTOL), against (a) the reference's own SoA/AoS V1 outputs
 stored in the golden fixtures and (b) the CPU oracle on fresh seeded inputs.
 Empty splits must stay unwritten, exactly as in the reference.
+
+Every test runs twice: with the SoA cache served by the TMA page-ring kernel
+(the default) and by the register-ring kernel (TQB_STAGE1_KERNEL=regs); the
+AoS cache always uses the register-ring kernel.  After each run the device's
+count of bounded waits that gave up must be zero.
 """
 
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -22,6 +28,20 @@ from tqb import layout as L
 pytestmark = pytest.mark.gpu
 
 SENTINEL = -12345.0
+
+
+@pytest.fixture(autouse=True, params=["ring", "regs"])
+def stage1_kernel(request, cuda_device):
+    old = os.environ.get("TQB_STAGE1_KERNEL")
+    os.environ["TQB_STAGE1_KERNEL"] = request.param
+    tqb.wait_timeouts(reset=True)
+    yield request.param
+    torch.cuda.synchronize()
+    assert tqb.wait_timeouts(reset=True) == 0, "a bounded device wait gave up"
+    if old is None:
+        os.environ.pop("TQB_STAGE1_KERNEL", None)
+    else:
+        os.environ["TQB_STAGE1_KERNEL"] = old
 
 
 def _to(dev, z, key, dtype=None):
@@ -106,7 +126,8 @@ def _random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0, de
                 centroids=cents)
 
 
-@pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8), (8, 1), (16, 2), (24, 8), (6, 2), (4, 4)])
+@pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8), (8, 1), (16, 2), (24, 8), (6, 2), (4, 4),
+                                   (48, 16), (12, 3), (40, 8), (10, 5), (28, 4)])
 def test_gqa_shapes_vs_oracle(cuda_device, hq, hk):
     z = _random_case(hq * 100 + hk, 3, hq, hk, [300, 17, 1024])
     S = 5

@@ -75,6 +75,13 @@ extern "C" {
 
 int tqb_version(void) { return TQB_VERSION; }
 
+int tqb_wait_timeouts(unsigned int* count, int reset) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(count != nullptr, TQB_ERR_INVALID_ARG, "count is NULL");
+    const int rc = tqb::read_wait_timeouts(count, reset != 0);
+    return rc == TQB_OK ? TQB_OK : TQB_ERR_CUDA;
+}
+
 const char* tqb_strerror(int status) {
     switch (status) {
         case TQB_OK: return "ok";

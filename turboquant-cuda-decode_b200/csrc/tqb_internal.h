@@ -85,6 +85,13 @@ struct StoreParams {
 int report_launch(cudaError_t e);
 
 int launch_stage1(const Stage1Params& p, cudaStream_t stream, int num_sms);
+// SoA Stage1 fed by the TMA page ring (tqb_stage1_ring.cu); supported when
+// the cache and query rows are 16-byte aligned.
+bool stage1_ring_supported(const Stage1Params& p);
+int launch_stage1_ring(const Stage1Params& p, cudaStream_t stream, int num_sms);
+// Reads (and optionally clears) the count of bounded device waits that ran
+// out on the current device.
+int read_wait_timeouts(unsigned int* count, bool reset);
 int launch_stage2(const Stage2Params& p, cudaStream_t stream);
 int launch_merge(const MergeParams& p, cudaStream_t stream);
 int launch_store(const StoreParams& p, cudaStream_t stream);

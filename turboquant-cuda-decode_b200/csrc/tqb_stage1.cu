@@ -44,6 +44,8 @@
 //    product is fp32-accurate; the vzero term sum_t p_t * vzero_t is added
 //    per head in fp32.
 #include <cuda_runtime.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "tqb_common.cuh"
 #include "tqb_internal.h"
@@ -593,7 +595,18 @@ int launch_t(const Stage1Params& P, cudaStream_t stream, int num_sms) {
 
 }  // namespace
 
+// TQB_STAGE1_KERNEL=regs selects the register-ring kernel for an SoA cache
+// too (the TMA page-ring kernel is the default there); read on every call.
+static bool force_register_kernel() {
+    const char* v = getenv("TQB_STAGE1_KERNEL");
+    return v != nullptr && strcmp(v, "regs") == 0;
+}
+
 int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
+    if (stage1_ring_supported(P) && !force_register_kernel()) {
+        const int rc = launch_stage1_ring(P, stream, num_sms);
+        if (rc != TQB_ERR_UNSUPPORTED) return rc;  // else: tensor maps refused, use the register kernel
+    }
     const bool soa = P.layout == TQB_LAYOUT_SOA;
     if (P.G <= 4) return soa ? launch_t<1, TQB_LAYOUT_SOA>(P, stream, num_sms)
                              : launch_t<1, TQB_LAYOUT_AOS>(P, stream, num_sms);

@@ -1,0 +1,836 @@
+// tqb_stage1_ring.cu — sm_100a Stage1 for the SoA cache, fed by a TMA page ring.
+//
+// Same result as the register-ring kernel in tqb_stage1.cu (reference:
+// reference/soa_decode_v1.py:43-314): per (sequence b, query head h, split s)
+// the normalised partial output and natural-log LSE of the split's tokens.
+//
+// Structure (one CTA per SM, persistent):
+//  * A CTA holds kGroups groups.  A group is 8 compute warps plus one
+//    producer warp.  The group walks "tiles" of 8 consecutive work items
+//    (b, s, KV head; head fastest), one item per compute warp, so with Hk = 8
+//    the 8 warps share every page of one (b, s) split.
+//  * The producer warp moves each page of the tile into a kStages-deep
+//    shared-memory ring with TMA (no multicast): one cp.async.bulk.tensor of
+//    the tile's head slices (a 4-D tensor map over [block][head][token][128 B]
+//    with a box of {128 B, 16 tokens, 8 heads}; narrower runs use boxes of
+//    4/2/1 heads) plus one cp.async.bulk of their metadata, all completing on
+//    the stage's "full" mbarrier.  The compute warps release a
+//    stage through its "empty" mbarrier.  Loads therefore need no registers
+//    and no per-page address arithmetic in the compute warps, and up to
+//    kStages pages per group are in flight, independently of the math.
+//  * In shared memory a head's 16 token rows are one 2 KB column, written
+//    with the 128-byte swizzle (16-byte chunk j of token t lands at chunk
+//    j ^ (t & 7)).  The compute lanes own tokens tau(g) =
+//    {0,4,2,6,8,12,10,14}[g] and tau(g)+1, so every K (LDS.128), V (LDS.64)
+//    and metadata load of a page is free of bank conflicts; the PV operand
+//    tokens of lane (g, c) are then {2c, 2c+1, 2c+8, 2c+9}, the natural k
+//    order of mma.m16n8k16.
+//  * The tile's query rows (fp32, one tensor copy of G rows per item) land in
+//    a per-group query area with its own full/empty barrier pair, ahead of
+//    the tile.
+//  * The math per page is the register kernel's: Q.K and P.V on the tensor
+//    cores with fp16 hi/lo splits (fp32-accurate), online softmax in the
+//    exp2 domain with a lazy reference max.
+//  * Every mbarrier wait is bounded (kWaitCycles); a wait that runs out bumps
+//    a device counter (tqb_wait_timeouts) and the warp leaves its loops, so a
+//    protocol fault ends the kernel instead of hanging the GPU.
+#include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched at run time
+#include <cuda_runtime.h>
+
+#include "tqb_common.cuh"
+#include "tqb_internal.h"
+
+namespace tqb {
+
+// Number of bounded mbarrier waits that ran out (read by tqb_wait_timeouts).
+__device__ unsigned int g_wait_timeouts = 0;
+
+namespace {
+
+constexpr int kGroupWarps = 8;                                 // compute warps per group
+constexpr int kColBytes = kBlockSize * kDataBytes;             // 2048: one head's page column
+constexpr int kMetaSlot = 3 * kBlockSize * 2;                  // 96 B: knorm, vscale, vzero
+constexpr int kMetaOff = kGroupWarps * kColBytes;              // 16384
+constexpr int kStageBytes = 17408;                             // data + metadata, 1024-aligned
+static_assert(kMetaOff + kGroupWarps * kMetaSlot <= kStageBytes && kStageBytes % 1024 == 0, "stage");
+constexpr int kQRowBytes = kHeadDim * 4;                       // one fp32 query row
+constexpr int kLutStride = 256;                                // bytes per table entry
+constexpr int kLutCopies = 32;                                 // one copy per lane
+constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
+constexpr int kLutAddr = 0x10000;                              // shared address of the table
+constexpr int kDynBase = 0x400;  // shared address of dynamic shared memory (1 KB reserved below it)
+constexpr int kBarStride = 128;                                // barrier block per group
+constexpr long long kWaitCycles = 2000000000LL;                // ~1 s at 1.9 GHz
+constexpr float kLazy = 8.0f;                                  // lazy-rescale slack (log2)
+constexpr float kWMax = 32768.0f;                              // largest W on the lazy path
+
+// Warp roles: kGroups x 8 compute warps (whole warpgroups) and one producer
+// warpgroup whose warp gi feeds group gi (its other warps leave at once).
+// setmaxnreg moves registers from the producer warpgroup to the compute
+// warpgroups; the shares add up to at most the launch allocation
+// (kThreads x kLaunchRegs), so every setmaxnreg.inc can be satisfied.
+template <int NT>
+struct Cfg {
+    static constexpr int kGroups = NT == 1 ? 2 : 1;
+    static constexpr int kStages = 3;
+    static constexpr int kHeadsPerWarp = 4 * NT;
+    static constexpr int kQBytes = kGroupWarps * kHeadsPerWarp * kQRowBytes;
+    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kComputeWarps = kGroups * kGroupWarps;
+    static constexpr int kWarps = kComputeWarps + 4;
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kLaunchRegs = NT == 1 ? 96 : 168;     // 65536 / kThreads, rounded down to 8
+    static constexpr int kProducerRegs = 32;
+    static constexpr int kComputeRegs = NT == 1 ? 112 : 232;
+    static_assert(kThreads * kLaunchRegs <= 65536, "launch registers");
+    static_assert(kComputeWarps * 32 * kComputeRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs,
+                  "register split exceeds the launch allocation");
+    // Dynamic shared memory, which starts at shared address kDynBase: the K
+    // table sits at shared address 0x10000, so a PRMT of (table page 0x01,
+    // K byte, lane copy offset) is its complete LDS address.  Below it: group
+    // 0's ring and the barrier blocks; above it: the query areas and group
+    // 1's ring.  Every ring stage and query area is 1024-byte aligned.
+    static constexpr int kLutOff = kLutAddr - kDynBase;            // 64512
+    static constexpr int kBarOff = kRingBytes;                     // after group 0's ring
+    static constexpr int kHighOff = kLutOff + kLutBytes;           // 130048
+    static __host__ __device__ constexpr int ring_off(int gi) { return gi == 0 ? 0 : kHighOff + kQBytes; }
+    static __host__ __device__ constexpr int q_off(int gi) { return gi == 0 ? kHighOff : kHighOff + kQBytes + kRingBytes; }
+    static constexpr int kSmem = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
+    static_assert(kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
+    static_assert(8 * (2 * kStages + 2) + 4 * kStages <= kBarStride, "barrier block");
+    static_assert(kSmem <= 232448, "shared memory per CTA");
+};
+
+// Tensor maps of one launch (kernel parameters, __grid_constant__):
+// page[i] covers the SoA data region as [block][head][token][128 B] (dims
+// innermost first: 128 B, token, head, block) with a box of 8 >> i heads and
+// the 128-byte swizzle; query covers q_rot as [B][Hq][128 fp32] with a box of
+// G rows.
+struct RingMaps {
+    CUtensorMap page[4];
+    CUtensorMap query;
+};
+
+// ---- mbarrier / bulk-copy primitives (PTX ISA 8.x, sm_90+) -----------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits until every lane has observed the completion of the phase of `bar`
+// with the given parity.  Warp-uniform result: false (and one count in
+// g_wait_timeouts per warp) when kWaitCycles pass first.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+        if (__any_sync(0xffffffffu, clock64() - t0 > kWaitCycles)) {
+            if ((threadIdx.x & 31) == 0) atomicAdd(&g_wait_timeouts, 1u);
+            return false;
+        }
+    }
+}
+// Global -> shared bulk copy completing on `bar` (16-byte aligned, size a
+// multiple of 16).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+// Tensor-map copies (global -> shared, completing on `bar`).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4}], [%5];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
+}
+// Table entry at a shared address (the table is constant once built).
+__device__ __forceinline__ uint2 lut_ld(uint32_t a) {
+    uint2 r;
+    asm("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t r;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(r) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+    const uint4 u = lds128(a);
+    return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Work item -> (b, s, KV head) and its token range [start, end); false when
+// the item does not exist or its split is empty (left unwritten).
+struct ItemInfo {
+    int b, s, kvh, start, end;
+};
+__device__ __forceinline__ bool decode_item(const Stage1Params& P, uint32_t item, ItemInfo& r) {
+    r.b = r.s = r.kvh = r.start = r.end = 0;
+    if (item >= (uint32_t)P.num_items) return false;
+    const uint32_t rest = P.div_hk.div(item);
+    r.kvh = (int)(item - rest * (uint32_t)P.Hk);
+    const uint32_t bq = P.div_s.div(rest);
+    r.s = (int)(rest - bq * (uint32_t)P.S);
+    r.b = (int)bq;
+    const int nsp = P.nsplits ? min(__ldg(P.nsplits + r.b), P.S) : P.S;
+    if (r.s >= nsp) return false;
+    const int L = min(__ldg(P.seq_lens + r.b), P.max_blocks * kBlockSize);
+    const int split_len = (L + nsp - 1) / nsp;
+    r.start = split_len * r.s;
+    r.end = min(r.start + split_len, L);
+    return r.start < r.end;
+}
+
+// Lanes 0-7 decode the 8 items of tile t (lane l: item 8t + l); returns the
+// lane's page count (0 for lanes >= 8 and empty items) in `np` and the
+// tile's page count (max over its items) as the result.
+__device__ __forceinline__ int tile_items(const Stage1Params& P, uint32_t t, int lane, ItemInfo& ir, int& np) {
+    np = 0;
+    if (lane < kGroupWarps && decode_item(P, t * kGroupWarps + lane, ir))
+        np = (ir.end - 1) / kBlockSize - ir.start / kBlockSize + 1;
+    else
+        ir.b = ir.s = ir.kvh = ir.start = ir.end = 0;
+    int m = np;
+#pragma unroll
+    for (int o = 1; o < kGroupWarps; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return __shfl_sync(0xffffffffu, m, 0);  // uniform over the warp
+}
+
+// Shared-memory map of one group.
+struct GroupSmem {
+    uint32_t ring, qarea, bars;
+    __device__ uint32_t stage(int s) const { return ring + (uint32_t)s * kStageBytes; }
+    __device__ uint32_t full(int s) const { return bars + 8u * s; }
+    template <int NS>
+    __device__ uint32_t empty(int s) const { return bars + 8u * (NS + s); }
+    template <int NS>
+    __device__ uint32_t q_full() const { return bars + 16u * NS; }
+    template <int NS>
+    __device__ uint32_t q_empty() const { return bars + 16u * NS + 8; }
+    template <int NS>
+    __device__ uint32_t vmask(int s) const { return bars + 16u * NS + 16 + 4u * s; }
+};
+
+// ---------------------------------------------------------------------------
+// Producer warp: query rows and pages of each tile into the group's ring.
+// Runs at kProducerRegs registers, so run parameters live one run per lane
+// and block ids are fetched one stage ahead into a single register.
+// ---------------------------------------------------------------------------
+template <int NT>
+__device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M, const GroupSmem& gs, int gi,
+                                        int lane) {
+    using C = Cfg<NT>;
+    constexpr int NS = C::kStages;
+    const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
+    const uint32_t tile_stride = gridDim.x * C::kGroups;
+    const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
+    const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
+    // Every tile starts at ring slot 0; bit s of `uses` is the parity of the
+    // number of pages slot s has taken so far, `used` marks slots in use.
+    uint32_t tq = 0, uses = 0, used = 0;
+    bool abort = false;
+
+    // Query rows of a tile (lanes 0-7: its items) into the query area, once
+    // the compute warps have released the previous tile's rows.
+    auto issue_query = [&](const ItemInfo& x, int npx) {
+        const uint32_t vit = __ballot_sync(0xffffffffu, npx > 0) & 0xFFu;
+        if (!mbar_wait(gs.q_empty<NS>(), (tq & 1u) ^ 1u)) return false;
+        if (lane == 0) mbar_arrive_tx(gs.q_full<NS>(), (uint32_t)__popc(vit) * P.G * kQRowBytes);
+        __syncwarp();
+        if (lane < kGroupWarps && npx > 0)  // item `lane`: its G query rows, one tensor copy
+            tma_load_3d(gs.qarea + (uint32_t)(lane * C::kHeadsPerWarp) * kQRowBytes, &M.query, 0, x.kvh * P.G, x.b,
+                        gs.q_full<NS>());
+        tq++;
+        return true;
+    };
+    // Next tile of this group with at least one page (or t >= num_tiles).
+    auto next_tile = [&](uint32_t t, ItemInfo& x, int& npx, int& np_tile) {
+        for (; t < num_tiles; t += tile_stride)
+            if ((np_tile = tile_items(P, t, lane, x, npx)) > 0) return t;
+        return t;
+    };
+
+    ItemInfo ir;
+    int np = 0, np_tile = 0;
+    uint32_t t = next_tile(blockIdx.x * C::kGroups + gi, ir, np, np_tile);
+    if (t < num_tiles && !issue_query(ir, np)) abort = true;
+    while (t < num_tiles && !abort) {
+        // The next tile is decoded now; its query rows go out once page 0 of
+        // this tile has been released (the compute warps have read this
+        // tile's rows by then), well before they are needed.
+        ItemInfo irn;
+        int npn = 0, np_tile_n = 0;
+        const uint32_t tn = next_tile(t + tile_stride, irn, npn, np_tile_n);
+        bool next_query_sent = tn >= num_tiles;
+        // Runs of consecutive items sharing one (b, s): their head slices are
+        // adjacent in every token row, so one copy per row serves a run.
+        const int key = np > 0 ? ir.b * P.S + ir.s : -1 - lane;
+        const int key_prev = __shfl_up_sync(0xffffffffu, key, 1);
+        const int key_next = __shfl_down_sync(0xffffffffu, key, 1);
+        const bool leader = np > 0 && (lane == 0 || key_prev != key);
+        const bool last = np > 0 && (lane == kGroupWarps - 1 || key_next != key);
+        const uint32_t lmask = __ballot_sync(0xffffffffu, leader) & 0xFFu;
+        const uint32_t emask = __ballot_sync(0xffffffffu, last) & 0xFFu;
+        const int nruns = __popc(lmask);
+        // Lane r < nruns describes run r: first warp (column), width, pages,
+        // first KV head and block-table position.
+        const int col = lane < nruns ? (int)__fns(lmask, 0, lane + 1) : 0;
+        const int r_np = __shfl_sync(0xffffffffu, np, col);
+        const int r_b = __shfl_sync(0xffffffffu, ir.b, col);
+        const int r_pf = __shfl_sync(0xffffffffu, ir.start, col) / kBlockSize;
+        const int r_kvh = __shfl_sync(0xffffffffu, ir.kvh, col);
+        const int r_nw = lane < nruns ? __ffs(emask >> col) : 0;
+        const int32_t* r_bt = P.bt + (int64_t)r_b * P.bt_stride + r_pf;
+        const int np_r = lane < nruns ? r_np : 0;
+        int next_id = np_r > 0 ? __ldg(r_bt) : 0;
+
+        // ---- pages ---------------------------------------------------------
+        int slot = 0;
+        for (int k = 0; k < np_tile; k++) {
+            const int id = next_id;
+            next_id = k + 1 < np_r ? __ldg(r_bt + k + 1) : 0;  // lands while we wait
+            const bool here = k < np_r;
+            const bool ok = (uint32_t)id < nblocks;
+            const uint32_t bytes =
+                __reduce_add_sync(0xffffffffu, here ? (uint32_t)r_nw * (kBlockSize * kDataBytes + kMetaSlot) : 0u);
+            const uint32_t vm = __reduce_or_sync(0xffffffffu, (here && ok) ? ((1u << r_nw) - 1u) << col : 0u);
+            const uint32_t my_id = ok ? (uint32_t)id : 0u;  // a masked page copies block 0
+            if (k == NS && !next_query_sent) {
+                if (!issue_query(irn, npn)) { abort = true; break; }
+                next_query_sent = true;
+            }
+            if (!mbar_wait(gs.empty<NS>(slot), ((uses >> slot) & 1u) ^ 1u)) { abort = true; break; }
+            if (lane == 0) {
+                sts32(gs.vmask<NS>(slot), vm);
+                mbar_arrive_tx(gs.full(slot), bytes);
+            }
+            __syncwarp();
+            // Lane r < nruns copies run r: its head slices as boxes of 8/4/2/1
+            // heads (one box when the run is a whole group) and its metadata.
+            if (here) {
+                const uint32_t dst = gs.stage(slot);
+                int off = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int box = kGroupWarps >> i;
+                    if (r_nw & box) {
+                        tma_load_4d(dst + (uint32_t)(col + off) * kColBytes, &M.page[i], 0, 0, r_kvh + off,
+                                    (int)my_id, gs.full(slot));
+                        off += box;
+                    }
+                }
+                const uint8_t* blk = P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes;
+                bulk_g2s(dst + kMetaOff + (uint32_t)col * kMetaSlot,
+                         blk + kBlockSize * tok_bytes + (uint32_t)r_kvh * kMetaSlot, (uint32_t)r_nw * kMetaSlot,
+                         gs.full(slot));
+            }
+            uses ^= 1u << slot;
+            used |= 1u << slot;
+            if (++slot == NS) slot = 0;
+        }
+        if (!abort && !next_query_sent && !issue_query(irn, npn)) abort = true;
+        t = tn;
+        ir = irn;
+        np = npn;
+        np_tile = np_tile_n;
+    }
+    if (abort) {
+        // Let the copies already issued land before the CTA can exit: the
+        // last phase of every slot in use, then the last query rows.
+        for (int sl = 0; sl < NS; sl++)
+            if (((used >> sl) & 1u) && !mbar_wait(gs.full(sl), ((uses >> sl) & 1u) ^ 1u)) break;
+        if (tq > 0) mbar_wait(gs.q_full<NS>(), (tq - 1) & 1u);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Compute warp
+// ---------------------------------------------------------------------------
+template <int NT>
+struct ItemState {
+    uint32_t qf[NT][16];  // Q.K B fragments
+    float kfac[NT];       // score factor of this lane's head
+    float m_run[NT], l_part[NT], z_part[NT];
+    float acc[NT][8][4];  // P.V accumulators (codes scaled by 2^-20)
+};
+
+// Per-lane byte offsets inside a stage (fixed for the kernel); the swizzle
+// puts 16-byte chunk j of token t at chunk j ^ (t & 7) of its 128-byte row.
+struct LaneSmem {
+    uint32_t k0, k1;  // K bytes [16c, 16c+16) of tokens tau(g), tau(g)+1
+    uint32_t v0, v1;  // V bytes [8g, 8g+8) of tokens 2c, 2c+1 (2c+8, 2c+9: + 1024)
+    uint32_t meta;    // knorm pair of tokens tau(g), tau(g)+1 (vscale +32, vzero +64)
+};
+
+template <int NT>
+__device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, const LaneSmem& o, bool page_ok,
+                                          int tok0, int start, int end, uint32_t lut_sel_src, int g,
+                                          int c, int src_a) {
+    const uint4 k0 = lds128(sb + o.k0), k1 = lds128(sb + o.k1);
+    const uint32_t kn = lds32(sb + o.meta);
+    const bool va = page_ok && tok0 >= start && tok0 < end;
+    const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
+
+    // -- Q.K: M tile 0 = token tau(g) (rows g: C_hi, g+8: C_lo), tile 1 = tau(g)+1
+    float dq[NT][2][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+        const uint32_t w0 = word_of(k0, ks >> 1), w1 = word_of(k1, ks >> 1);
+        const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
+        // address 0x10000 | (K byte << 8) | lane copy offset, in one PRMT
+        const uint2 e0 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jA << 4)));
+        const uint2 e1 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jB << 4)));
+        const uint2 e2 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jA << 4)));
+        const uint2 e3 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jB << 4)));
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+            mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+        }
+    }
+    // V operands and scales are read after Q.K, which keeps them out of the
+    // register peak of the Q.K loop.
+    const uint32_t vsp = lds32(sb + o.meta + 32), vzp = lds32(sb + o.meta + 64);
+    uint2 v[4];
+    v[0] = lds64(sb + o.v0);
+    v[1] = lds64(sb + o.v1);
+    v[2] = lds64(sb + o.v0 + 8 * kDataBytes);
+    v[3] = lds64(sb + o.v1 + 8 * kDataBytes);
+    const float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
+    const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
+    const float vs1 = vb ? half_bits_to_float(vsp >> 16) : 0.0f;
+    const float vz0 = va ? half_bits_to_float(vzp) : 0.0f;
+    const float vz1 = vb ? half_bits_to_float(vzp >> 16) : 0.0f;
+
+    // -- online softmax (exp2 domain), lazy reference max --
+    uint32_t bw0[NT], bw1[NT];
+    float alpha[NT];
+    bool rescale = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        const float d0 = (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
+        const float d1 = (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
+        float s0 = d0 * kn0 * st.kfac[nt];
+        float s1 = d1 * kn1 * st.kfac[nt];
+        s0 = va ? s0 : -INFINITY;
+        s1 = vb ? s1 : -INFINITY;
+        const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
+        const float mold = st.m_run[nt];
+        float mref = tmax > mold + kLazy ? tmax : mold;
+        float mref_e = mref == -INFINITY ? 0.0f : mref;
+        float p0 = ex2(s0 - mref_e), p1 = ex2(s1 - mref_e);
+        float w0 = p0 * vs0, w1 = p1 * vs1;
+        if (__any_sync(0xffffffffu, fmaxf(w0, w1) > kWMax)) {
+            mref = fmaxf(mold, tmax);
+            mref_e = mref == -INFINITY ? 0.0f : mref;
+            p0 = ex2(s0 - mref_e);
+            p1 = ex2(s1 - mref_e);
+            w0 = p0 * vs0;
+            w1 = p1 * vs1;
+        }
+        alpha[nt] = (mold == -INFINITY || mref == mold) ? 1.0f : ex2(mold - mref);
+        rescale |= alpha[nt] != 1.0f;
+        st.l_part[nt] = st.l_part[nt] * alpha[nt] + (p0 + p1);
+        st.z_part[nt] = st.z_part[nt] * alpha[nt] + (p0 * vz0 + p1 * vz1);
+        st.m_run[nt] = mref;
+        const __half2 wh = __floats2half2_rn(w0, w1);
+        const __half2 wl = __floats2half2_rn(w0 - __low2float(wh), w1 - __high2float(wh));
+        // B fragment of P.V: lane (g, c) takes tokens {2c, 2c+1} from lane
+        // src_a (the owner of tau = 2c for head g>>1) and {2c+8, 2c+9} from
+        // lane src_a + 16, part g&1 (hi / lo).
+        const uint32_t hA = __shfl_sync(0xffffffffu, h2_as_u32(wh), src_a);
+        const uint32_t lA = __shfl_sync(0xffffffffu, h2_as_u32(wl), src_a);
+        const uint32_t hB = __shfl_sync(0xffffffffu, h2_as_u32(wh), src_a + 16);
+        const uint32_t lB = __shfl_sync(0xffffffffu, h2_as_u32(wl), src_a + 16);
+        bw0[nt] = (g & 1) ? lA : hA;
+        bw1[nt] = (g & 1) ? lB : hB;
+    }
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) st.acc[nt][i][k] *= alpha[nt];
+    }
+
+    // -- P.V: rows g / g+8 = low / high nibble of V byte i&3 of word i>>2,
+    //    k = tokens 2c, 2c+1, 2c+8, 2c+9; codes enter as exact fp16
+    //    subnormals code * 2^-20 (mantissa bits 4-7).
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int wi = i >> 2, bi = i & 3;
+        const uint32_t sel = (uint32_t)(bi | (bi << 4) | ((4 + bi) << 8) | ((4 + bi) << 12));
+        const uint32_t x0 = wi ? v[0].y : v[0].x;
+        const uint32_t x1 = wi ? v[1].y : v[1].x;
+        const uint32_t x2 = wi ? v[2].y : v[2].x;
+        const uint32_t x3 = wi ? v[3].y : v[3].x;
+        const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
+        const uint32_t a0 = (p01 << 4) & 0x00F000F0u;
+        const uint32_t a1 = p01 & 0x00F000F0u;
+        const uint32_t a2 = (p23 << 4) & 0x00F000F0u;
+        const uint32_t a3 = p23 & 0x00F000F0u;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) mma_16816(st.acc[nt][i], a0, a1, a2, a3, bw0[nt], bw1[nt]);
+    }
+}
+
+// One page from ring slot S (a compile-time constant, so every shared and
+// barrier address below is a register plus an immediate).
+template <int NT, int S>
+__device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
+                                          int k, int my_np, int w, int tok_first, int start, int end,
+                                          uint32_t lut_sel_src, int g, int c, int src_a, int lane) {
+    constexpr int NS = Cfg<NT>::kStages;
+    if (!mbar_wait(gs.full(S), (cbits >> S) & 1u)) return false;
+    cbits ^= 1u << S;
+    if (k < my_np) {
+        const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
+        page_math<NT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
+                      lut_sel_src, g, c, src_a);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(gs.empty<NS>(S));
+    return true;
+}
+
+template <int NT>
+__device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& gs, int gi, int w, int lane,
+                                        int ec) {
+    using C = Cfg<NT>;
+    constexpr int NS = C::kStages;
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
+    const uint32_t tile_stride = gridDim.x * C::kGroups;
+    // PRMT source: byte 0 = this lane's copy offset, byte 1 = table page 0x01, byte 2 = 0
+    const uint32_t lut_sel_src = (uint32_t)(lane % kLutCopies) * 8u | ((uint32_t)(kLutAddr >> 16) << 8);
+    const int tau = 8 * (g >> 2) + 2 * ((g >> 1) & 1) + 4 * (g & 1);
+    auto sw = [](int t, int chunk) { return (uint32_t)(t * kDataBytes + ((chunk ^ (t & 7)) << 4)); };
+    const uint32_t colw = gs.ring + (uint32_t)w * kColBytes;  // shared address of this warp's column
+    LaneSmem o;
+    o.k0 = colw + sw(tau, c);
+    o.k1 = colw + sw(tau + 1, c);
+    o.v0 = colw + sw(2 * c, 4 + (g >> 1)) + 8u * (g & 1);
+    o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
+    o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
+    // Owner of token 2c in the Q.K layout: tau(g') = 2c for g' = bitswap(c).
+    const int src_a = 4 * (((c & 1) << 1) | (c >> 1)) + (g >> 1);
+    uint32_t tq = 0;     // tiles done (query-barrier phase)
+    uint32_t cbits = 0;  // bit s: parity of the pages slot s has delivered
+
+    for (uint32_t t = blockIdx.x * C::kGroups + gi; t < num_tiles; t += tile_stride) {
+        ItemInfo ir;
+        int np;
+        const int np_tile = tile_items(P, t, lane, ir, np);
+        if (np_tile == 0) continue;
+        const int b = __shfl_sync(0xffffffffu, ir.b, w);
+        const int s = __shfl_sync(0xffffffffu, ir.s, w);
+        const int kvh = __shfl_sync(0xffffffffu, ir.kvh, w);
+        const int start = __shfl_sync(0xffffffffu, ir.start, w);
+        const int end = __shfl_sync(0xffffffffu, ir.end, w);
+        const int my_np = __shfl_sync(0xffffffffu, np, w);
+
+        // ---- query fragments from the tile's query rows ---------------------
+        if (!mbar_wait(gs.q_full<NS>(), tq & 1u)) return;
+        ItemState<NT> st;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int hl = (g >> 1) + 4 * nt;
+            float qv[32];
+            float amax = 0.0f;
+            if (my_np > 0 && hl < P.G) {
+                const uint32_t qa = gs.qarea + (uint32_t)(w * C::kHeadsPerWarp + hl) * kQRowBytes + 128u * c;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float4 f = lds_f4(qa + 16u * j);
+                    qv[4 * j] = f.x; qv[4 * j + 1] = f.y; qv[4 * j + 2] = f.z; qv[4 * j + 3] = f.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(qv[j]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) qv[j] = 0.0f;
+            }
+            amax = warp_max_xor(amax, 1, 2);
+            const int eq = fp16_scale_exp(amax);
+            const float qscale = ldexpf(1.0f, eq);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
+                const __half2 h = __floats2half2_rn(x0, x1);
+                const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+                st.qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
+            }
+            const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
+            st.kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
+            st.m_run[nt] = -INFINITY;
+            st.l_part[nt] = 0.0f;
+            st.z_part[nt] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) st.acc[nt][i][k] = 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(gs.q_empty<NS>());
+        tq++;
+
+        // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
+        const int tok_first = (start / kBlockSize) * kBlockSize + tau;
+        for (int k = 0; k < np_tile; k += NS) {
+            if (!page_step<NT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a,
+                                  lane))
+                return;
+            if (k + 1 < np_tile && !page_step<NT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
+                                                     lut_sel_src, g, c, src_a, lane))
+                return;
+            if (k + 2 < np_tile && !page_step<NT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
+                                                     lut_sel_src, g, c, src_a, lane))
+                return;
+        }
+        if (my_np == 0) continue;
+
+        // ---- epilogue: lane (g, c) holds dims 16g .. 16g+15 of head c + 4nt ----
+        constexpr float kCodeScale = 1048576.0f;  // 2^20: undo the subnormal code scale
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            float l = warp_sum_xor(st.l_part[nt], 4, 16);
+            l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
+            const float z = warp_sum_xor(st.z_part[nt], 4, 16);
+            const float inv = __frcp_rn(l);
+            const int hl = c + 4 * nt;
+            if (hl < P.G) {
+                float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + hl) * P.msh + (int64_t)s * P.mss;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    dst[16 * g + 2 * i] = ((st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale + z) * inv;
+                    dst[16 * g + 2 * i + 1] = ((st.acc[nt][i][2] + st.acc[nt][i][3]) * kCodeScale + z) * inv;
+                }
+                if (g == 0) dst[kHeadDim] = st.m_run[nt] * kLn2 + logf(l);
+            }
+        }
+    }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
+    stage1_ring_kernel(const Stage1Params P, const __grid_constant__ RingMaps M) {
+    using C = Cfg<NT>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- K table: 256 entries x 32 lane copies of {C_hi pair, C_lo pair} ----
+    float cmax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
+    const int ec = fp16_scale_exp(cmax);
+    const float cscale = ldexpf(1.0f, ec);
+    for (int e = tid; e < 256 * kLutCopies; e += C::kThreads) {
+        const int byte = e / kLutCopies;
+        const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
+        const __half2 h = __floats2half2_rn(clo, chi);
+        const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
+        *reinterpret_cast<uint2*>(smem + C::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
+    }
+
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    if (base != (uint32_t)kDynBase) {  // the table address above assumes this window layout
+        if (tid == 0) atomicAdd(&g_wait_timeouts, 1u);
+        return;
+    }
+    const bool producer = warp >= C::kComputeWarps;
+    const int gi = producer ? warp - C::kComputeWarps : warp / kGroupWarps;
+    GroupSmem gs;
+    gs.ring = base + (uint32_t)C::ring_off(gi);
+    gs.qarea = base + (uint32_t)C::q_off(gi);
+    gs.bars = base + C::kBarOff + (uint32_t)gi * kBarStride;
+    if (tid < C::kGroups) {
+        GroupSmem gb;
+        gb.bars = base + C::kBarOff + (uint32_t)tid * kBarStride;
+        for (int s = 0; s < C::kStages; s++) {
+            mbar_init(gb.full(s), 1);
+            mbar_init(gb.template empty<C::kStages>(s), kGroupWarps);
+        }
+        mbar_init(gb.template q_full<C::kStages>(), 1);
+        mbar_init(gb.template q_empty<C::kStages>(), kGroupWarps);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    }
+    __syncthreads();
+
+    if (producer) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::kProducerRegs));
+        if (gi < C::kGroups) produce<NT>(P, M, gs, gi, lane);
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::kComputeRegs));
+        consume<NT>(P, gs, gi, warp % kGroupWarps, lane, ec);
+    }
+}
+
+// True when the compiled kernel launches with enough registers per thread
+// for its setmaxnreg split (otherwise a setmaxnreg.inc could wait forever,
+// so the ring kernel is not used).
+template <int NT>
+bool ring_registers_ok() {
+    using C = Cfg<NT>;
+    static int ok = -1;
+    if (ok < 0) {
+        cudaFuncAttributes a{};
+        ok = cudaFuncGetAttributes(&a, stage1_ring_kernel<NT>) == cudaSuccess &&
+             (int64_t)a.numRegs * C::kThreads >=
+                 (int64_t)C::kComputeWarps * 32 * C::kComputeRegs + 128 * C::kProducerRegs &&
+             a.maxThreadsPerBlock >= C::kThreads;
+        if (!ok) cudaGetLastError();
+    }
+    return ok == 1;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on libcuda).
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// Tensor maps of the page data and query rows of one launch; false when the
+// driver rejects them.
+bool encode_maps(const Stage1Params& P, RingMaps& M) {
+    EncodeTiledFn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t nblk = P.num_blocks > 0 ? (cuuint64_t)P.num_blocks : (cuuint64_t)0x7fffffff;
+    const cuuint64_t dims[4] = {(cuuint64_t)kDataBytes, (cuuint64_t)kBlockSize, (cuuint64_t)P.Hk, nblk};
+    const cuuint64_t strides[3] = {(cuuint64_t)P.Hk * kDataBytes, (cuuint64_t)kDataBytes, (cuuint64_t)P.block_bytes};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int i = 0; i < 4; i++) {
+        const int heads = (kGroupWarps >> i) < P.Hk ? (kGroupWarps >> i) : P.Hk;
+        const cuuint32_t box[4] = {(cuuint32_t)kDataBytes, (cuuint32_t)kBlockSize, (cuuint32_t)heads, 1};
+        if (enc(&M.page[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(P.cache), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    const cuuint64_t qdims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)P.Hq, (cuuint64_t)P.B};
+    const cuuint64_t qstr[2] = {(cuuint64_t)P.qsh * 4, (cuuint64_t)P.qsb * 4};
+    const cuuint32_t qbox[3] = {(cuuint32_t)kHeadDim, (cuuint32_t)P.G, 1};
+    return enc(&M.query, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(P.q), qdims, qstr, qbox, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NT>
+int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream, int num_sms) {
+    using C = Cfg<NT>;
+    auto kern = stage1_ring_kernel<NT>;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+            return report_launch(cudaGetLastError());
+        configured_dev = dev;
+    }
+    const int64_t tiles = (P.num_items + kGroupWarps - 1) / kGroupWarps;
+    const int64_t need = (tiles + C::kGroups - 1) / C::kGroups;
+    const int64_t grid = need < num_sms ? need : num_sms;
+    if (grid <= 0) return TQB_OK;
+    kern<<<(unsigned)grid, C::kThreads, C::kSmem, stream>>>(P, M);
+    return report_launch(cudaGetLastError());
+}
+
+}  // namespace
+
+bool stage1_ring_supported(const Stage1Params& P) {
+    const bool regs_ok = P.G <= 4 ? ring_registers_ok<1>() : ring_registers_ok<2>();
+    // Query rows are copied by a tensor map: 16-byte row strides, >= one row.
+    return regs_ok && P.layout == TQB_LAYOUT_SOA && P.G >= 1 && P.G <= 8 &&
+           (reinterpret_cast<uintptr_t>(P.cache) & 15) == 0 && (P.block_bytes & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(P.q) & 15) == 0 && P.qsh >= kHeadDim && (P.qsh & 3) == 0 &&
+           P.qsb >= P.qsh && (P.qsb & 3) == 0 && encoder() != nullptr;
+}
+
+int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) {
+    RingMaps M;
+    if (!encode_maps(P, M)) return TQB_ERR_UNSUPPORTED;
+    return P.G <= 4 ? launch_ring_t<1>(P, M, stream, num_sms) : launch_ring_t<2>(P, M, stream, num_sms);
+}
+
+int read_wait_timeouts(unsigned int* count, bool reset) {
+    cudaError_t e = cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int));
+    if (e == cudaSuccess && reset) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(unsigned int));
+    }
+    return e == cudaSuccess ? TQB_OK : report_launch(e);
+}
+
+}  // namespace tqb

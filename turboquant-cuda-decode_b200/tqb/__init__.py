@@ -9,7 +9,7 @@ drop-in launchers (``tqb.compat``), the cache layout (``tqb.layout``), the
 codebook (``tqb.codebook``) and multi-GPU sharding (``tqb.sharding``).
 """
 
-from ._lib import TqbError, version  # noqa: F401
+from ._lib import TqbError, version, wait_timeouts  # noqa: F401
 from .codebook import build_pair_lut, get_centroids, get_midpoints  # noqa: F401
 from .compat import (  # noqa: F401
     convert_soa_to_aos_kv_cache,

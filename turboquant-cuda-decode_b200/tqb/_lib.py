@@ -34,7 +34,20 @@ EXPORTED_SYMBOLS = (
     "tqb_strerror",
     "tqb_last_error_detail",
     "tqb_version",
+    "tqb_wait_timeouts",
 )
+
+
+# Status names, the same text tqb_strerror() returns (usable before the
+# library is loaded, e.g. for the error that says it cannot be loaded).
+STATUS_TEXT = {
+    TQB_OK: "ok",
+    TQB_ERR_INVALID_ARG: "invalid argument",
+    TQB_ERR_UNSUPPORTED: "unsupported shape or configuration",
+    TQB_ERR_ALIGNMENT: "misaligned pointer or stride",
+    TQB_ERR_LAUNCH: "kernel launch failed",
+    TQB_ERR_CUDA: "CUDA runtime error",
+}
 
 
 class TqbError(RuntimeError):
@@ -42,7 +55,7 @@ class TqbError(RuntimeError):
 
     def __init__(self, status: int, detail: str = ""):
         self.status = status
-        msg = f"tqb: {strerror(status) if status else 'error'}"
+        msg = f"tqb: {STATUS_TEXT.get(status, f'status {status}')}"
         if detail:
             msg += f": {detail}"
         super().__init__(msg)
@@ -122,6 +135,8 @@ def load() -> ctypes.CDLL:
             lib.tqb_last_error_detail.restype = ctypes.c_char_p
             lib.tqb_version.argtypes = []
             lib.tqb_version.restype = ctypes.c_int
+            lib.tqb_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+            lib.tqb_wait_timeouts.restype = ctypes.c_int
             _lib = lib
     return _lib
 
@@ -141,3 +156,11 @@ def check(status: int) -> None:
 
 def version() -> int:
     return load().tqb_version()
+
+
+def wait_timeouts(reset: bool = True) -> int:
+    """Bounded device waits that gave up on the current device (0 in a
+    healthy run); clears the counter when ``reset``."""
+    n = ctypes.c_uint(0)
+    check(load().tqb_wait_timeouts(ctypes.byref(n), int(bool(reset))))
+    return int(n.value)
