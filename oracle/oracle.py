@@ -256,5 +256,24 @@ def stage2_np(mid_o, seq_lens, num_splits_per_seq=None):
     return out, lse
 
 
+def merge_np(partials):
+    """Merge G per-range partials ``[G, B, Hq, D+1]`` (O, natural-log LSE in
+    the last slot) into (O [B, Hq, D], LSE [B, Hq]) in float64.  The split
+    merge's running log-sum-exp algebra (reference baseline/stage2.py:37-52)
+    applied across KV ranges; a part with LSE = -inf (an empty range) is
+    skipped, and a row with no part left gives NaN / -inf."""
+    p = np.asarray(partials, np.float64)
+    G, B, Hq, D1 = p.shape
+    lse = p[..., D1 - 1]                       # [G, B, Hq]
+    keep = np.isfinite(lse) | (lse > 0)
+    m = np.where(keep, lse, -np.inf).max(0)    # [B, Hq]
+    with np.errstate(invalid="ignore", divide="ignore"):
+        w = np.where(keep, np.exp(lse - m[None]), 0.0)
+        num = (w[..., None] * np.where(keep[..., None], p[..., : D1 - 1], 0.0)).sum(0)
+        den = w.sum(0)
+        out = num / den[..., None]
+        return out, m + np.log(den)
+
+
 def default_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

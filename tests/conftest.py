@@ -6,6 +6,8 @@ from __future__ import annotations
 import sys
 from pathlib import Path
 
+import math
+
 import numpy as np
 import pytest
 
@@ -67,3 +69,36 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+def random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0):
+    """Seeded cache written by the CPU oracle store (reference semantics),
+    shuffled block pool, random garbage in unused slots."""
+    import tqb
+    from oracle import oracle as O
+    from tqb import layout as L
+
+    rng = np.random.default_rng(seed)
+    pages = [max(1, math.ceil(n / 16)) for n in seq_lens]
+    nblk = sum(pages) + pool_extra
+    slot = L.SLOT_SIZE
+    cache = rng.integers(0, 256, size=(nblk, 16, Hk, slot), dtype=np.uint8)
+    perm = rng.permutation(nblk)
+    bt = np.zeros((B, max(pages)), np.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]]
+        k += pages[b]
+    cents = tqb.get_centroids(128, 4).numpy()
+    mids = tqb.get_midpoints(tqb.get_centroids(128, 4)).numpy()
+    ntok = int(sum(seq_lens))
+    slots = np.concatenate([bt[b, np.arange(n) // 16] * 16 + np.arange(n) % 16 for b, n in enumerate(seq_lens)]).astype(np.int32)
+    key = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
+    norms = np.linalg.norm(key, axis=1).astype(np.float32)
+    R = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    y = ((key / (norms[:, None] + 1e-8)) @ R).astype(np.float32)
+    val = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
+    O.store(O.LAYOUT_SOA, y, norms, val, mids, cents, slots, cache, norm_correction=True)
+    q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
+    return dict(q_rot=q, kv_cache=cache, block_table=bt, seq_lens=np.asarray(seq_lens, np.int32),
+                centroids=cents)

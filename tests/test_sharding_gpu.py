@@ -1,0 +1,107 @@
+"""Multi-GPU sharding on the GPU.  With one GPU, every rank of a DP / TP / SP
+layout runs in turn on cuda:0 and the results are reassembled (SP through
+the tqb_merge_partials kernel); with two or more GPUs, SP also runs as one
+process per GPU over NCCL.  All compare with the single-process CPU oracle
+over the whole sequence at the conftest tolerance."""
+
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close, random_case
+from oracle import oracle as O
+import tqb
+from tqb import sharding
+
+pytestmark = pytest.mark.gpu
+
+
+def _full_ref(c):
+    mid = O.stage1(c["q_rot"], c["kv_cache"], c["block_table"], c["seq_lens"], c["centroids"], 1)
+    return O.stage2(mid, c["seq_lens"])
+
+
+def _dev(c, k, dev):
+    return torch.from_numpy(np.ascontiguousarray(c[k])).to(dev)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sp_ranks_merged_by_kernel(cuda_device, world):
+    lens = [1000, 17, 4100, 1]
+    c = random_case(100 + world, len(lens), 32, 8, lens)
+    dev = cuda_device
+    parts = []
+    for r in range(world):
+        bt, sl, _ = sharding.sp_shard(_dev(c, "block_table", dev), lens, world, r)
+        parts.append(sharding.local_partial(_dev(c, "q_rot", dev), _dev(c, "kv_cache", dev), bt, sl,
+                                            _dev(c, "centroids", dev), 16))
+    out = torch.empty(len(lens), 32, 128, device=dev)
+    lse = torch.empty(len(lens), 32, device=dev)
+    tqb.merge_partials(torch.stack(parts).contiguous(), out, lse)
+    ref_out, ref_lse = _full_ref(c)
+    assert_close(out.cpu().numpy(), ref_out, what=f"SP{world} output")
+    assert_close(lse.cpu().numpy(), ref_lse, what=f"SP{world} lse")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_ranks_reassembled(cuda_device, world):
+    lens = [300, 77, 1024]
+    c = random_case(200 + world, len(lens), 64, 8, lens)
+    dev = cuda_device
+    outs = []
+    for r in range(world):
+        kv = sharding.tp_shard_cache(_dev(c, "kv_cache", dev), world, r)
+        q = sharding.tp_shard_query(_dev(c, "q_rot", dev), 8, world, r).contiguous()
+        part = sharding.local_partial(q, kv, _dev(c, "block_table", dev), _dev(c, "seq_lens", dev),
+                                      _dev(c, "centroids", dev), 4)
+        outs.append(part)
+    got = torch.cat(outs, dim=1).cpu().numpy()  # heads back in order
+    ref_out, ref_lse = _full_ref(c)
+    assert_close(got[..., :128], ref_out, what=f"TP{world} output")
+    assert_close(got[..., 128], ref_lse, what=f"TP{world} lse")
+
+
+def test_dp_ranks_reassembled(cuda_device):
+    lens = [700, 30, 2000, 512, 513, 90, 1600]
+    c = random_case(300, len(lens), 32, 8, lens)
+    dev = cuda_device
+    world = 4
+    plan = sharding.plan_batch(lens, world)
+    got = np.empty((len(lens), 32, 129), np.float32)
+    for r in range(world):
+        idx = torch.tensor(plan[r], dtype=torch.long)
+        part = sharding.local_partial(_dev(c, "q_rot", dev)[idx.to(dev)].contiguous(), _dev(c, "kv_cache", dev),
+                                      _dev(c, "block_table", dev)[idx.to(dev)].contiguous(),
+                                      _dev(c, "seq_lens", dev)[idx.to(dev)].contiguous(), _dev(c, "centroids", dev), 8)
+        got[plan[r]] = part.cpu().numpy()
+    ref_out, ref_lse = _full_ref(c)
+    assert_close(got[..., :128], ref_out, what="DP output")
+    assert_close(got[..., 128], ref_lse, what="DP lse")
+
+
+@pytest.mark.multigpu
+def test_sp_nccl_two_gpus(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import _dist_workers as W
+
+    lens = [2000, 33, 700]
+    c = random_case(400, len(lens), 32, 8, lens)
+    case = tmp_path / "case.npz"
+    np.savez(case, **c)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(W.sp_nccl_worker, args=(2, port, str(case), str(tmp_path), 8), nprocs=2,
+                       start_method="spawn", join=True)
+    ref_out, ref_lse = _full_ref(c)
+    for r in range(2):
+        with np.load(tmp_path / f"nccl{r}.npz") as z:
+            assert_close(z["out"], ref_out, what=f"NCCL SP rank {r} output")
+            assert_close(z["lse"], ref_lse, what=f"NCCL SP rank {r} lse")

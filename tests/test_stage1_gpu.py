@@ -20,7 +20,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN_CASES, assert_close
+from conftest import GOLDEN_CASES, assert_close, random_case
 from oracle import oracle as O
 import tqb
 from tqb import layout as L
@@ -97,39 +97,10 @@ def test_compat_launchers(cuda_device, golden):
     assert_close(lse.cpu().numpy(), z["lse_stage2"], what="launch_stage2 lse")
 
 
-def _random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0, dev="cuda"):
-    """Seeded cache written by the CPU oracle store (reference semantics),
-    shuffled block pool, random garbage in unused slots."""
-    rng = np.random.default_rng(seed)
-    pages = [max(1, math.ceil(n / 16)) for n in seq_lens]
-    nblk = sum(pages) + pool_extra
-    slot = L.SLOT_SIZE
-    cache = rng.integers(0, 256, size=(nblk, 16, Hk, slot), dtype=np.uint8)
-    perm = rng.permutation(nblk)
-    bt = np.zeros((B, max(pages)), np.int32)
-    k = 0
-    for b in range(B):
-        bt[b, : pages[b]] = perm[k : k + pages[b]]
-        k += pages[b]
-    cents = tqb.get_centroids(128, 4).numpy()
-    mids = tqb.get_midpoints(tqb.get_centroids(128, 4)).numpy()
-    ntok = int(sum(seq_lens))
-    slots = np.concatenate([bt[b, np.arange(n) // 16] * 16 + np.arange(n) % 16 for b, n in enumerate(seq_lens)]).astype(np.int32)
-    key = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
-    norms = np.linalg.norm(key, axis=1).astype(np.float32)
-    R = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
-    y = ((key / (norms[:, None] + 1e-8)) @ R).astype(np.float32)
-    val = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
-    O.store(O.LAYOUT_SOA, y, norms, val, mids, cents, slots, cache, norm_correction=True)
-    q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
-    return dict(q_rot=q, kv_cache=cache, block_table=bt, seq_lens=np.asarray(seq_lens, np.int32),
-                centroids=cents)
-
-
 @pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8), (8, 1), (16, 2), (24, 8), (6, 2), (4, 4),
                                    (48, 16), (12, 3), (40, 8), (10, 5), (28, 4)])
 def test_gqa_shapes_vs_oracle(cuda_device, hq, hk):
-    z = _random_case(hq * 100 + hk, 3, hq, hk, [300, 17, 1024])
+    z = random_case(hq * 100 + hk, 3, hq, hk, [300, 17, 1024])
     S = 5
     ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S)
     _check(_run(cuda_device, z, S=S), ref, f"GQA {hq}/{hk}")
@@ -137,7 +108,7 @@ def test_gqa_shapes_vs_oracle(cuda_device, hq, hk):
 
 def test_ragged_per_sequence_splits(cuda_device):
     lens = [512, 1, 16, 17, 4000, 777, 33, 1500]
-    z = _random_case(5, len(lens), 32, 8, lens)
+    z = random_case(5, len(lens), 32, 8, lens)
     nsp = L.splits_per_sequence(lens, 512, 32)
     nsp[3] = 4  # 17 tokens in 4 splits of 5: the last split holds 2 tokens
     S = 32
@@ -149,7 +120,7 @@ def test_ragged_per_sequence_splits(cuda_device):
 def test_long_split_reloads_block_ids(cuda_device):
     """A split spanning > 32 pages exercises the block-id window refill."""
     lens = [16 * 70 + 5, 16 * 33]
-    z = _random_case(9, 2, 32, 8, lens)
+    z = random_case(9, 2, 32, 8, lens)
     ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], 1)
     _check(_run(cuda_device, z, S=1), ref, "long split")
 
@@ -157,7 +128,7 @@ def test_long_split_reloads_block_ids(cuda_device):
 def test_strided_views(cuda_device):
     """Non-contiguous q/mid_o views and a block stride larger than the block
     (a cache carved out of a bigger allocation)."""
-    z = _random_case(3, 2, 32, 8, [200, 70])
+    z = random_case(3, 2, 32, 8, [200, 70])
     dev = cuda_device
     nb = z["kv_cache"].shape[0]
     big = torch.zeros(nb, 17152 + 256, dtype=torch.uint8, device=dev)
@@ -179,7 +150,7 @@ def test_strided_views(cuda_device):
 def test_large_magnitudes(cuda_device):
     """Query magnitudes far from 1 (power-of-two scaling keeps the fp16
     operand split exact) and large V scales."""
-    z = _random_case(21, 2, 32, 8, [256, 100])
+    z = random_case(21, 2, 32, 8, [256, 100])
     S = 4
     for scale in (1e-3, 30.0):
         z2 = dict(z, q_rot=(z["q_rot"] * scale).astype(np.float32))
