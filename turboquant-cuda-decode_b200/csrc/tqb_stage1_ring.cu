@@ -10,7 +10,7 @@
 //    (b, s, KV head; head fastest), one item per compute warp, so with Hk = 8
 //    the 8 warps share every page of one (b, s) split.
 //  * The producer warp moves each page of the tile into a kStages-deep
-//    shared-memory ring with TMA (no multicast): one cp.async.bulk.tensor of
+//    shared-memory ring with TMA (CTA-local loads only): one cp.async.bulk.tensor of
 //    the tile's head slices (a 4-D tensor map over [block][head][token][128 B]
 //    with a box of {128 B, 16 tokens, 8 heads}; narrower runs use boxes of
 //    4/2/1 heads) plus one cp.async.bulk of their metadata, all completing on
