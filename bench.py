@@ -381,38 +381,60 @@ def main():
     out = torch.empty(B, Hq, 128, device=dev)
     lse = torch.empty(B, Hq, device=dev)
 
-    def step():
+    def stage1_call():
         tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, layout=args.layout)
+
+    def step():
+        stage1_call()
         tqb.stage2(mid, w["seq_lens"], out, lse)
+
+    # The decode step is captured once as a CUDA graph (as a serving engine
+    # launches it) and replayed: the timed region holds the GPU work without
+    # the Python argument marshalling between launches.  Stage1 alone is
+    # timed the same way for the roofline.
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap):
+        step()
+        torch.cuda.synchronize(dev)
+        g_step, g_s1 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=cap):
+            step()
+        with torch.cuda.graph(g_s1, stream=cap):
+            stage1_call()
+    torch.cuda.synchronize(dev)
 
     clocks = ClockSampler(dev)
     clocks.start()
     for _ in range(args.warmup):
-        step()
+        g_step.replay()
     torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     K = args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     start.record()
     for i in range(K):
-        ev[i][0].record()
-        tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, layout=args.layout)
-        ev[i][1].record()
-        tqb.stage2(mid, w["seq_lens"], out, lse)
+        g_step.replay()
     end.record()
     torch.cuda.synchronize(dev)
     w1 = time.perf_counter()
     barrier(world)
+    # Stage1 alone (same inputs, K launches back to back)
+    a1, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a1.record()
+    for i in range(K):
+        g_s1.replay()
+    b1.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
     clocks.mark(w0, w1)
     clocks.stop()
     total_ms = max_over_ranks(start.elapsed_time(end), world)
-    s1_ms = [a.elapsed_time(b) for a, b in ev]
-    s1_avg_ms = max_over_ranks(statistics.mean(s1_ms), world)
+    s1_avg_ms = max_over_ranks(a1.elapsed_time(b1) / K, world)
     ms_per_step = total_ms / K
     value = world * B / (ms_per_step * 1e-3)
+    del g_step, g_s1
 
     # -- end to end through the production entry point, host buffers ------
     e2e = None
@@ -486,11 +508,14 @@ def main():
                          % (w["kv"].numel() / 1e6)},
         "stage1_us": s1_avg_ms * 1e3,
         "stage2_us": (ms_per_step - s1_avg_ms) * 1e3,
+        "timing": "CUDA-graph replay of the decode step (Stage1 + Stage2), CUDA events; stage1_us from Stage1-only replays",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
-                     "algorithmic_bytes_per_launch": alg, "kernel": "tqb stage1_kernel"},
+                     "algorithmic_bytes_per_launch": alg,
+                     "kernel": ("tqb stage1_ring_kernel (TMA page ring)" if args.layout == "soa"
+                                else "tqb stage1_kernel (register ring)")},
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "e2e": e2e,

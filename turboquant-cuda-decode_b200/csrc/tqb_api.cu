@@ -183,6 +183,8 @@ int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
     TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0 && a->num_splits > 0, TQB_ERR_INVALID_ARG,
                 "batch/heads/num_splits must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE((int64_t)a->batch * a->num_q_heads < (int64_t(1) << 31), TQB_ERR_UNSUPPORTED,
+                "batch * num_q_heads must be < 2^31");
     if (a->batch == 0) return TQB_OK;
     TQB_REQUIRE(a->mid_o && a->seq_lens && a->output && a->lse, TQB_ERR_INVALID_ARG,
                 "a required pointer is NULL");

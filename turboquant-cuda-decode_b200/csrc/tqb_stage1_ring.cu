@@ -148,19 +148,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 // Global -> shared bulk copy completing on `bar` (16-byte aligned, size a
 // multiple of 16).
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
 }
 // Tensor-map copies (global -> shared, completing on `bar`).
+// The page data is read exactly once: its copies carry an L2 evict-first
+// policy so the stream does not push the partials (mid_o, read back by
+// Stage2 right after) out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+    return pol;
+}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-        "%5}], [%6];\n" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4, %5}], [%6], %7;\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -278,6 +287,7 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
     // number of pages slot s has taken so far, `used` marks slots in use.
     uint32_t tq = 0, uses = 0, used = 0;
     bool abort = false;
+    const uint64_t stream_policy = l2_evict_first_policy();
 
     // Query rows of a tile (lanes 0-7: its items) into the query area, once
     // the compute warps have released the previous tile's rows.
@@ -364,14 +374,14 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
                     const int box = kGroupWarps >> i;
                     if (r_nw & box) {
                         tma_load_4d(dst + (uint32_t)(col + off) * kColBytes, &M.page[i], 0, 0, r_kvh + off,
-                                    (int)my_id, gs.full(slot));
+                                    (int)my_id, gs.full(slot), stream_policy);
                         off += box;
                     }
                 }
                 const uint8_t* blk = P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes;
                 bulk_g2s(dst + kMetaOff + (uint32_t)col * kMetaSlot,
                          blk + kBlockSize * tok_bytes + (uint32_t)r_kvh * kMetaSlot, (uint32_t)r_nw * kMetaSlot,
-                         gs.full(slot));
+                         gs.full(slot), stream_policy);
             }
             uses ^= 1u << slot;
             used |= 1u << slot;

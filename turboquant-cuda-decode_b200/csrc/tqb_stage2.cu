@@ -4,9 +4,8 @@
 // log-sum-exp merge over the non-empty splits of mid_o,
 //     out = sum_s w_s O_s / sum_s w_s,  w_s = exp(lse_s - max),
 //     lse = max + ln(sum_s w_s).
-// The merge reads 33.8 MB at the B64x4K workload against 0.13 MB written, so
-// it is an HBM-bound streaming pass: one warp per (b, h), each lane owning 4
-// of the 128 dims, coalesced 128-byte row reads per split.
+// The merge reads 33.8 MB at the B64x4K workload (mostly from L2, written by
+// Stage1 just before) against 1 MB written: a latency-bound streaming pass.
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -17,53 +16,58 @@ namespace tqb {
 namespace {
 
 constexpr int kWarpsPerCta = 8;
+constexpr int kFastSplits = 32;  // split counts served with all loads in flight
 
-// Two passes per (b, h) so that every load is independent of the previous
-// split's result: (1) lane s of a 32-split chunk reads LSE_s, the warp forms
-// the max and the weights w_s = exp(LSE_s - max); (2) every lane reads its 4
-// dims of all splits (unrolled, loads in flight together) and accumulates
-// w_s * O_s.  Same algebra as the reference's running merge.
-__global__ void __launch_bounds__(kWarpsPerCta * 32) stage2_kernel(const Stage2Params P) {
-    const int lane = threadIdx.x & 31;
-    const int64_t item = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-    if (item >= (int64_t)P.B * P.Hq) return;
+// One CTA of 128 threads per (b, h), thread d owning output dim d: every
+// split row is read as one coalesced 512-byte run by the CTA, and each thread
+// has all of its split loads in flight at once (the partials are mostly
+// L2-resident right after Stage1).  Two passes so that no load waits on the
+// previous split's result: (1) the maximum LSE over the non-empty splits,
+// (2) sum_s w_s O_s and sum_s w_s with w_s = exp(LSE_s - max).  Same algebra
+// as the reference's running merge.
+__global__ void __launch_bounds__(kHeadDim) stage2_kernel(const Stage2Params P) {
+    const int64_t item = blockIdx.x;  // b * Hq + h
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
+    const int d = threadIdx.x;
     const int nsp = P.nsplits ? min(__ldg(P.nsplits + b), P.S) : P.S;
     const int L = __ldg(P.seq_lens + b);
     const int split_len = nsp > 0 ? (L + nsp - 1) / nsp : 0;
+    // split s is non-empty iff split_len * s < L (its end is min(.., L))
+    const int nvalid = split_len > 0 ? min(nsp, (L + split_len - 1) / split_len) : 0;
     const float* row0 = P.mid + (int64_t)b * P.msb + (int64_t)h * P.msh;
-    auto nonempty = [&](int s) { return s < nsp && split_len * s < min(split_len * (s + 1), L); };
 
-    float gmax = -INFINITY;
-    for (int s0 = 0; s0 < nsp; s0 += 32) {
-        const int s = s0 + lane;
-        const float l = nonempty(s) ? __ldg(row0 + (int64_t)s * P.mss + kHeadDim) : -INFINITY;
-        gmax = fmaxf(gmax, warp_max_xor(l, 1, 16));
-    }
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float wsum = 0.0f;
-    for (int s0 = 0; s0 < nsp; s0 += 32) {
-        const int s = s0 + lane;
-        const bool ok = nonempty(s);
-        const float l = ok ? __ldg(row0 + (int64_t)s * P.mss + kHeadDim) : -INFINITY;
-        const float wl = ok ? expf(l - gmax) : 0.0f;
-        wsum += warp_sum_xor(wl, 1, 16);
-        const int n = min(32, nsp - s0);
-#pragma unroll 8
-        for (int k = 0; k < n; k++) {
-            const float w = __shfl_sync(0xffffffffu, wl, k);
-            const float* row = row0 + (int64_t)(s0 + k) * P.mss;
+    float gmax = -INFINITY, acc = 0.0f, wsum = 0.0f;
+    if (nvalid <= kFastSplits) {
+        // Every load in flight at once: kFastSplits predicated (LSE, O) pairs.
+        float ls[kFastSplits], os[kFastSplits];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float v = __ldg(row + lane + 32 * j);
-                acc[j] += w * (w != 0.0f ? v : 0.0f);
-            }
+        for (int s = 0; s < kFastSplits; s++) {
+            const float* row = row0 + (int64_t)s * P.mss;
+            ls[s] = s < nvalid ? __ldg(row + kHeadDim) : -INFINITY;
+            os[s] = s < nvalid ? __ldg(row + d) : 0.0f;
+        }
+#pragma unroll
+        for (int s = 0; s < kFastSplits; s++) gmax = fmaxf(gmax, ls[s]);
+#pragma unroll
+        for (int s = 0; s < kFastSplits; s++) {
+            const float w = s < nvalid ? expf(ls[s] - gmax) : 0.0f;
+            acc += w * os[s];
+            wsum += w;
+        }
+    } else {
+#pragma unroll 16
+        for (int s = 0; s < nvalid; s++) gmax = fmaxf(gmax, __ldg(row0 + (int64_t)s * P.mss + kHeadDim));
+#pragma unroll 16
+        for (int s = 0; s < nvalid; s++) {
+            const float* row = row0 + (int64_t)s * P.mss;
+            const float w = expf(__ldg(row + kHeadDim) - gmax);
+            acc += w * __ldg(row + d);
+            wsum += w;
         }
     }
     float* out = P.out + (int64_t)b * P.osb + (int64_t)h * P.osh;
-#pragma unroll
-    for (int j = 0; j < 4; j++) out[lane + 32 * j] = __fdiv_rn(acc[j], wsum);
-    if (lane == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
+    out[d] = __fdiv_rn(acc, wsum);
+    if (d == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
 }
 
 // Cross-GPU merge of G (O, LSE) partials laid out [G, B, Hq, D+1]; parts
@@ -98,8 +102,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) merge_kernel(const MergePar
 int launch_stage2(const Stage2Params& P, cudaStream_t stream) {
     const int64_t items = (int64_t)P.B * P.Hq;
     if (items == 0) return TQB_OK;
-    const int64_t grid = (items + kWarpsPerCta - 1) / kWarpsPerCta;
-    stage2_kernel<<<(unsigned)grid, kWarpsPerCta * 32, 0, stream>>>(P);
+    stage2_kernel<<<(unsigned)items, kHeadDim, 0, stream>>>(P);
     return report_launch(cudaGetLastError());
 }
 
