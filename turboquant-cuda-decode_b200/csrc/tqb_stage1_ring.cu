@@ -233,7 +233,8 @@ __device__ __forceinline__ bool decode_item(const Stage1Params& P, uint32_t item
     const int nsp = P.nsplits ? min(__ldg(P.nsplits + r.b), P.S) : P.S;
     if (r.s >= nsp) return false;
     const int L = min(__ldg(P.seq_lens + r.b), P.max_blocks * kBlockSize);
-    const int split_len = (L + nsp - 1) / nsp;
+    // ceil(L / nsp); the uniform split count divides by its invariant divisor
+    const int split_len = P.nsplits ? (L + nsp - 1) / nsp : (int)P.div_s.div((uint32_t)(L + nsp - 1));
     r.start = split_len * r.s;
     r.end = min(r.start + split_len, L);
     return r.start < r.end;
@@ -467,27 +468,32 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     const float vz0 = va ? half_bits_to_float(vzp) : 0.0f;
     const float vz1 = vb ? half_bits_to_float(vzp >> 16) : 0.0f;
 
-    // -- online softmax (exp2 domain), lazy reference max --
+    // -- online softmax (exp2 domain), lazy reference max: a page is weighted
+    //    against the running reference m_run while no score exceeds it by
+    //    more than kLazy (log2 units) and no weight leaves fp16; only then is
+    //    the exact row max formed (three shuffles) and the state rescaled.
     uint32_t bw0[NT], bw1[NT];
     float alpha[NT];
     bool rescale = false;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
+        // columns 2c / 2c+1: Q_hi / Q_lo parts of head c; rows g / g+8:
+        // C_hi / C_lo parts of the token
         const float d0 = (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
         const float d1 = (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
         float s0 = d0 * kn0 * st.kfac[nt];
         float s1 = d1 * kn1 * st.kfac[nt];
         s0 = va ? s0 : -INFINITY;
         s1 = vb ? s1 : -INFINITY;
-        const float tmax = warp_max_xor(fmaxf(s0, s1), 4, 16);
         const float mold = st.m_run[nt];
-        float mref = tmax > mold + kLazy ? tmax : mold;
-        float mref_e = mref == -INFINITY ? 0.0f : mref;
-        float p0 = ex2(s0 - mref_e), p1 = ex2(s1 - mref_e);
+        const float mold_e = mold == -INFINITY ? 0.0f : mold;
+        float p0 = ex2(s0 - mold_e), p1 = ex2(s1 - mold_e);
         float w0 = p0 * vs0, w1 = p1 * vs1;
-        if (__any_sync(0xffffffffu, fmaxf(w0, w1) > kWMax)) {
-            mref = fmaxf(mold, tmax);
-            mref_e = mref == -INFINITY ? 0.0f : mref;
+        float mref = mold;
+        const bool over = fmaxf(s0, s1) > mold + kLazy || fmaxf(w0, w1) > kWMax;
+        if (__any_sync(0xffffffffu, over)) {
+            mref = fmaxf(mold, warp_max_xor(fmaxf(s0, s1), 4, 16));
+            const float mref_e = mref == -INFINITY ? 0.0f : mref;
             p0 = ex2(s0 - mref_e);
             p1 = ex2(s1 - mref_e);
             w0 = p0 * vs0;
