@@ -166,6 +166,29 @@ const char* tqb_strerror(int status);
 const char* tqb_last_error_detail(void);
 int tqb_version(void);
 
+/*
+ * Allocation-free decode (no reference counterpart): Stage1 + Stage2 with
+ * the split partials kept in a static device buffer of the library instead
+ * of a caller-provided mid_o (stage1.mid_o and its strides are ignored).
+ * For callers that cannot allocate per call: a C or C++ host without a
+ * caching allocator (cudaMalloc/cudaFree synchronise the device on every
+ * step) and serving loops whose device memory is planned up front.
+ * Limit: batch * num_q_heads * num_splits <= 8192 (a 4 MiB buffer per
+ * device); larger calls return TQB_ERR_UNSUPPORTED.  The buffer address is
+ * looked up on the first call on each device; make that first call before
+ * any stream capture.  Calls that overlap on one device share the buffer
+ * and race: serialise them.
+ */
+typedef struct tqb_decode_static_args {
+    tqb_stage1_args stage1;      /* as for tqb_stage1; mid_o fields ignored */
+    float* output;               /* [B, Hq, D] */
+    int64_t out_stride_b, out_stride_h;
+    float* lse;                  /* [B, Hq] */
+    int64_t lse_stride_b;
+} tqb_decode_static_args;
+
+int tqb_decode_static(const tqb_decode_static_args* args, cudaStream_t stream);
+
 /* Diagnostics (no reference counterpart).  The SoA Stage1 kernel paces its
  * TMA page ring with mbarrier waits that give up after about a second; each
  * wait that gives up adds one to a per-device counter (the kernel then ends

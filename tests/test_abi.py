@@ -95,6 +95,7 @@ int main(void) {
   printf("tqb_stage2_args %zu\n", sizeof(tqb_stage2_args));
   printf("tqb_merge_args %zu\n", sizeof(tqb_merge_args));
   printf("tqb_store_args %zu\n", sizeof(tqb_store_args));
+  printf("tqb_decode_static_args %zu\n", sizeof(tqb_decode_static_args));
   %FIELDS%
   return 0;
 }
@@ -103,7 +104,8 @@ int main(void) {
 
 def test_ctypes_structs_match_c_layout(tmp_path: Path):
     structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
-               "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs}
+               "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs,
+               "tqb_decode_static_args": _lib.DecodeStaticArgs}
     fields = "\n".join(f"F({c}, {f})" for c, py in structs.items() for f, _ in py._fields_)
     src = tmp_path / "probe.c"
     src.write_text(C_LAYOUT_PROBE.replace("%FIELDS%", fields))

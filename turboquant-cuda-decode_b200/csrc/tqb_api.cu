@@ -64,6 +64,8 @@ int sm_count() {
 }  // namespace
 
 namespace tqb {
+void set_error_detail(const char* msg) { snprintf(g_detail, sizeof(g_detail), "%s", msg); }
+
 int report_launch(cudaError_t e) {
     if (e == cudaSuccess) return TQB_OK;
     snprintf(g_detail, sizeof(g_detail), "kernel launch: %s", cudaGetErrorString(e));

@@ -83,6 +83,8 @@ struct StoreParams {
 // Records the CUDA error text for tqb_last_error_detail(); returns
 // TQB_OK or TQB_ERR_LAUNCH.
 int report_launch(cudaError_t e);
+// Sets the text tqb_last_error_detail() returns on this thread.
+void set_error_detail(const char* msg);
 
 int launch_stage1(const Stage1Params& p, cudaStream_t stream, int num_sms);
 // SoA Stage1 fed by the TMA page ring (tqb_stage1_ring.cu); supported when

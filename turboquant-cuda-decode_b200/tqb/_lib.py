@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "tqb_last_error_detail",
     "tqb_version",
     "tqb_wait_timeouts",
+    "tqb_decode_static",
 )
 
 
@@ -89,6 +90,17 @@ class Stage2Args(ctypes.Structure):
     ]
 
 
+class DecodeStaticArgs(ctypes.Structure):
+    """``tqb_decode_static_args``: Stage1 arguments (mid_o ignored) plus the
+    Stage2 outputs."""
+
+    _fields_ = [
+        ("stage1", Stage1Args),
+        ("output", _vp), ("out_stride_b", _i64), ("out_stride_h", _i64),
+        ("lse", _vp), ("lse_stride_b", _i64),
+    ]
+
+
 class MergeArgs(ctypes.Structure):
     _fields_ = [
         ("partials", _vp), ("num_parts", _i32), ("batch", _i32), ("num_q_heads", _i32),
@@ -137,6 +149,8 @@ def load() -> ctypes.CDLL:
             lib.tqb_version.restype = ctypes.c_int
             lib.tqb_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
             lib.tqb_wait_timeouts.restype = ctypes.c_int
+            lib.tqb_decode_static.argtypes = [ctypes.POINTER(DecodeStaticArgs), _vp]
+            lib.tqb_decode_static.restype = ctypes.c_int
             _lib = lib
     return _lib
 
