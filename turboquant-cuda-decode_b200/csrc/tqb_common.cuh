@@ -78,12 +78,29 @@ __device__ __forceinline__ float warp_sum_xor(float v, int from, int to) {
 
 // Power-of-two exponent e such that max_abs * 2^e lies in [2^14, 2^15):
 // scaling fp16 operands this way keeps hi/lo splits away from both overflow
-// and the subnormal range.  Returns 0 for 0/non-finite inputs.
+// and the subnormal range.  Read from the exponent bits (for a normal
+// max_abs = m * 2^(E-126), m in [0.5, 1), e = 15 - (E - 126)); 0 for zero and
+// non-finite inputs; clamped to [-100, 100] (a subnormal max_abs).
 __device__ __forceinline__ int fp16_scale_exp(float max_abs) {
-    if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
-    int e;
-    frexpf(max_abs, &e);  // max_abs = m * 2^e, m in [0.5, 1)
-    return 15 - e;
+    const int be = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu);
+    if (!(max_abs > 0.0f) || be == 0xFF) return 0;
+    const int e = 15 - (be - 126);
+    return e < -100 ? -100 : (e > 100 ? 100 : e);
+}
+
+// 2^e for integer e in [-126, 127], built from the exponent bits.
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// Hardware reciprocal and base-2 logarithm (relative error about 2^-23).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
 }  // namespace tqb

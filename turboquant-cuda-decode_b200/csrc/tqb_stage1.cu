@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
 #pragma unroll
     for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     const int ec = fp16_scale_exp(cmax);
-    const float cscale = ldexpf(1.0f, ec);
+    const float cscale = exp2i(ec);
     for (int e = tid; e < 256 * kCopies; e += kThreads) {
         const int byte = e / kCopies;
         const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
             }
             amax = warp_max_xor(amax, 1, 2);
             const int eq = fp16_scale_exp(amax);
-            const float qscale = ldexpf(1.0f, eq);
+            const float qscale = exp2i(eq);
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
             // Score factor of this lane's softmax head (c + 4 nt), whose
             // scale exponent lives on lane 8c.
             const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
-            st.kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
+            st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
             st.m_run[nt] = -INFINITY;
             st.l_part[nt] = 0.0f;
             st.z_part[nt] = 0.0f;
@@ -546,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
             float l = warp_sum_xor(st.l_part[nt], 4, 16);
             l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
             const float z = warp_sum_xor(st.z_part[nt], 4, 16);
-            const float inv = __frcp_rn(l);
+            const float inv = rcp_approx(l);
             const int hl = c + 4 * nt;
             float* row = stage + hl * (kHeadDim + 1);
             if (hl < P.G) {
@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
                     row[16 * g + 2 * i] = lo * inv;
                     row[16 * g + 2 * i + 1] = hi * inv;
                 }
-                if (g == 0) row[kHeadDim] = st.m_run[nt] * kLn2 + logf(l);
+                if (g == 0) row[kHeadDim] = (st.m_run[nt] + lg2_approx(l)) * kLn2;
             }
         }
         __syncwarp();

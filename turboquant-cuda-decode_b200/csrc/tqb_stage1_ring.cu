@@ -624,7 +624,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
             }
             amax = warp_max_xor(amax, 1, 2);
             const int eq = fp16_scale_exp(amax);
-            const float qscale = ldexpf(1.0f, eq);
+            const float qscale = exp2i(eq);
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
@@ -633,7 +633,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
                 st.qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
             }
             const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
-            st.kfac[nt] = P.attn_scale * kLog2e * ldexpf(1.0f, -(eq_head + ec));
+            st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
             st.m_run[nt] = -INFINITY;
             st.l_part[nt] = 0.0f;
             st.z_part[nt] = 0.0f;
@@ -668,7 +668,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
             float l = warp_sum_xor(st.l_part[nt], 4, 16);
             l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
             const float z = warp_sum_xor(st.z_part[nt], 4, 16);
-            const float inv = __frcp_rn(l);
+            const float inv = rcp_approx(l);
             const int hl = c + 4 * nt;
             if (hl < P.G) {
                 float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + hl) * P.msh + (int64_t)s * P.mss;
@@ -677,7 +677,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
                     dst[16 * g + 2 * i] = ((st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale + z) * inv;
                     dst[16 * g + 2 * i + 1] = ((st.acc[nt][i][2] + st.acc[nt][i][3]) * kCodeScale + z) * inv;
                 }
-                if (g == 0) dst[kHeadDim] = st.m_run[nt] * kLn2 + logf(l);
+                if (g == 0) dst[kHeadDim] = (st.m_run[nt] + lg2_approx(l)) * kLn2;
             }
         }
     }
@@ -695,7 +695,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
 #pragma unroll
     for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     const int ec = fp16_scale_exp(cmax);
-    const float cscale = ldexpf(1.0f, ec);
+    const float cscale = exp2i(ec);
     for (int e = tid; e < 256 * kLutCopies; e += C::kThreads) {
         const int byte = e / kLutCopies;
         const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
