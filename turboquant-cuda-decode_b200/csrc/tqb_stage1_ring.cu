@@ -546,12 +546,55 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     }
 }
 
+// Partial output rows of one item: lane (g, c) holds dims 16g .. 16g+15 of
+// head c + 4 nt.  They are staged in this warp's 2 KB column of its last ring
+// slot as [4 heads][128] fp32 (16-byte chunk j of head h at chunk j ^ h:
+// conflict-free both ways) and written back as 128-byte coalesced runs.
+template <int NT>
+__device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<NT>& st, uint32_t col, int b, int s,
+                                         int kvh, int g, int c, int lane) {
+    constexpr float kCodeScale = 1048576.0f;  // 2^20: undo the subnormal code scale
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        float l = warp_sum_xor(st.l_part[nt], 4, 16);
+        l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
+        const float z = warp_sum_xor(st.z_part[nt], 4, 16);
+        const float inv = rcp_approx(l);
+        auto val = [&](int i, int hi) {
+            return (((hi ? st.acc[nt][i][2] + st.acc[nt][i][3] : st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale +
+                     z) * inv);
+        };
+#pragma unroll
+        for (int j = 0; j < 4; j++)  // dims 16g + 4j .. 16g + 4j + 3
+            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(
+                             col + (uint32_t)c * 512u + ((uint32_t)((4 * g + j) ^ c) << 4)),
+                         "f"(val(2 * j, 0)), "f"(val(2 * j, 1)), "f"(val(2 * j + 1, 0)), "f"(val(2 * j + 1, 1))
+                         : "memory");
+        __syncwarp();
+        const int heads = min(4, P.G - 4 * nt);
+        for (int hl = 0; hl < heads; hl++) {
+            float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + 4 * nt + hl) * P.msh + (int64_t)s * P.mss;
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                dst[32 * q + lane] =
+                    __uint_as_float(lds32(col + (uint32_t)hl * 512u + ((uint32_t)((8 * q + (lane >> 2)) ^ hl) << 4) +
+                                          4u * (lane & 3)));
+        }
+        if (g == 0 && c + 4 * nt < P.G) {
+            float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + c + 4 * nt) * P.msh + (int64_t)s * P.mss;
+            dst[kHeadDim] = (st.m_run[nt] + lg2_approx(l)) * kLn2;
+        }
+        __syncwarp();  // the column is rewritten by the next n-tile
+    }
+}
+
 // One page from ring slot S (a compile-time constant, so every shared and
 // barrier address below is a register plus an immediate).
 template <int NT, int S>
 __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
                                           int k, int my_np, int w, int tok_first, int start, int end,
-                                          uint32_t lut_sel_src, int g, int c, int src_a, int lane) {
+                                          uint32_t lut_sel_src, int g, int c, int src_a, int lane,
+                                          bool release) {
     constexpr int NS = Cfg<NT>::kStages;
     if (!mbar_wait(gs.full(S), (cbits >> S) & 1u)) return false;
     cbits ^= 1u << S;
@@ -561,7 +604,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
                       lut_sel_src, g, c, src_a);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(gs.empty<NS>(S));
+    if (release && lane == 0) mbar_arrive(gs.empty<NS>(S));
     return true;
 }
 
@@ -648,38 +691,25 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
         const int tok_first = (start / kBlockSize) * kBlockSize + tau;
+        // The last page's slot is released after the epilogue, which stages
+        // the output rows in this warp's column of that slot.
         for (int k = 0; k < np_tile; k += NS) {
             if (!page_step<NT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a,
-                                  lane))
+                                  lane, k + 1 < np_tile))
                 return;
             if (k + 1 < np_tile && !page_step<NT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a, lane))
+                                                     lut_sel_src, g, c, src_a, lane, k + 2 < np_tile))
                 return;
             if (k + 2 < np_tile && !page_step<NT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a, lane))
+                                                     lut_sel_src, g, c, src_a, lane, k + 3 < np_tile))
                 return;
         }
-        if (my_np == 0) continue;
-
-        // ---- epilogue: lane (g, c) holds dims 16g .. 16g+15 of head c + 4nt ----
-        constexpr float kCodeScale = 1048576.0f;  // 2^20: undo the subnormal code scale
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            float l = warp_sum_xor(st.l_part[nt], 4, 16);
-            l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
-            const float z = warp_sum_xor(st.z_part[nt], 4, 16);
-            const float inv = rcp_approx(l);
-            const int hl = c + 4 * nt;
-            if (hl < P.G) {
-                float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + hl) * P.msh + (int64_t)s * P.mss;
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    dst[16 * g + 2 * i] = ((st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale + z) * inv;
-                    dst[16 * g + 2 * i + 1] = ((st.acc[nt][i][2] + st.acc[nt][i][3]) * kCodeScale + z) * inv;
-                }
-                if (g == 0) dst[kHeadDim] = (st.m_run[nt] + lg2_approx(l)) * kLn2;
-            }
-        }
+        const int last_slot = (np_tile - 1) % NS;
+        if (my_np > 0) epilogue<NT>(P, st, gs.stage(last_slot) + (uint32_t)w * kColBytes, b, s, kvh, g, c, lane);
+        // generic-proxy writes to the slot, then the producer's TMA: fence, release
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(gs.empty<NS>(last_slot));
     }
 }
 
