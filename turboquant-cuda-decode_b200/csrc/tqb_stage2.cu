@@ -16,19 +16,21 @@ namespace tqb {
 namespace {
 
 constexpr int kWarpsPerCta = 8;
-constexpr int kFastSplits = 32;  // split counts served with all loads in flight
+constexpr int kSplitsPerPass = 8;  // splits whose loads a warp keeps in flight at once
 
-// One CTA of 128 threads per (b, h), thread d owning output dim d: every
-// split row is read as one coalesced 512-byte run by the CTA, and each thread
-// has all of its split loads in flight at once (the partials are mostly
-// L2-resident right after Stage1).  Two passes so that no load waits on the
-// previous split's result: (1) the maximum LSE over the non-empty splits,
-// (2) sum_s w_s O_s and sum_s w_s with w_s = exp(LSE_s - max).  Same algebra
-// as the reference's running merge.
-__global__ void __launch_bounds__(kHeadDim) stage2_kernel(const Stage2Params P) {
+// One CTA of 4 warps per (b, h).  Warp w merges the non-empty splits
+// s = w, w + 4, w + 8, ... of (b, h): lane l owns dims l, l+32, l+64, l+96,
+// so each split row is read as four coalesced 128-byte runs, and the warp
+// issues the loads of up to kSplitsPerPass splits before using any of them.
+// The four warps' (max, sum, acc) then combine through shared memory.  Same
+// log-sum-exp algebra as the reference's running merge.
+__global__ void __launch_bounds__(kHeadDim, 8) stage2_kernel(const Stage2Params P) {
+    constexpr int kParts = kHeadDim / 32;  // warps per CTA
+    __shared__ float s_acc[kParts][kHeadDim];
+    __shared__ float s_max[kParts], s_sum[kParts];
     const int64_t item = blockIdx.x;  // b * Hq + h
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
-    const int d = threadIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nsp = P.nsplits ? min(__ldg(P.nsplits + b), P.S) : P.S;
     const int L = __ldg(P.seq_lens + b);
     const int split_len = nsp > 0 ? (L + nsp - 1) / nsp : 0;
@@ -36,37 +38,53 @@ __global__ void __launch_bounds__(kHeadDim) stage2_kernel(const Stage2Params P) 
     const int nvalid = split_len > 0 ? min(nsp, (L + split_len - 1) / split_len) : 0;
     const float* row0 = P.mid + (int64_t)b * P.msb + (int64_t)h * P.msh;
 
-    float gmax = -INFINITY, acc = 0.0f, wsum = 0.0f;
-    if (nvalid <= kFastSplits) {
-        // Every load in flight at once: kFastSplits predicated (LSE, O) pairs.
-        float ls[kFastSplits], os[kFastSplits];
+    float m = -INFINITY, sum = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int s0 = warp; s0 < nvalid; s0 += kParts * kSplitsPerPass) {
+        float ls[kSplitsPerPass], os[kSplitsPerPass][4];
 #pragma unroll
-        for (int s = 0; s < kFastSplits; s++) {
+        for (int k = 0; k < kSplitsPerPass; k++) {
+            const int s = s0 + kParts * k;
             const float* row = row0 + (int64_t)s * P.mss;
-            ls[s] = s < nvalid ? __ldg(row + kHeadDim) : -INFINITY;
-            os[s] = s < nvalid ? __ldg(row + d) : 0.0f;
-        }
+            ls[k] = s < nvalid ? __ldg(row + kHeadDim) : -INFINITY;
 #pragma unroll
-        for (int s = 0; s < kFastSplits; s++) gmax = fmaxf(gmax, ls[s]);
+            for (int j = 0; j < 4; j++) os[k][j] = s < nvalid ? __ldg(row + lane + 32 * j) : 0.0f;
+        }
+        float mn = m;
 #pragma unroll
-        for (int s = 0; s < kFastSplits; s++) {
-            const float w = s < nvalid ? expf(ls[s] - gmax) : 0.0f;
-            acc += w * os[s];
-            wsum += w;
+        for (int k = 0; k < kSplitsPerPass; k++) mn = fmaxf(mn, ls[k]);
+        const float scale = m == -INFINITY ? 0.0f : expf(m - mn);
+        sum *= scale;
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[j] *= scale;
+#pragma unroll
+        for (int k = 0; k < kSplitsPerPass; k++) {
+            const float w = ls[k] == -INFINITY ? 0.0f : expf(ls[k] - mn);
+            sum += w;
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[j] += w * os[k][j];
         }
-    } else {
-#pragma unroll 16
-        for (int s = 0; s < nvalid; s++) gmax = fmaxf(gmax, __ldg(row0 + (int64_t)s * P.mss + kHeadDim));
-#pragma unroll 16
-        for (int s = 0; s < nvalid; s++) {
-            const float* row = row0 + (int64_t)s * P.mss;
-            const float w = expf(__ldg(row + kHeadDim) - gmax);
-            acc += w * __ldg(row + d);
-            wsum += w;
-        }
+        m = mn;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) s_acc[warp][lane + 32 * j] = acc[j];
+    if (lane == 0) {
+        s_max[warp] = m;
+        s_sum[warp] = sum;
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    float gmax = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < kParts; p++) gmax = fmaxf(gmax, s_max[p]);
+    float o = 0.0f, wsum = 0.0f;
+#pragma unroll
+    for (int p = 0; p < kParts; p++) {
+        const float w = s_max[p] == -INFINITY ? 0.0f : expf(s_max[p] - gmax);
+        o += w * s_acc[p][d];
+        wsum += w * s_sum[p];
     }
     float* out = P.out + (int64_t)b * P.osb + (int64_t)h * P.osh;
-    out[d] = __fdiv_rn(acc, wsum);
+    out[d] = __fdiv_rn(o, wsum);
     if (d == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
 }
 
