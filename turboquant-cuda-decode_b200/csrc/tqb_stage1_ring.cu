@@ -537,8 +537,8 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         const uint32_t x2 = wi ? v[2].y : v[2].x;
         const uint32_t x3 = wi ? v[3].y : v[3].x;
         const uint32_t p01 = prmt(x0, x1, sel), p23 = prmt(x2, x3, sel);
-        const uint32_t a0 = (p01 << 4) & 0x00F000F0u;
-        const uint32_t a1 = p01 & 0x00F000F0u;
+        const uint32_t a0 = (p01 << 4) & 0x00F000F0u;  // row g:   low nibble
+        const uint32_t a1 = p01 & 0x00F000F0u;         // row g+8: high nibble
         const uint32_t a2 = (p23 << 4) & 0x00F000F0u;
         const uint32_t a3 = p23 & 0x00F000F0u;
 #pragma unroll
@@ -649,31 +649,40 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         ItemState<NT> st;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
+            // Lanes g and g^1 share a head and dims 32c .. 32c+31 but keep the
+            // hi (even g) or lo (odd g) parts: each converts 16 of the 32
+            // floats and the pair swaps the halves the other keeps.
             const int hl = (g >> 1) + 4 * nt;
-            float qv[32];
+            const bool odd = g & 1;
+            float qv[16];
             float amax = 0.0f;
             if (my_np > 0 && hl < P.G) {
-                const uint32_t qa = gs.qarea + (uint32_t)(w * C::kHeadsPerWarp + hl) * kQRowBytes + 128u * c;
+                const uint32_t qa = gs.qarea + (uint32_t)(w * C::kHeadsPerWarp + hl) * kQRowBytes + 128u * c +
+                                    (odd ? 64u : 0u);
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < 4; j++) {
                     const float4 f = lds_f4(qa + 16u * j);
                     qv[4 * j] = f.x; qv[4 * j + 1] = f.y; qv[4 * j + 2] = f.z; qv[4 * j + 3] = f.w;
                 }
 #pragma unroll
-                for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(qv[j]));
+                for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(qv[j]));
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; j++) qv[j] = 0.0f;
+                for (int j = 0; j < 16; j++) qv[j] = 0.0f;
             }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
             amax = warp_max_xor(amax, 1, 2);
             const int eq = fp16_scale_exp(amax);
             const float qscale = exp2i(eq);
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
+            for (int j = 0; j < 8; j++) {
                 const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
                 const __half2 h = __floats2half2_rn(x0, x1);
                 const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-                st.qf[nt][j] = (g & 1) ? h2_as_u32(l) : h2_as_u32(h);
+                const uint32_t keep = odd ? h2_as_u32(l) : h2_as_u32(h);
+                const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? h2_as_u32(h) : h2_as_u32(l), 4);
+                st.qf[nt][j] = odd ? got : keep;      // fragments 0-7: floats of the even lane
+                st.qf[nt][8 + j] = odd ? keep : got;  // fragments 8-15: floats of the odd lane
             }
             const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
             st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
