@@ -138,9 +138,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     const long long t0 = clock64();
-    while (true) {
+    for (uint32_t i = 1;; i++) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-        if (__any_sync(0xffffffffu, clock64() - t0 > kWaitCycles)) {
+        // the clock bound is checked every 64 polls (each try_wait already
+        // holds the warp for a while when the phase is incomplete)
+        if ((i & 63u) == 0 && __any_sync(0xffffffffu, clock64() - t0 > kWaitCycles)) {
             if ((threadIdx.x & 31) == 0) atomicAdd(&g_wait_timeouts, 1u);
             return false;
         }
@@ -603,8 +605,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
         page_math<NT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
                       lut_sel_src, g, c, src_a);
     }
-    __syncwarp();
-    if (release && lane == 0) mbar_arrive(gs.empty<NS>(S));
+    if (release) mbar_arrive(gs.empty<NS>(S));  // all 32 lanes (no branch on the lane)
     return true;
 }
 
@@ -694,8 +695,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 #pragma unroll
                 for (int k = 0; k < 4; k++) st.acc[nt][i][k] = 0.0f;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(gs.q_empty<NS>());
+        mbar_arrive(gs.q_empty<NS>());  // all 32 lanes
         tq++;
 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
@@ -717,8 +717,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         if (my_np > 0) epilogue<NT>(P, st, gs.stage(last_slot) + (uint32_t)w * kColBytes, b, s, kvh, g, c, lane);
         // generic-proxy writes to the slot, then the producer's TMA: fence, release
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(gs.empty<NS>(last_slot));
+        mbar_arrive(gs.empty<NS>(last_slot));  // all 32 lanes
     }
 }
 
@@ -759,10 +758,10 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         gb.bars = base + C::kBarOff + (uint32_t)tid * kBarStride;
         for (int s = 0; s < C::kStages; s++) {
             mbar_init(gb.full(s), 1);
-            mbar_init(gb.template empty<C::kStages>(s), kGroupWarps);
+            mbar_init(gb.template empty<C::kStages>(s), kGroupWarps * 32);  // every compute lane arrives
         }
         mbar_init(gb.template q_full<C::kStages>(), 1);
-        mbar_init(gb.template q_empty<C::kStages>(), kGroupWarps);
+        mbar_init(gb.template q_empty<C::kStages>(), kGroupWarps * 32);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
