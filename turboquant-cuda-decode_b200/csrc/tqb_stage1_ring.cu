@@ -9,7 +9,7 @@
 //    producer warp.  The group walks "tiles" of 8 consecutive work items
 //    (b, s, KV head; head fastest), one item per compute warp, so with Hk = 8
 //    the 8 warps share every page of one (b, s) split.
-//  * The producer warp moves each page of the tile into a kStages-deep
+//  * The producer warps (two per group) move each page of the tile into a kStages-deep
 //    shared-memory ring with TMA (CTA-local loads only): one cp.async.bulk.tensor of
 //    the tile's head slices (a 4-D tensor map over [block][head][token][128 B]
 //    with a box of {128 B, 16 tokens, 8 heads}; narrower runs use boxes of
@@ -60,12 +60,14 @@ constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
 constexpr int kLutAddr = 0x10000;                              // shared address of the table
 constexpr int kDynBase = 0x400;  // shared address of dynamic shared memory (1 KB reserved below it)
 constexpr int kBarStride = 128;                                // barrier block per group
+constexpr int kProducersPerGroup = 2;  // the issue handoff is unambiguous for two
 constexpr long long kWaitCycles = 2000000000LL;                // ~1 s at 1.9 GHz
 constexpr float kLazy = 8.0f;                                  // lazy-rescale slack (log2)
 constexpr float kWMax = 32768.0f;                              // largest W on the lazy path
 
 // Warp roles: kGroups x 8 compute warps (whole warpgroups) and one producer
-// warpgroup whose warp gi feeds group gi (its other warps leave at once).
+// warpgroup whose warps feed the groups, two per group taking turns page by
+// page.
 // setmaxnreg moves registers from the producer warpgroup to the compute
 // warpgroups; the shares add up to at most the launch allocation
 // (kThreads x kLaunchRegs), so every setmaxnreg.inc can be satisfied.
@@ -97,7 +99,8 @@ struct Cfg {
     static __host__ __device__ constexpr int q_off(int gi) { return gi == 0 ? kHighOff : kHighOff + kQBytes + kRingBytes; }
     static constexpr int kSmem = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
     static_assert(kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
-    static_assert(8 * (2 * kStages + 2) + 4 * kStages <= kBarStride, "barrier block");
+    static_assert(8 * (2 * kStages + 2) + 4 * kStages + 12 <= kBarStride, "barrier block");
+    static_assert((16 * kStages + 16 + 4 * kStages + 4) % 8 == 0, "handoff barrier alignment");
     static_assert(kSmem <= 232448, "shared memory per CTA");
 };
 
@@ -270,6 +273,10 @@ struct GroupSmem {
     __device__ uint32_t q_empty() const { return bars + 16u * NS + 8; }
     template <int NS>
     __device__ uint32_t vmask(int s) const { return bars + 16u * NS + 16 + 4u * s; }
+    // Issue-order handoff between the group's producers: phase G completes
+    // when page G (counted over all tiles) has been announced on its slot.
+    template <int NS>
+    __device__ uint32_t issued() const { return bars + 16u * NS + 16 + 4u * NS + 4u; }
 };
 
 // ---------------------------------------------------------------------------
@@ -279,22 +286,32 @@ struct GroupSmem {
 // ---------------------------------------------------------------------------
 template <int NT>
 __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M, const GroupSmem& gs, int gi,
-                                        int lane) {
+                                        int lane, int pj, int npj) {
     using C = Cfg<NT>;
     constexpr int NS = C::kStages;
     const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
     const uint32_t tile_stride = gridDim.x * C::kGroups;
     const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
     const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
+    // The group's two producer warps take turns: producer pj copies the pages
+    // whose group-wide index is pj (mod 2), and producer 0 also the query rows.  Both
+    // walk every page, so the slot phases they track stay exact, and a page
+    // is announced on its slot only after the previous page was (the
+    // `issued` handoff): every slot's previous use was therefore announced,
+    // and its release before that one observed, when a producer waits for a
+    // release, so no wait can alias an older phase of the same parity.  The
+    // copies themselves are issued after the handoff and overlap.
     // Every tile starts at ring slot 0; bit s of `uses` is the parity of the
     // number of pages slot s has taken so far, `used` marks slots in use.
     uint32_t tq = 0, uses = 0, used = 0;
+    uint32_t gpage = 0;  // pages of this group so far, over all tiles
     bool abort = false;
     const uint64_t stream_policy = l2_evict_first_policy();
 
     // Query rows of a tile (lanes 0-7: its items) into the query area, once
     // the compute warps have released the previous tile's rows.
     auto issue_query = [&](const ItemInfo& x, int npx) {
+        if (pj != 0) return true;
         const uint32_t vit = __ballot_sync(0xffffffffu, npx > 0) & 0xFFu;
         if (!mbar_wait(gs.q_empty<NS>(), (tq & 1u) ^ 1u)) return false;
         if (lane == 0) mbar_arrive_tx(gs.q_full<NS>(), (uint32_t)__popc(vit) * P.G * kQRowBytes);
@@ -361,15 +378,21 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
                 if (!issue_query(irn, npn)) { abort = true; break; }
                 next_query_sent = true;
             }
-            if (!mbar_wait(gs.empty<NS>(slot), ((uses >> slot) & 1u) ^ 1u)) { abort = true; break; }
-            if (lane == 0) {
+            // strict alternation over the group's global page count: each
+            // producer's previous page is gpage - 2, so the handoff barrier is
+            // at most one phase behind the one waited for
+            const bool mine = gpage % (uint32_t)npj == (uint32_t)pj;
+            if (mine && gpage > 0 && !mbar_wait(gs.issued<NS>(), (gpage - 1) & 1u)) { abort = true; break; }
+            if (mine && !mbar_wait(gs.empty<NS>(slot), ((uses >> slot) & 1u) ^ 1u)) { abort = true; break; }
+            if (mine && lane == 0) {
                 sts32(gs.vmask<NS>(slot), vm);
                 mbar_arrive_tx(gs.full(slot), bytes);
+                mbar_arrive(gs.issued<NS>());  // page gpage announced: the next producer may go
             }
             __syncwarp();
             // Lane r < nruns copies run r: its head slices as boxes of 8/4/2/1
             // heads (one box when the run is a whole group) and its metadata.
-            if (here) {
+            if (mine && here) {
                 const uint32_t dst = gs.stage(slot);
                 int off = 0;
 #pragma unroll
@@ -388,6 +411,7 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             }
             uses ^= 1u << slot;
             used |= 1u << slot;
+            gpage++;
             if (++slot == NS) slot = 0;
         }
         if (!abort && !next_query_sent && !issue_query(irn, npn)) abort = true;
@@ -401,7 +425,7 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
         // last phase of every slot in use, then the last query rows.
         for (int sl = 0; sl < NS; sl++)
             if (((used >> sl) & 1u) && !mbar_wait(gs.full(sl), ((uses >> sl) & 1u) ^ 1u)) break;
-        if (tq > 0) mbar_wait(gs.q_full<NS>(), (tq - 1) & 1u);
+        if (pj == 0 && tq > 0) mbar_wait(gs.q_full<NS>(), (tq - 1) & 1u);
     }
 }
 
@@ -748,7 +772,9 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         return;
     }
     const bool producer = warp >= C::kComputeWarps;
-    const int gi = producer ? warp - C::kComputeWarps : warp / kGroupWarps;
+    // producer warp p of the producer warpgroup feeds group p % kGroups as its
+    // producer p / kGroups (two per group; with one group warps 2-3 idle)
+    const int gi = producer ? (warp - C::kComputeWarps) % C::kGroups : warp / kGroupWarps;
     GroupSmem gs;
     gs.ring = base + (uint32_t)C::ring_off(gi);
     gs.qarea = base + (uint32_t)C::q_off(gi);
@@ -762,6 +788,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         }
         mbar_init(gb.template q_full<C::kStages>(), 1);
         mbar_init(gb.template q_empty<C::kStages>(), kGroupWarps * 32);
+        mbar_init(gb.template issued<C::kStages>(), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
@@ -769,7 +796,8 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
 
     if (producer) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::kProducerRegs));
-        if (gi < C::kGroups) produce<NT>(P, M, gs, gi, lane);
+        const int pj = (warp - C::kComputeWarps) / C::kGroups;
+        if (pj < kProducersPerGroup) produce<NT>(P, M, gs, gi, lane, pj, kProducersPerGroup);
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::kComputeRegs));
         consume<NT>(P, gs, gi, warp % kGroupWarps, lane, ec);
