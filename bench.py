@@ -39,9 +39,21 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 CONFIGS = {
-    # name: (B, seq_len, Hq, Hk, splits)
+    # name: (B, seq_len, Hq, Hk, splits); c1 is the headline (DP, weak
+    # scaling: one c1 workload per GPU); c2-c4 are the sharded configs
+    # (fixed total work split over the GPUs: strong scaling).
     "c1": dict(B=64, L=4096, Hq=32, Hk=8, S=32,
                workload="Qwen3-4B decode Stage1+Stage2, B64 x 4096 ctx, Hq32/Hk8, D128, bs16, 32 splits"),
+    "c2": dict(B=128, Lmin=512, Lmax=16384, Hq=32, Hk=8, S=32, split_tokens=512, parallel="dp",
+               workload="ragged paged batch: B128, seq_lens U[512,16384] (seeded), Hq32/Hk8, "
+                        "splits min(32, ceil(len/512)), shuffled block pool; DP by batch (LPT-balanced)"),
+    "c3": dict(B=256, L=8192, Hq=64, Hk=8, S=32, parallel="tp",
+               workload="Llama-3-70B-shaped decode: B256 x 8192 ctx, Hq64/Hk8 (GQA-8), 32 splits; "
+                        "TP by KV head"),
+    "c4": dict(B=4, L=131072, Hq=32, Hk=8, S=128, parallel="sp",
+               workload="long-context decode: B4 x 131072 ctx, Hq32/Hk8; SP split-KV, NCCL all-gather of "
+                        "partials + merge kernel; 128 local splits per GPU (the reference config's 16 leave "
+                        "most SMs idle: 512 work items; the merge kernel combines any split count)"),
 }
 FALLBACK_HBM_GBS = 6650.0
 
@@ -324,6 +336,10 @@ def run_reference(args, world, rank):
     baseline/stage2.py:8-55).  Rank 0 only; other ranks exit without work."""
     if rank != 0:
         return
+    if args.config != "c1":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm runs the c1 headline config only"}),
+              flush=True)
+        return
     from oracle import oracle as O
 
     cfg = CONFIGS[args.config]
@@ -358,10 +374,165 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def _store_random_pages(kv, bt_row, n_tok, Hk, gen, dev, cents, mids, R):
+    """Seeded N(0,1) K/V for the first n_tok tokens of one sequence, written
+    by the sm_100a store into the pages bt_row lists."""
+    import tqb
+
+    chunk = 8192
+    tok = torch.arange(n_tok, device=dev)
+    slots = (bt_row[tok // 16].long() * 16 + tok % 16).to(torch.int32)
+    for s0 in range(0, n_tok, chunk):
+        n = min(chunk, n_tok - s0)
+        key = torch.randn(n, Hk, 128, generator=gen, device=dev)
+        val = torch.randn(n, Hk, 128, generator=gen, device=dev)
+        tqb.triton_turboquant_store(key, val, kv, slots[s0:s0 + n], R, mids, 4, 66, 4, centroids=cents,
+                                    norm_correction=True, layout="soa")
+
+
+def build_sharded(cfg: dict, seed: int, dev: torch.device, world: int, rank: int):
+    """This rank's share of a c2/c3/c4 workload (SoA cache on this GPU)."""
+    import tqb
+    from tqb import sharding
+
+    par = cfg["parallel"]
+    Hq, Hk, S = cfg["Hq"], cfg["Hk"], cfg["S"]
+    if par == "dp":
+        lens_all = np.random.default_rng(seed).integers(cfg["Lmin"], cfg["Lmax"] + 1, size=cfg["B"]).tolist()
+        mine = sharding.plan_batch(lens_all, world)[rank]
+        lens = [lens_all[b] for b in mine]
+        nsp = [min(S, math.ceil(n / cfg["split_tokens"])) for n in lens]
+        total_seqs = cfg["B"]
+    elif par == "tp":
+        kv0, kv1, q0, q1 = sharding.plan_kv_heads(Hq, Hk, world)[rank]
+        Hq, Hk = q1 - q0, kv1 - kv0
+        lens, nsp, total_seqs = [cfg["L"]] * cfg["B"], None, cfg["B"]
+    else:  # sp
+        t0, t1 = sharding.plan_sequence(cfg["L"], world)[rank]
+        lens, nsp, total_seqs = [t1 - t0] * cfg["B"], None, cfg["B"]
+    B = len(lens)
+    gen = torch.Generator(device=dev).manual_seed(seed + 7919 * rank)
+    cents = tqb.get_centroids(128, 4).to(dev)
+    mids = tqb.get_midpoints(cents)
+    R = orthogonal(seed + 1).to(dev)
+    pages = [max(1, math.ceil(n / 16)) for n in lens]
+    nblk = sum(pages)
+    perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 2 + rank)).to(torch.int32)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]]
+        k += pages[b]
+    bt = bt.to(dev)
+    kv = torch.zeros(nblk, 16, Hk, 134, dtype=torch.uint8, device=dev)
+    for b in range(B):
+        _store_random_pages(kv, bt[b], lens[b], Hk, gen, dev, cents, mids, R)
+    q_rot = (torch.randn(B, Hq, 128, generator=gen, device=dev).to(torch.bfloat16).float() @ R).contiguous()
+    torch.cuda.synchronize(dev)
+    return dict(kv=kv, bt=bt, seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev), cents=cents,
+                q_rot=q_rot, B=B, Hq=Hq, Hk=Hk, S=S, lens=lens, total_seqs=total_seqs,
+                nsplits=None if nsp is None else torch.tensor(nsp, dtype=torch.int32, device=dev))
+
+
+def run_sharded(args, world, rank, local):
+    """c2 / c3 / c4: the sharded configs, strong-scaled over the GPUs.  The
+    timed step is this rank's Stage1 + Stage2 (a CUDA graph) and, for SP, the
+    NCCL all-gather of the partials and the merge kernel; the step time is
+    the maximum over ranks."""
+    import tqb
+    from tqb import sharding
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    w = build_sharded(cfg, args.seed, dev, world, rank)
+    B, Hq, S = w["B"], w["Hq"], w["S"]
+    mid = torch.empty(B, Hq, S, 129, device=dev)
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    part = torch.empty(B, Hq, 129, device=dev)
+    fout = torch.empty(B, Hq, 128, device=dev)
+    flse = torch.empty(B, Hq, device=dev)
+
+    def local_step():
+        tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, num_splits_per_seq=w["nsplits"])
+        tqb.stage2(mid, w["seq_lens"], out, lse, num_splits_per_seq=w["nsplits"])
+
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap):
+        local_step()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            local_step()
+    torch.cuda.synchronize(dev)
+
+    def step():
+        g.replay()
+        if cfg["parallel"] == "sp":
+            part[..., :128] = out
+            part[..., 128] = lse
+            parts = sharding.gather_partials(part)
+            tqb.merge_partials(parts, fout, flse)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    K = args.steps
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        step()
+    b_.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b_) / K, world)
+    a1, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mid2 = torch.empty_like(mid)
+    a1.record()
+    for _ in range(K):
+        tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid2, num_splits_per_seq=w["nsplits"])
+    b1.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    s1_ms = max_over_ranks(a1.elapsed_time(b1) / K, world)
+    cache_bytes = sum(w["lens"]) * w["Hk"] * 134
+    if rank == 0:
+        peak, peak_kind = measured_peak_hbm()
+        line = {
+            "metric": "decode_tokens_per_s", "value": w["total_seqs"] / (ms * 1e-3), "unit": "tok/s",
+            "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (4-bit K/V codes)",
+            "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store)",
+            "config": {"workload": cfg["workload"], "layout": "soa", "global_batch": w["total_seqs"],
+                       "parallelism": f"{cfg['parallel']}{world}", "rank0_batch": B, "rank0_heads": Hq,
+                       "rank0_cache_bytes": cache_bytes},
+            "stage1_us_max_over_ranks": s1_ms * 1e3,
+            "rank0_stage1_hbm_gbs": cache_bytes / (s1_ms * 1e-3) / 1e9,
+            "rank0_stage1_frac_of_peak": cache_bytes / (s1_ms * 1e-3) / 1e9 / peak,
+            "peak_source": peak_kind,
+            "timing": "step = CUDA-graph replay of the local Stage1+Stage2" +
+                      (" + NCCL all-gather + merge kernel" if cfg["parallel"] == "sp" else "") +
+                      ", CUDA events, max over ranks",
+            "e2e": None, "e2e_note": "the end-to-end leg is measured on the c1 headline config",
+        }
+        print(json.dumps(line), flush=True)
+    del g
+
+
 def main():
     args = parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
+    if args.impl == "ours" and args.config != "c1":
+        run_sharded(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         if world > 1:
