@@ -54,6 +54,7 @@ constexpr int kMetaOff = kGroupWarps * kColBytes;              // 16384
 constexpr int kStageBytes = 17408;                             // data + metadata, 1024-aligned
 static_assert(kMetaOff + kGroupWarps * kMetaSlot <= kStageBytes && kStageBytes % 1024 == 0, "stage");
 constexpr int kQRowBytes = kHeadDim * 4;                       // one fp32 query row
+constexpr int kStgBytes = 2 * kQRowBytes;                      // per-warp output staging
 constexpr int kLutStride = 256;                                // bytes per table entry
 constexpr int kLutCopies = 32;                                 // one copy per lane
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
@@ -97,7 +98,10 @@ struct Cfg {
     static constexpr int kHighOff = kLutOff + kLutBytes;           // 130048
     static __host__ __device__ constexpr int ring_off(int gi) { return gi == 0 ? 0 : kHighOff + kQBytes; }
     static __host__ __device__ constexpr int q_off(int gi) { return gi == 0 ? kHighOff : kHighOff + kQBytes + kRingBytes; }
-    static constexpr int kSmem = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
+    // Output staging: 1 KB per compute warp (two fp32 rows of 128) after the
+    // rest, never written by a copy engine.
+    static constexpr int kStgOff = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
+    static constexpr int kSmem = kStgOff + kComputeWarps * kStgBytes;
     static_assert(kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
     static_assert(8 * (2 * kStages + 2) + 4 * kStages + 12 <= kBarStride, "barrier block");
     static_assert((16 * kStages + 16 + 4 * kStages + 4) % 8 == 0, "handoff barrier alignment");
@@ -262,7 +266,7 @@ __device__ __forceinline__ int tile_items(const Stage1Params& P, uint32_t t, int
 
 // Shared-memory map of one group.
 struct GroupSmem {
-    uint32_t ring, qarea, bars;
+    uint32_t ring, qarea, bars, stg;
     __device__ uint32_t stage(int s) const { return ring + (uint32_t)s * kStageBytes; }
     __device__ uint32_t full(int s) const { return bars + 8u * s; }
     template <int NS>
@@ -451,9 +455,20 @@ struct LaneSmem {
 template <int NT>
 __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, const LaneSmem& o, bool page_ok,
                                           int tok0, int start, int end, uint32_t lut_sel_src, int g,
-                                          int c, int src_a) {
+                                          int c, int src_a, uint32_t release_bar) {
+    // Every ring byte this lane uses is read first and the slot released, so
+    // its next page is fetched while this one is computed.  The arrive has
+    // release semantics: the reads above it are performed before the
+    // producer can observe the arrival.
     const uint4 k0 = lds128(sb + o.k0), k1 = lds128(sb + o.k1);
     const uint32_t kn = lds32(sb + o.meta);
+    const uint32_t vsp = lds32(sb + o.meta + 32), vzp = lds32(sb + o.meta + 64);
+    uint2 v[4];
+    v[0] = lds64(sb + o.v0);
+    v[1] = lds64(sb + o.v1);
+    v[2] = lds64(sb + o.v0 + 8 * kDataBytes);
+    v[3] = lds64(sb + o.v1 + 8 * kDataBytes);
+    mbar_arrive(release_bar);
     const bool va = page_ok && tok0 >= start && tok0 < end;
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
 
@@ -480,14 +495,6 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
             mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
     }
-    // V operands and scales are read after Q.K, which keeps them out of the
-    // register peak of the Q.K loop.
-    const uint32_t vsp = lds32(sb + o.meta + 32), vzp = lds32(sb + o.meta + 64);
-    uint2 v[4];
-    v[0] = lds64(sb + o.v0);
-    v[1] = lds64(sb + o.v1);
-    v[2] = lds64(sb + o.v0 + 8 * kDataBytes);
-    v[3] = lds64(sb + o.v1 + 8 * kDataBytes);
     const float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
     const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
     const float vs1 = vb ? half_bits_to_float(vsp >> 16) : 0.0f;
@@ -553,7 +560,9 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
 
     // -- P.V: rows g / g+8 = low / high nibble of V byte i&3 of word i>>2,
     //    k = tokens 2c, 2c+1, 2c+8, 2c+9; codes enter as exact fp16
-    //    subnormals code * 2^-20 (mantissa bits 4-7).
+    //    subnormals code * 2^-20 (mantissa bits 4-7).  Taking the low
+    //    nibble in place (code * 2^-24) saves the shift but is not exact on
+    //    the tensor cores: 36 % of the c1 partials changed, by up to 3.8e-5.
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int wi = i >> 2, bi = i & 3;
@@ -573,9 +582,10 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
 }
 
 // Partial output rows of one item: lane (g, c) holds dims 16g .. 16g+15 of
-// head c + 4 nt.  They are staged in this warp's 2 KB column of its last ring
-// slot as [4 heads][128] fp32 (16-byte chunk j of head h at chunk j ^ h:
-// conflict-free both ways) and written back as 128-byte coalesced runs.
+// head c + 4 nt.  They pass through this warp's 1 KB staging area two heads
+// at a time, as [2 heads][128] fp32 (16-byte chunk j of row r at chunk
+// j ^ r: conflict-free both ways), and are written back as 128-byte
+// coalesced runs.
 template <int NT>
 __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<NT>& st, uint32_t col, int b, int s,
                                          int kvh, int g, int c, int lane) {
@@ -590,27 +600,39 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
             return (((hi ? st.acc[nt][i][2] + st.acc[nt][i][3] : st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale +
                      z) * inv);
         };
-#pragma unroll
-        for (int j = 0; j < 4; j++)  // dims 16g + 4j .. 16g + 4j + 3
-            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(
-                             col + (uint32_t)c * 512u + ((uint32_t)((4 * g + j) ^ c) << 4)),
-                         "f"(val(2 * j, 0)), "f"(val(2 * j, 1)), "f"(val(2 * j + 1, 0)), "f"(val(2 * j + 1, 1))
-                         : "memory");
-        __syncwarp();
         const int heads = min(4, P.G - 4 * nt);
-        for (int hl = 0; hl < heads; hl++) {
-            float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + 4 * nt + hl) * P.msh + (int64_t)s * P.mss;
 #pragma unroll
-            for (int q = 0; q < 4; q++)
-                dst[32 * q + lane] =
-                    __uint_as_float(lds32(col + (uint32_t)hl * 512u + ((uint32_t)((8 * q + (lane >> 2)) ^ hl) << 4) +
-                                          4u * (lane & 3)));
+        for (int pass = 0; pass < 2; pass++) {
+            const int r = c & 1;  // staging row of this lane's head
+            if ((c >> 1) == pass) {
+#pragma unroll
+                for (int j = 0; j < 4; j++)  // dims 16g + 4j .. 16g + 4j + 3
+                    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(
+                                     col + (uint32_t)r * 512u + ((uint32_t)((4 * g + j) ^ r) << 4)),
+                                 "f"(val(2 * j, 0)), "f"(val(2 * j, 1)), "f"(val(2 * j + 1, 0)),
+                                 "f"(val(2 * j + 1, 1))
+                                 : "memory");
+            }
+            __syncwarp();
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const int hl = 2 * pass + rr;
+                if (hl < heads) {
+                    float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + 4 * nt + hl) * P.msh +
+                                 (int64_t)s * P.mss;
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        dst[32 * q + lane] = __uint_as_float(
+                            lds32(col + (uint32_t)rr * 512u + ((uint32_t)((8 * q + (lane >> 2)) ^ rr) << 4) +
+                                  4u * (lane & 3)));
+                }
+            }
+            __syncwarp();  // the area is rewritten by the next pass
         }
         if (g == 0 && c + 4 * nt < P.G) {
             float* dst = P.mid + (int64_t)b * P.msb + (int64_t)(kvh * P.G + c + 4 * nt) * P.msh + (int64_t)s * P.mss;
             dst[kHeadDim] = (st.m_run[nt] + lg2_approx(l)) * kLn2;
         }
-        __syncwarp();  // the column is rewritten by the next n-tile
     }
 }
 
@@ -619,17 +641,18 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
 template <int NT, int S>
 __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
                                           int k, int my_np, int w, int tok_first, int start, int end,
-                                          uint32_t lut_sel_src, int g, int c, int src_a, int lane,
-                                          bool release) {
+                                          uint32_t lut_sel_src, int g, int c, int src_a) {
     constexpr int NS = Cfg<NT>::kStages;
     if (!mbar_wait(gs.full(S), (cbits >> S) & 1u)) return false;
     cbits ^= 1u << S;
+    // all 32 lanes arrive on the slot's release barrier (no branch on the lane)
     if (k < my_np) {
         const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
         page_math<NT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
-                      lut_sel_src, g, c, src_a);
+                      lut_sel_src, g, c, src_a, gs.empty<NS>(S));
+    } else {
+        mbar_arrive(gs.empty<NS>(S));
     }
-    if (release) mbar_arrive(gs.empty<NS>(S));  // all 32 lanes (no branch on the lane)
     return true;
 }
 
@@ -724,24 +747,17 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
         const int tok_first = (start / kBlockSize) * kBlockSize + tau;
-        // The last page's slot is released after the epilogue, which stages
-        // the output rows in this warp's column of that slot.
         for (int k = 0; k < np_tile; k += NS) {
-            if (!page_step<NT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a,
-                                  lane, k + 1 < np_tile))
+            if (!page_step<NT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a))
                 return;
             if (k + 1 < np_tile && !page_step<NT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a, lane, k + 2 < np_tile))
+                                                     lut_sel_src, g, c, src_a))
                 return;
             if (k + 2 < np_tile && !page_step<NT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a, lane, k + 3 < np_tile))
+                                                     lut_sel_src, g, c, src_a))
                 return;
         }
-        const int last_slot = (np_tile - 1) % NS;
-        if (my_np > 0) epilogue<NT>(P, st, gs.stage(last_slot) + (uint32_t)w * kColBytes, b, s, kvh, g, c, lane);
-        // generic-proxy writes to the slot, then the producer's TMA: fence, release
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        mbar_arrive(gs.empty<NS>(last_slot));  // all 32 lanes
+        if (my_np > 0) epilogue<NT>(P, st, gs.stg + (uint32_t)w * kStgBytes, b, s, kvh, g, c, lane);
     }
 }
 
@@ -778,6 +794,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     GroupSmem gs;
     gs.ring = base + (uint32_t)C::ring_off(gi);
     gs.qarea = base + (uint32_t)C::q_off(gi);
+    gs.stg = base + (uint32_t)(C::kStgOff + gi * kGroupWarps * kStgBytes);
     gs.bars = base + C::kBarOff + (uint32_t)gi * kBarStride;
     if (tid < C::kGroups) {
         GroupSmem gb;
