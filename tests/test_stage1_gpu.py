@@ -13,6 +13,7 @@ count of bounded waits that gave up must be zero.
 
 from __future__ import annotations
 
+import functools
 import math
 import os
 
@@ -115,6 +116,28 @@ def test_ragged_per_sequence_splits(cuda_device):
     ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
                    num_splits_per_seq=np.asarray(nsp, np.int32))
     _check(_run(cuda_device, z, nsp=nsp, S=S), ref, "per-seq splits")
+
+
+@functools.lru_cache(maxsize=1)
+def _ragged_batch():
+    rng = np.random.default_rng(77)
+    lens = rng.integers(0, 1500, size=160)
+    lens[::23] = 0
+    lens = lens.tolist()
+    return lens, random_case(31, len(lens), 32, 8, lens)
+
+
+@pytest.mark.parametrize("per_seq", [False, True])
+def test_ragged_batch_weight_cuts(cuda_device, per_seq):
+    """A large ragged batch (empty sequences included) takes the weight-cut
+    tile walk: every group gets a contiguous tile range that can start and
+    end inside a sequence, and every non-empty split is written once."""
+    lens, z = _ragged_batch()
+    S = 16
+    nsp = L.splits_per_sequence(lens, 96, S) if per_seq else None
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                   num_splits_per_seq=None if nsp is None else np.asarray(nsp, np.int32))
+    _check(_run(cuda_device, z, nsp=nsp, S=S), ref, "ragged batch")
 
 
 def test_long_split_reloads_block_ids(cuda_device):

@@ -62,6 +62,7 @@ constexpr int kLutAddr = 0x10000;                              // shared address
 constexpr int kDynBase = 0x400;  // shared address of dynamic shared memory (1 KB reserved below it)
 constexpr int kBarStride = 128;                                // barrier block per group
 constexpr int kProducersPerGroup = 2;  // the issue handoff is unambiguous for two
+constexpr int kSplitCost = 16;         // per-split weight in tokens (query rows, epilogue)
 constexpr long long kWaitCycles = 2000000000LL;                // ~1 s at 1.9 GHz
 constexpr float kLazy = 8.0f;                                  // lazy-rescale slack (log2)
 constexpr float kWMax = 32768.0f;                              // largest W on the lazy path
@@ -103,7 +104,7 @@ struct Cfg {
     static constexpr int kStgOff = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
     static constexpr int kSmem = kStgOff + kComputeWarps * kStgBytes;
     static_assert(kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
-    static_assert(8 * (2 * kStages + 2) + 4 * kStages + 12 <= kBarStride, "barrier block");
+    static_assert(8 * (2 * kStages + 2) + 4 * kStages + 12 <= 96 && 96 + 12 <= kBarStride, "barrier block");
     static_assert((16 * kStages + 16 + 4 * kStages + 4) % 8 == 0, "handoff barrier alignment");
     static_assert(kSmem <= 232448, "shared memory per CTA");
 };
@@ -264,6 +265,123 @@ __device__ __forceinline__ int tile_items(const Stage1Params& P, uint32_t t, int
     return __shfl_sync(0xffffffffu, m, 0);  // uniform over the warp
 }
 
+// ---------------------------------------------------------------------------
+// Balanced tile ranges.  The items (b, s, KV head) in order are weighted by
+// their split's token count plus kSplitCost (empty splits weigh nothing) and
+// cut into gridDim.x * kGroups ranges of equal weight; group g takes the
+// tiles whose first item starts inside its range: a contiguous run of tiles
+// of about equal work, whatever the spread of sequence lengths.  Every CTA
+// derives the same cut from seq_lens (and nsplits), so no state is shared
+// between CTAs or launches.
+// ---------------------------------------------------------------------------
+struct SeqSplit {
+    int L, sl, ne;  // clamped length, split length, non-empty splits
+};
+__device__ __forceinline__ SeqSplit seq_split_of(const Stage1Params& P, int len, int nsplit) {
+    SeqSplit r{0, 1, 0};
+    const int nsp = min(nsplit, P.S);
+    const int L = min(len, P.max_blocks * kBlockSize);
+    if (nsp <= 0 || L <= 0) return r;
+    r.L = L;
+    r.sl = (L + nsp - 1) / nsp;  // ceil(L / nsp), the split rule of decode_item
+    r.ne = (L + r.sl - 1) / r.sl;
+    return r;
+}
+__device__ __forceinline__ SeqSplit seq_split(const Stage1Params& P, int b) {
+    return seq_split_of(P, __ldg(P.seq_lens + b), P.nsplits ? __ldg(P.nsplits + b) : P.S);
+}
+__device__ __forceinline__ long long seq_weight(const Stage1Params& P, const SeqSplit& q) {
+    return (long long)P.Hk * ((long long)q.L + (long long)kSplitCost * q.ne);
+}
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// Tile of the first item of sequence b whose start weight reaches r (>= 1,
+// at most the sequence's weight): split s* = the last split starting below
+// r, then the KV head in it.
+__device__ __forceinline__ uint32_t cut_tile(const Stage1Params& P, const SeqSplit& q, int b, long long r,
+                                             uint32_t num_tiles) {
+    const long long unit = (long long)P.Hk * (q.sl + kSplitCost);
+    const long long ss = min((long long)(q.ne - 1), (r - 1) / unit);
+    const long long a = unit * ss;
+    const long long per = (long long)(min((int)(ss + 1) * q.sl, q.L) - (int)ss * q.sl) + kSplitCost;
+    const long long kv = (r - a + per - 1) / per;  // in [1, Hk]
+    const long long item = ((long long)b * P.S + ss) * P.Hk + kv;
+    return (uint32_t)min((long long)num_tiles, (item + kGroupWarps - 1) / kGroupWarps);
+}
+// Tile walk of group gi of this CTA: tiles first, first + stride, ... below
+// end, in res[0..2].  A batch whose sequences all have the same length and
+// split count takes the round-robin walk (already balanced); any other
+// batch the contiguous ranges of the weight cut.  One warp (compact loops:
+// this code runs once, cold, ahead of every other warp's first tile).
+__device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uint32_t num_tiles, uint32_t (&res)[3],
+                          int lane) {
+    const uint32_t cuts = gridDim.x * (uint32_t)groups_per_cta;
+    const uint32_t g = blockIdx.x * (uint32_t)groups_per_cta + (uint32_t)gi;
+    long long tot = 0;
+    int lmin = 0x7fffffff, lmax = -0x7fffffff, nmin = 0x7fffffff, nmax = -0x7fffffff;
+#pragma unroll 1
+    for (int b0 = 0; b0 < P.B; b0 += 32) {
+        const int b = b0 + lane;
+        if (b < P.B) {
+            const int len = __ldg(P.seq_lens + b), nsp = P.nsplits ? __ldg(P.nsplits + b) : P.S;
+            tot += seq_weight(P, seq_split_of(P, len, nsp));
+            lmin = min(lmin, len);
+            lmax = max(lmax, len);
+            nmin = min(nmin, nsp);
+            nmax = max(nmax, nsp);
+        }
+    }
+    tot = warp_sum_ll(tot);
+    if (__reduce_min_sync(0xffffffffu, lmin) == __reduce_max_sync(0xffffffffu, lmax) &&
+        __reduce_min_sync(0xffffffffu, nmin) == __reduce_max_sync(0xffffffffu, nmax)) {
+        res[0] = g;
+        res[1] = num_tiles;
+        res[2] = cuts;
+        return;
+    }
+    res[2] = 1u;
+    const long long qt = tot / (long long)cuts, rt = tot % (long long)cuts;
+#pragma unroll 1
+    for (int k = 0; k < 2; k++) {
+        // cut g + k: the tile of the first item whose start weight reaches
+        // floor((g + k) * tot / cuts); weight 0 is tile 0, the last cut (or
+        // every cut when nothing has a token) the end
+        const uint32_t gk = g + (uint32_t)k;
+        const long long tgt = qt * gk + rt * gk / (long long)cuts;  // no overflow
+        uint32_t t = num_tiles;
+        if (tot > 0 && gk < cuts && tgt == 0) t = 0;
+        if (tot > 0 && gk < cuts && tgt > 0) {
+            long long base = 0;
+#pragma unroll 1
+            for (int b0 = 0; b0 < P.B; b0 += 32) {
+                const int b = b0 + lane;
+                SeqSplit q{0, 1, 0};
+                if (b < P.B) q = seq_split(P, b);
+                const long long w = seq_weight(P, q);
+                long long incl = w;
+#pragma unroll 1
+                for (int o = 1; o < 32; o <<= 1) {
+                    const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += v;
+                }
+                const long long excl = base + incl - w;
+                const bool here = w > 0 && excl < tgt && tgt <= base + incl;
+                const uint32_t m = __ballot_sync(0xffffffffu, here);
+                if (m) {
+                    const uint32_t tl = here ? cut_tile(P, q, b, tgt - excl, num_tiles) : 0u;
+                    t = __shfl_sync(0xffffffffu, tl, __ffs(m) - 1);
+                    break;
+                }
+                base += __shfl_sync(0xffffffffu, incl, 31);
+            }
+        }
+        res[k] = t;
+    }
+}
+
 // Shared-memory map of one group.
 struct GroupSmem {
     uint32_t ring, qarea, bars, stg;
@@ -281,6 +399,9 @@ struct GroupSmem {
     // when page G (counted over all tiles) has been announced on its slot.
     template <int NS>
     __device__ uint32_t issued() const { return bars + 16u * NS + 16 + 4u * NS + 4u; }
+    // The group's tile walk {first, end, stride} (written once before the
+    // roles split).
+    __device__ uint32_t tiles() const { return bars + 96u; }
 };
 
 // ---------------------------------------------------------------------------
@@ -293,8 +414,7 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
                                         int lane, int pj, int npj) {
     using C = Cfg<NT>;
     constexpr int NS = C::kStages;
-    const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
-    const uint32_t tile_stride = gridDim.x * C::kGroups;
+    const uint32_t t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
     const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
     // The group's two producer warps take turns: producer pj copies the pages
@@ -326,25 +446,25 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
         tq++;
         return true;
     };
-    // Next tile of this group with at least one page (or t >= num_tiles).
+    // Next tile of this group with at least one page (or t >= t_end).
     auto next_tile = [&](uint32_t t, ItemInfo& x, int& npx, int& np_tile) {
-        for (; t < num_tiles; t += tile_stride)
+        for (; t < t_end; t += t_stride)
             if ((np_tile = tile_items(P, t, lane, x, npx)) > 0) return t;
         return t;
     };
 
     ItemInfo ir;
     int np = 0, np_tile = 0;
-    uint32_t t = next_tile(blockIdx.x * C::kGroups + gi, ir, np, np_tile);
-    if (t < num_tiles && !issue_query(ir, np)) abort = true;
-    while (t < num_tiles && !abort) {
+    uint32_t t = next_tile(lds32(gs.tiles()), ir, np, np_tile);
+    if (t < t_end && !issue_query(ir, np)) abort = true;
+    while (t < t_end && !abort) {
         // The next tile is decoded now; its query rows go out once page 0 of
         // this tile has been released (the compute warps have read this
         // tile's rows by then), well before they are needed.
         ItemInfo irn;
         int npn = 0, np_tile_n = 0;
-        const uint32_t tn = next_tile(t + tile_stride, irn, npn, np_tile_n);
-        bool next_query_sent = tn >= num_tiles;
+        const uint32_t tn = next_tile(t + t_stride, irn, npn, np_tile_n);
+        bool next_query_sent = tn >= t_end;
         // Runs of consecutive items sharing one (b, s): their head slices are
         // adjacent in every token row, so one copy per row serves a run.
         const int key = np > 0 ? ir.b * P.S + ir.s : -1 - lane;
@@ -662,8 +782,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     using C = Cfg<NT>;
     constexpr int NS = C::kStages;
     const int g = lane >> 2, c = lane & 3;
-    const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
-    const uint32_t tile_stride = gridDim.x * C::kGroups;
+    const uint32_t t_first = lds32(gs.tiles()), t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     // PRMT source: byte 0 = this lane's copy offset, byte 1 = table page 0x01, byte 2 = 0
     const uint32_t lut_sel_src = (uint32_t)(lane % kLutCopies) * 8u | ((uint32_t)(kLutAddr >> 16) << 8);
     const int tau = 8 * (g >> 2) + 2 * ((g >> 1) & 1) + 4 * (g & 1);
@@ -680,7 +799,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     uint32_t tq = 0;     // tiles done (query-barrier phase)
     uint32_t cbits = 0;  // bit s: parity of the pages slot s has delivered
 
-    for (uint32_t t = blockIdx.x * C::kGroups + gi; t < num_tiles; t += tile_stride) {
+    for (uint32_t t = t_first; t < t_end; t += t_stride) {
         ItemInfo ir;
         int np;
         const int np_tile = tile_items(P, t, lane, ir, np);
@@ -774,13 +893,21 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     const int ec = fp16_scale_exp(cmax);
     const float cscale = exp2i(ec);
-    for (int e = tid; e < 256 * kLutCopies; e += C::kThreads) {
+    // The last kGroups warps plan the groups' tile walks (reading seq_lens)
+    // while the others build the table.
+    const uint32_t num_tiles = (uint32_t)((P.num_items + kGroupWarps - 1) / kGroupWarps);
+    const int planner = warp - (C::kWarps - C::kGroups);  // group planned by this warp, if >= 0
+    uint32_t walk[3] = {0u, 0u, 0u};
+    if (planner >= 0)
+        tile_walk(P, planner, C::kGroups, num_tiles, walk, lane);
+    else
+        for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
         const int byte = e / kLutCopies;
         const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
         *reinterpret_cast<uint2*>(smem + C::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
-    }
+        }
 
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     if (base != (uint32_t)kDynBase) {  // the table address above assumes this window layout
@@ -796,6 +923,12 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     gs.qarea = base + (uint32_t)C::q_off(gi);
     gs.stg = base + (uint32_t)(C::kStgOff + gi * kGroupWarps * kStgBytes);
     gs.bars = base + C::kBarOff + (uint32_t)gi * kBarStride;
+    if (planner >= 0 && lane == 0) {
+        const uint32_t tiles = base + C::kBarOff + (uint32_t)planner * kBarStride + 96u;
+        sts32(tiles, walk[0]);
+        sts32(tiles + 4u, walk[1]);
+        sts32(tiles + 8u, walk[2]);
+    }
     if (tid < C::kGroups) {
         GroupSmem gb;
         gb.bars = base + C::kBarOff + (uint32_t)tid * kBarStride;
