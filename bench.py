@@ -50,10 +50,11 @@ CONFIGS = {
     "c3": dict(B=256, L=8192, Hq=64, Hk=8, S=32, parallel="tp",
                workload="Llama-3-70B-shaped decode: B256 x 8192 ctx, Hq64/Hk8 (GQA-8), 32 splits; "
                         "TP by KV head"),
-    "c4": dict(B=4, L=131072, Hq=32, Hk=8, S=128, parallel="sp",
+    "c4": dict(B=4, L=131072, Hq=32, Hk=8, S=74, parallel="sp",
                workload="long-context decode: B4 x 131072 ctx, Hq32/Hk8; SP split-KV, NCCL all-gather of "
-                        "partials + merge kernel; 128 local splits per GPU (the reference config's 16 leave "
-                        "most SMs idle: 512 work items; the merge kernel combines any split count)"),
+                        "partials + merge kernel; 74 local splits per GPU: 4 x 74 x 8 KV heads = 296 tiles, "
+                        "one per Stage1 group on 148 SMs (the reference config's 16 leave most SMs idle; "
+                        "the merge kernel combines any split count)"),
 }
 FALLBACK_HBM_GBS = 6650.0
 
@@ -69,7 +70,12 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
-    return ap.parse_args()
+    ap.add_argument("--splits", type=int, default=None,
+                    help="override the config's (local) KV split count")
+    args = ap.parse_args()
+    if args.splits is not None:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], S=args.splits)
+    return args
 
 
 # ---------------------------------------------------------------------------
