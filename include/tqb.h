@@ -29,6 +29,11 @@
  *                   baseline/stage2.py:44-55)
  *   tqb_store    <- triton_turboquant_store kernel launch
  *                   (reference/soa_store.py:494-524, reference/aos_store.py:420-447)
+ *   tqb_rotate_query <- the launcher's query cast + rotation GEMM + copy,
+ *                   q_rot = (query.float() @ PiT).contiguous()
+ *                   (reference/soa_decode_v1.py:535-538)
+ *   tqb_stage2_typed <- the Stage2 launch plus the final output.to(query.dtype)
+ *                   (reference/soa_decode_v1.py:625-643)
  */
 #ifndef TQB_H_
 #define TQB_H_
@@ -50,6 +55,12 @@ typedef enum tqb_status {
     TQB_ERR_LAUNCH = -4,       /* cudaGetLastError after the launch */
     TQB_ERR_CUDA = -5          /* other CUDA runtime failure */
 } tqb_status;
+
+typedef enum tqb_dtype {
+    TQB_DTYPE_F32 = 0,
+    TQB_DTYPE_F16 = 1,
+    TQB_DTYPE_BF16 = 2
+} tqb_dtype;
 
 typedef enum tqb_layout {
     TQB_LAYOUT_SOA = 0, /* block = [16 tok][Hk][K64|V64] + [Hk][3][16] fp16 meta */
@@ -116,6 +127,32 @@ typedef struct tqb_stage2_args {
 } tqb_stage2_args;
 
 int tqb_stage2(const tqb_stage2_args* args, cudaStream_t stream);
+
+/*
+ * Stage2 with the output written directly in `out_dtype` (a tqb_dtype) to
+ * `output` (args->output is ignored; its strides, in elements, still apply):
+ * the fp32 result rounded to nearest even, bit-identical to Stage2 followed
+ * by the launcher's output.to(query.dtype) (reference/soa_decode_v1.py:643).
+ */
+int tqb_stage2_typed(const tqb_stage2_args* args, int out_dtype, void* output, cudaStream_t stream);
+
+/*
+ * Query rotation: q_rot[b, h, :] = float(query[b, h, :]) @ rotation, with
+ * rotation = Pi^T, a [D, D] row-major fp32 matrix, accumulated in fp32 (the
+ * launcher's cast + GEMM + copy, reference/soa_decode_v1.py:535-538, in one
+ * kernel).  query: [B, Hq, D] of query_dtype with unit stride over D.
+ */
+typedef struct tqb_rotate_args {
+    const void* query;
+    int32_t query_dtype;               /* tqb_dtype */
+    int64_t q_stride_b, q_stride_h;    /* elements */
+    const float* rotation;             /* [D, D] row-major, 16-byte aligned */
+    float* q_rot;                      /* [B, Hq, D] */
+    int64_t out_stride_b, out_stride_h;
+    int32_t batch, num_q_heads, head_dim;
+} tqb_rotate_args;
+
+int tqb_rotate_query(const tqb_rotate_args* args, cudaStream_t stream);
 
 /*
  * Cross-GPU merge: partials[g, b, h, 0:D] / partials[g, b, h, D] are the

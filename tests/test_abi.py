@@ -75,6 +75,17 @@ def test_argument_validation_without_launch(lib):
     a.num_kv_heads = 8
     assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG  # NULL pointers
     assert lib.tqb_stage1(None, None) == _lib.TQB_ERR_INVALID_ARG
+    r = _lib.RotateArgs()
+    r.batch, r.num_q_heads, r.head_dim, r.query_dtype = 1, 32, 128, 7  # no such dtype
+    assert lib.tqb_rotate_query(ctypes.byref(r), None) == _lib.TQB_ERR_INVALID_ARG
+    r.query_dtype, r.head_dim = _lib.TQB_DTYPE_BF16, 64
+    assert lib.tqb_rotate_query(ctypes.byref(r), None) == _lib.TQB_ERR_UNSUPPORTED
+    r.head_dim = 128
+    assert lib.tqb_rotate_query(ctypes.byref(r), None) == _lib.TQB_ERR_INVALID_ARG  # NULL pointers
+    t = _lib.Stage2Args()
+    t.batch, t.num_q_heads, t.head_dim, t.num_splits = 1, 32, 128, 4
+    assert lib.tqb_stage2_typed(ctypes.byref(t), 5, None, None) == _lib.TQB_ERR_INVALID_ARG
+    assert b"out_dtype" in lib.tqb_last_error_detail()
     s = _lib.StoreArgs()
     s.num_tokens, s.num_kv_heads, s.head_dim, s.block_size, s.n_centroids = 1, 8, 128, 16, 8
     assert lib.tqb_store(ctypes.byref(s), None) == _lib.TQB_ERR_UNSUPPORTED
@@ -96,6 +107,7 @@ int main(void) {
   printf("tqb_merge_args %zu\n", sizeof(tqb_merge_args));
   printf("tqb_store_args %zu\n", sizeof(tqb_store_args));
   printf("tqb_decode_static_args %zu\n", sizeof(tqb_decode_static_args));
+  printf("tqb_rotate_args %zu\n", sizeof(tqb_rotate_args));
   %FIELDS%
   return 0;
 }
@@ -105,7 +117,7 @@ int main(void) {
 def test_ctypes_structs_match_c_layout(tmp_path: Path):
     structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
                "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs,
-               "tqb_decode_static_args": _lib.DecodeStaticArgs}
+               "tqb_decode_static_args": _lib.DecodeStaticArgs, "tqb_rotate_args": _lib.RotateArgs}
     fields = "\n".join(f"F({c}, {f})" for c, py in structs.items() for f, _ in py._fields_)
     src = tmp_path / "probe.c"
     src.write_text(C_LAYOUT_PROBE.replace("%FIELDS%", fields))

@@ -104,3 +104,45 @@ def test_store_bit_exact_vs_oracle_large(cuda_device):
     torch.cuda.synchronize()
     got = cache.cpu().numpy()
     assert np.array_equal(got, ref), f"{(got != ref).sum()} bytes differ"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_stage2_typed_output_equals_cast(cuda_device, golden, dtype):
+    """A 16-bit Stage2 output is the fp32 merge rounded to nearest even:
+    bit-identical to merging into fp32 and casting (the launcher's
+    output.to(query.dtype), reference/soa_decode_v1.py:643)."""
+    z = golden["ragged_gqa4"]
+    dev = cuda_device
+    mid = torch.from_numpy(z["mid_o_soa_v1"]).to(dev)
+    sl = torch.from_numpy(z["seq_lens"]).to(dev)
+    B, Hq = mid.shape[:2]
+    o32 = torch.empty(B, Hq, 128, device=dev)
+    l32 = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, sl, o32, l32)
+    o16 = torch.empty(B, Hq, 128, dtype=dtype, device=dev)
+    l16 = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, sl, o16, l16)
+    torch.cuda.synchronize()
+    assert torch.equal(o16.view(torch.int16), o32.to(dtype).view(torch.int16))
+    assert torch.equal(l16, l32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_rotate_query_vs_torch(cuda_device, dtype):
+    """Cast + rotation in one kernel against the launcher's
+    query.float() @ PiT (reference/soa_decode_v1.py:535-538), on a strided
+    query view; fp32 accumulation, so only the summation order differs."""
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(5)
+    big = torch.randn(37, 40, 128, generator=g, device=dev).to(dtype)
+    q = big[:, 3:35]  # [37, 32, 128], batch stride 40*128
+    PiT = torch.linalg.qr(torch.randn(128, 128, generator=g, device=dev))[0].contiguous()
+    ref = q.double() @ PiT.double()
+    got = tqb.rotate_query(q, PiT)
+    out = torch.full((37, 36, 128), -7.0, device=dev)
+    tqb.rotate_query(q, PiT, out=out[:, 2:34])
+    torch.cuda.synchronize()
+    err = (got.double() - ref).abs().max().item()
+    assert err <= 1e-5 * max(1.0, ref.abs().max().item()), err
+    assert torch.equal(out[:, 2:34], got)
+    assert torch.all(out[:, :2] == -7.0) and torch.all(out[:, 34:] == -7.0)

@@ -179,20 +179,22 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
     return TQB_OK;
 }
 
-int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
+// Stage2 with the output written as `dtype` to `out` (a->output ignored).
+static int stage2_impl(const tqb_stage2_args* a, void* out, int dtype, cudaStream_t stream) {
     g_detail[0] = '\0';
     TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(dtype == TQB_DTYPE_F32 || dtype == TQB_DTYPE_F16 || dtype == TQB_DTYPE_BF16, TQB_ERR_INVALID_ARG,
+                "out_dtype must be TQB_DTYPE_F32, TQB_DTYPE_F16 or TQB_DTYPE_BF16");
     TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0 && a->num_splits > 0, TQB_ERR_INVALID_ARG,
                 "batch/heads/num_splits must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE((int64_t)a->batch * a->num_q_heads < (int64_t(1) << 31), TQB_ERR_UNSUPPORTED,
                 "batch * num_q_heads must be < 2^31");
     if (a->batch == 0) return TQB_OK;
-    TQB_REQUIRE(a->mid_o && a->seq_lens && a->output && a->lse, TQB_ERR_INVALID_ARG,
-                "a required pointer is NULL");
-    TQB_REQUIRE(aligned(a->mid_o, 4) && aligned(a->output, 4) && aligned(a->lse, 4),
-                TQB_ERR_ALIGNMENT, "buffers must be 4-byte aligned");
-    DeviceGuard guard(a->output);
+    TQB_REQUIRE(a->mid_o && a->seq_lens && out && a->lse, TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->mid_o, 4) && aligned(out, dtype == TQB_DTYPE_F32 ? 4 : 2) && aligned(a->lse, 4),
+                TQB_ERR_ALIGNMENT, "buffers must be aligned to their element size");
+    DeviceGuard guard(out);
     TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning output");
     tqb::Stage2Params p{};
     p.mid = a->mid_o;
@@ -201,7 +203,8 @@ int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
     p.mss = a->mid_stride_s;
     p.seq_lens = a->seq_lens;
     p.nsplits = a->num_splits_per_seq;
-    p.out = a->output;
+    p.out = out;
+    p.out_dtype = dtype;
     p.osb = a->out_stride_b;
     p.osh = a->out_stride_h;
     p.lse = a->lse;
@@ -209,9 +212,46 @@ int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
     p.B = a->batch;
     p.Hq = a->num_q_heads;
     p.S = a->num_splits;
-    const int rc = tqb::launch_stage2(p, stream);
-    if (rc != TQB_OK) return rc;
-    return TQB_OK;
+    return tqb::launch_stage2(p, stream);
+}
+
+int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
+    return stage2_impl(a, a ? a->output : nullptr, TQB_DTYPE_F32, stream);
+}
+
+int tqb_stage2_typed(const tqb_stage2_args* a, int out_dtype, void* output, cudaStream_t stream) {
+    return stage2_impl(a, output, out_dtype, stream);
+}
+
+int tqb_rotate_query(const tqb_rotate_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->query_dtype == TQB_DTYPE_F32 || a->query_dtype == TQB_DTYPE_F16 ||
+                    a->query_dtype == TQB_DTYPE_BF16,
+                TQB_ERR_INVALID_ARG, "query_dtype must be TQB_DTYPE_F32, TQB_DTYPE_F16 or TQB_DTYPE_BF16");
+    TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0, TQB_ERR_INVALID_ARG, "batch/heads must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE((int64_t)a->batch * a->num_q_heads < (int64_t(1) << 31), TQB_ERR_UNSUPPORTED,
+                "batch * num_q_heads must be < 2^31");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->query && a->rotation && a->q_rot, TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->query, a->query_dtype == TQB_DTYPE_F32 ? 4 : 2) && aligned(a->rotation, 16) &&
+                    aligned(a->q_rot, 4),
+                TQB_ERR_ALIGNMENT, "query/q_rot must be aligned to their element size, rotation to 16 bytes");
+    DeviceGuard guard(a->q_rot);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning q_rot");
+    tqb::RotateParams p{};
+    p.q = a->query;
+    p.dtype = a->query_dtype;
+    p.qsb = a->q_stride_b;
+    p.qsh = a->q_stride_h;
+    p.rot = a->rotation;
+    p.out = a->q_rot;
+    p.osb = a->out_stride_b;
+    p.osh = a->out_stride_h;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    return tqb::launch_rotate(p, stream);
 }
 
 int tqb_merge_partials(const tqb_merge_args* a, cudaStream_t stream) {

@@ -52,11 +52,23 @@ struct Stage2Params {
     int64_t msb, msh, mss;
     const int32_t* seq_lens;
     const int32_t* nsplits;
-    float* out;
+    void* out;      // [B, Hq, D] of out_dtype
+    int out_dtype;  // TQB_DTYPE_*
     int64_t osb, osh;
     float* lse;
     int64_t lsb;
     int B, Hq, S;
+};
+
+// q_rot[b, h, :] = float(q[b, h, :]) @ rot (rot [D, D] row-major fp32).
+struct RotateParams {
+    const void* q;
+    int dtype;  // TQB_DTYPE_* of q
+    int64_t qsb, qsh;
+    const float* rot;
+    float* out;
+    int64_t osb, osh;
+    int B, Hq;
 };
 
 struct MergeParams {
@@ -96,6 +108,7 @@ int launch_stage1_ring(const Stage1Params& p, cudaStream_t stream, int num_sms);
 int read_wait_timeouts(unsigned int* count, bool reset);
 int launch_stage2(const Stage2Params& p, cudaStream_t stream);
 int launch_merge(const MergeParams& p, cudaStream_t stream);
+int launch_rotate(const RotateParams& p, cudaStream_t stream);
 int launch_store(const StoreParams& p, cudaStream_t stream);
 
 }  // namespace tqb

@@ -6,6 +6,8 @@
 //     lse = max + ln(sum_s w_s).
 // The merge reads 33.8 MB at the B64x4K workload (mostly from L2, written by
 // Stage1 just before) against 1 MB written: a latency-bound streaming pass.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -18,12 +20,23 @@ namespace {
 constexpr int kWarpsPerCta = 8;
 constexpr int kSplitsPerPass = 8;  // splits whose loads a warp keeps in flight at once
 
+// Output element conversion (round to nearest even, as torch's .to(dtype)).
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
 // One CTA of 4 warps per (b, h).  Warp w merges the non-empty splits
 // s = w, w + 4, w + 8, ... of (b, h): lane l owns dims l, l+32, l+64, l+96,
 // so each split row is read as four coalesced 128-byte runs, and the warp
 // issues the loads of up to kSplitsPerPass splits before using any of them.
 // The four warps' (max, sum, acc) then combine through shared memory.  Same
 // log-sum-exp algebra as the reference's running merge.
+template <typename OutT>
 __global__ void __launch_bounds__(kHeadDim, 8) stage2_kernel(const Stage2Params P) {
     constexpr int kParts = kHeadDim / 32;  // warps per CTA
     __shared__ float s_acc[kParts][kHeadDim];
@@ -83,8 +96,8 @@ __global__ void __launch_bounds__(kHeadDim, 8) stage2_kernel(const Stage2Params 
         o += w * s_acc[p][d];
         wsum += w * s_sum[p];
     }
-    float* out = P.out + (int64_t)b * P.osb + (int64_t)h * P.osh;
-    out[d] = __fdiv_rn(o, wsum);
+    OutT* out = static_cast<OutT*>(P.out) + (int64_t)b * P.osb + (int64_t)h * P.osh;
+    out[d] = from_f32<OutT>(__fdiv_rn(o, wsum));
     if (d == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
 }
 
@@ -120,7 +133,12 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) merge_kernel(const MergePar
 int launch_stage2(const Stage2Params& P, cudaStream_t stream) {
     const int64_t items = (int64_t)P.B * P.Hq;
     if (items == 0) return TQB_OK;
-    stage2_kernel<<<(unsigned)items, kHeadDim, 0, stream>>>(P);
+    switch (P.out_dtype) {
+        case TQB_DTYPE_F32: stage2_kernel<float><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
+        case TQB_DTYPE_F16: stage2_kernel<__half><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
+        case TQB_DTYPE_BF16: stage2_kernel<__nv_bfloat16><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
+        default: return TQB_ERR_INVALID_ARG;
+    }
     return report_launch(cudaGetLastError());
 }
 

@@ -23,4 +23,4 @@ from .compat import (  # noqa: F401
     triton_turboquant_decode_attention,
     triton_turboquant_store,
 )
-from .ops import merge_partials, stage1, stage2, store  # noqa: F401
+from .ops import merge_partials, rotate_query, stage1, stage2, store  # noqa: F401

@@ -25,6 +25,10 @@ TQB_ERR_CUDA = -5
 TQB_LAYOUT_SOA = 0
 TQB_LAYOUT_AOS = 1
 
+TQB_DTYPE_F32 = 0
+TQB_DTYPE_F16 = 1
+TQB_DTYPE_BF16 = 2
+
 # Every symbol include/tqb.h declares.
 EXPORTED_SYMBOLS = (
     "tqb_stage1",
@@ -36,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "tqb_version",
     "tqb_wait_timeouts",
     "tqb_decode_static",
+    "tqb_stage2_typed",
+    "tqb_rotate_query",
 )
 
 
@@ -101,6 +107,14 @@ class DecodeStaticArgs(ctypes.Structure):
     ]
 
 
+class RotateArgs(ctypes.Structure):
+    _fields_ = [
+        ("query", _vp), ("query_dtype", _i32), ("q_stride_b", _i64), ("q_stride_h", _i64),
+        ("rotation", _vp), ("q_rot", _vp), ("out_stride_b", _i64), ("out_stride_h", _i64),
+        ("batch", _i32), ("num_q_heads", _i32), ("head_dim", _i32),
+    ]
+
+
 class MergeArgs(ctypes.Structure):
     _fields_ = [
         ("partials", _vp), ("num_parts", _i32), ("batch", _i32), ("num_q_heads", _i32),
@@ -151,6 +165,10 @@ def load() -> ctypes.CDLL:
             lib.tqb_wait_timeouts.restype = ctypes.c_int
             lib.tqb_decode_static.argtypes = [ctypes.POINTER(DecodeStaticArgs), _vp]
             lib.tqb_decode_static.restype = ctypes.c_int
+            lib.tqb_stage2_typed.argtypes = [ctypes.POINTER(Stage2Args), ctypes.c_int, _vp, _vp]
+            lib.tqb_stage2_typed.restype = ctypes.c_int
+            lib.tqb_rotate_query.argtypes = [ctypes.POINTER(RotateArgs), _vp]
+            lib.tqb_rotate_query.restype = ctypes.c_int
             _lib = lib
     return _lib
 

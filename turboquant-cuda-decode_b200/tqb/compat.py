@@ -136,7 +136,12 @@ def triton_turboquant_decode_attention(
     B, Hq, D = query.shape
     if PiT is None:
         PiT = Pi.T.contiguous()
-    q_rot = (query.float() @ PiT).contiguous()
+    # cast + rotation in one kernel (the reference: query.float() @ PiT,
+    # reference/soa_decode_v1.py:535-538)
+    if query.dtype in (torch.float32, torch.float16, torch.bfloat16):
+        q_rot = ops.rotate_query(query if query.stride(2) == 1 else query.contiguous(), PiT.float().contiguous())
+    else:
+        q_rot = (query.float() @ PiT).contiguous()
     S = max_num_kv_splits
     if mid_o_buf is not None and mid_o_buf.shape[0] >= B and mid_o_buf.shape[2] >= S:
         mid_o = mid_o_buf[:B, :Hq, :S, :]
@@ -146,7 +151,11 @@ def triton_turboquant_decode_attention(
             buf_holder._tq_mid_o_buf = mid_o
     ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout="soa",
                attn_scale=scale)
-    if output_buf is not None and output_buf.shape[0] >= B:
+    if query.dtype in (torch.float16, torch.bfloat16):
+        # Stage2 writes the query's dtype directly (the reference merges into
+        # fp32 and then casts: reference/soa_decode_v1.py:643; same rounding)
+        output = torch.empty(B, Hq, D, dtype=query.dtype, device=query.device)
+    elif output_buf is not None and output_buf.shape[0] >= B:
         output = output_buf[:B, :Hq, :D]
     else:
         output = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
@@ -159,7 +168,7 @@ def triton_turboquant_decode_attention(
         if buf_holder is not None:
             buf_holder._tq_lse_buf = lse
     ops.stage2(mid_o, seq_lens, output, lse)
-    return output.to(query.dtype)
+    return output if output.dtype == query.dtype else output.to(query.dtype)
 
 
 def triton_turboquant_store(

@@ -16,7 +16,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import MergeArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
+from ._lib import MergeArgs, RotateArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
 from .layout import BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, layout_id
 
 
@@ -29,6 +29,10 @@ def _cuda(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
     _require(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
     _require(t.is_cuda, f"{name} must be a CUDA tensor")
     _require(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+
+
+_DTYPE_ID = {torch.float32: _lib.TQB_DTYPE_F32, torch.float16: _lib.TQB_DTYPE_F16,
+             torch.bfloat16: _lib.TQB_DTYPE_BF16}
 
 
 def _stream(device: torch.device) -> int:
@@ -105,10 +109,14 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
 def stage2(mid_o: torch.Tensor, seq_lens: torch.Tensor, output: torch.Tensor, lse: torch.Tensor, *,
            num_splits_per_seq: Optional[torch.Tensor] = None, stream: Optional[int] = None):
     """Merge the non-empty splits of ``mid_o`` into ``output [B, Hq, D]`` and
-    ``lse [B, Hq]``."""
+    ``lse [B, Hq]``.  ``output`` may be float32, float16 or bfloat16: a
+    16-bit output receives the fp32 result rounded to nearest even (the
+    launcher's ``output.to(query.dtype)``, reference/soa_decode_v1.py:643,
+    without the extra pass)."""
     _cuda(mid_o, "mid_o", torch.float32)
     _cuda(seq_lens, "seq_lens", torch.int32)
-    _cuda(output, "output", torch.float32)
+    _require(isinstance(output, torch.Tensor) and output.is_cuda and output.dtype in _DTYPE_ID,
+             "output must be a float32/float16/bfloat16 CUDA tensor")
     _cuda(lse, "lse", torch.float32)
     _require(mid_o.dim() == 4 and mid_o.stride(3) == 1, "mid_o must be [B, Hq, S, D+1]")
     B, Hq, S, D1 = mid_o.shape
@@ -128,8 +136,42 @@ def stage2(mid_o: torch.Tensor, seq_lens: torch.Tensor, output: torch.Tensor, ls
     a.lse_stride_b = lse.stride(0)
     a.batch, a.num_q_heads, a.head_dim, a.num_splits = B, Hq, D1 - 1, S
     with torch.cuda.device(mid_o.device):
-        _lib.check(_lib.load().tqb_stage2(a, stream if stream is not None else _stream(mid_o.device)))
+        st = stream if stream is not None else _stream(mid_o.device)
+        if output.dtype == torch.float32:
+            _lib.check(_lib.load().tqb_stage2(a, st))
+        else:
+            _lib.check(_lib.load().tqb_stage2_typed(a, _DTYPE_ID[output.dtype], output.data_ptr(), st))
     return output, lse
+
+
+def rotate_query(query: torch.Tensor, rotation: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                 stream: Optional[int] = None) -> torch.Tensor:
+    """``float(query) @ rotation`` for ``query [B, Hq, D]`` (float32, float16
+    or bfloat16, unit stride over D) and ``rotation = Pi^T [D, D]`` float32:
+    the launcher's cast + GEMM + copy (reference/soa_decode_v1.py:535-538) in
+    one kernel, fp32 accumulation.  Writes ``out`` (float32 [B, Hq, D],
+    allocated when None) and returns it."""
+    _require(isinstance(query, torch.Tensor) and query.is_cuda and query.dtype in _DTYPE_ID,
+             "query must be a float32/float16/bfloat16 CUDA tensor")
+    _cuda(rotation, "rotation", torch.float32)
+    _require(query.dim() == 3 and query.shape[2] == HEAD_DIM and query.stride(2) == 1,
+             "query must be [B, Hq, 128] with unit stride over the last dim")
+    _require(tuple(rotation.shape) == (HEAD_DIM, HEAD_DIM) and rotation.is_contiguous(),
+             "rotation must be a contiguous [128, 128] matrix")
+    B, Hq, D = query.shape
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
+    _cuda(out, "out", torch.float32)
+    _require(tuple(out.shape) == (B, Hq, D) and out.stride(2) == 1, "out must be [B, Hq, 128]")
+    a = RotateArgs()
+    a.query, a.query_dtype = query.data_ptr(), _DTYPE_ID[query.dtype]
+    a.q_stride_b, a.q_stride_h = query.stride(0), query.stride(1)
+    a.rotation, a.q_rot = rotation.data_ptr(), out.data_ptr()
+    a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
+    a.batch, a.num_q_heads, a.head_dim = B, Hq, D
+    with torch.cuda.device(query.device):
+        _lib.check(_lib.load().tqb_rotate_query(a, stream if stream is not None else _stream(query.device)))
+    return out
 
 
 def merge_partials(partials: torch.Tensor, output: torch.Tensor, lse: Optional[torch.Tensor] = None, *,
