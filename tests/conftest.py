@@ -71,9 +71,11 @@ def cuda_device():
     return torch.device("cuda:0")
 
 
-def random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0):
+def random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0, layout="soa"):
     """Seeded cache written by the CPU oracle store (reference semantics),
-    shuffled block pool, random garbage in unused slots."""
+    shuffled block pool, random garbage in unused slots.  ``layout="aos"``
+    writes the AoS cache as the reference AoS store does (the norm correction
+    is applied by the AoS decode, not folded into the stored norm)."""
     import tqb
     from oracle import oracle as O
     from tqb import layout as L
@@ -98,7 +100,10 @@ def random_case(seed, B, Hq, Hk, seq_lens, pool_extra=3, block_stride_pad=0):
     R = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
     y = ((key / (norms[:, None] + 1e-8)) @ R).astype(np.float32)
     val = rng.standard_normal((ntok * Hk, 128)).astype(np.float32)
-    O.store(O.LAYOUT_SOA, y, norms, val, mids, cents, slots, cache, norm_correction=True)
+    if layout == "soa":
+        O.store(O.LAYOUT_SOA, y, norms, val, mids, cents, slots, cache, norm_correction=True)
+    else:
+        O.store(O.LAYOUT_AOS, y, norms, val, mids, cents, slots, cache, norm_correction=False)
     q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
     return dict(q_rot=q, kv_cache=cache, block_table=bt, seq_lens=np.asarray(seq_lens, np.int32),
                 centroids=cents)

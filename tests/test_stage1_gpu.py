@@ -107,6 +107,17 @@ def test_gqa_shapes_vs_oracle(cuda_device, hq, hk):
     _check(_run(cuda_device, z, S=S), ref, f"GQA {hq}/{hk}")
 
 
+@pytest.mark.parametrize("hq,hk", [(32, 8), (64, 8), (8, 1), (16, 2), (16, 4), (32, 4), (8, 8), (48, 16), (12, 3)])
+def test_aos_gqa_shapes_vs_oracle(cuda_device, hq, hk):
+    """AoS cache: KV head counts dividing 8 run on the TMA page ring (whole
+    blocks per run), the others on the register kernel."""
+    z = random_case(hq * 100 + hk + 7, 3, hq, hk, [300, 17, 1024], layout="aos")
+    S = 5
+    ref = O.stage1(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                   layout=O.LAYOUT_AOS)
+    _check(_run(cuda_device, z, layout="aos", S=S), ref, f"AoS GQA {hq}/{hk}")
+
+
 def test_ragged_per_sequence_splits(cuda_device):
     lens = [512, 1, 16, 17, 4000, 777, 33, 1500]
     z = random_case(5, len(lens), 32, 8, lens)

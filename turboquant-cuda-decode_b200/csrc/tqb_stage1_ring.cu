@@ -56,7 +56,16 @@ static_assert(kMetaOff + kGroupWarps * kMetaSlot <= kStageBytes && kStageBytes %
 constexpr int kQRowBytes = kHeadDim * 4;                       // one fp32 query row
 constexpr int kStgBytes = 2 * kQRowBytes;                      // per-warp output staging
 constexpr int kLutStride = 256;                                // bytes per table entry
-constexpr int kLutCopies = 32;                                 // one copy per lane
+// K table entry: SoA {C_hi pair, C_lo pair} with one copy per lane; AoS adds
+// the byte's squared centroid sum (for the in-kernel norm correction) in a
+// 16-byte entry with 16 copies (128-bit loads are served 8 lanes at a time).
+template <int LAYOUT>
+struct Lut {
+    static constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
+    static constexpr int kCopies = 256 / kEntry;
+};
+constexpr int kAosSlot = 134;                                   // AoS bytes per (token, head)
+constexpr int kAosHead = kBlockSize * kAosSlot;                 // 2144: one head's slots of a page
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
 constexpr int kLutAddr = 0x10000;                              // shared address of the table
 constexpr int kDynBase = 0x400;  // shared address of dynamic shared memory (1 KB reserved below it)
@@ -196,6 +205,11 @@ __device__ __forceinline__ uint2 lut_ld(uint32_t a) {
     asm("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(a));
     return r;
 }
+__device__ __forceinline__ uint4 lut_ld4(uint32_t a) {
+    uint4 r;
+    asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 r;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
@@ -210,6 +224,24 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     uint32_t r;
     asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(r) : "r"(a));
     return r;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short r;
+    asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(r) : "r"(a));
+    return r;
+}
+// 16 / 8 bytes at a 2-byte aligned shared address (AoS slots are 134 bytes):
+// the covering aligned words, funnel-shifted into place.
+__device__ __forceinline__ uint4 lds128_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+__device__ __forceinline__ uint2 lds64_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8);
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
 }
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {
     const uint4 u = lds128(a);
@@ -409,7 +441,7 @@ struct GroupSmem {
 // Runs at kProducerRegs registers, so run parameters live one run per lane
 // and block ids are fetched one stage ahead into a single register.
 // ---------------------------------------------------------------------------
-template <int NT>
+template <int NT, int LAYOUT>
 __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M, const GroupSmem& gs, int gi,
                                         int lane, int pj, int npj) {
     using C = Cfg<NT>;
@@ -515,8 +547,13 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             }
             __syncwarp();
             // Lane r < nruns copies run r: its head slices as boxes of 8/4/2/1
-            // heads (one box when the run is a whole group) and its metadata.
-            if (mine && here) {
+            // heads (one box when the run is a whole group) and its metadata
+            // (SoA), or its whole block, unchanged, in one bulk copy (AoS:
+            // a run is all Hk heads of one (b, s), Hk dividing 8).
+            if (LAYOUT == TQB_LAYOUT_AOS && mine && here) {
+                bulk_g2s(gs.stage(slot) + (uint32_t)col * kAosHead, P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes,
+                         (uint32_t)r_nw * kAosHead, gs.full(slot), stream_policy);
+            } else if (mine && here) {
                 const uint32_t dst = gs.stage(slot);
                 int off = 0;
 #pragma unroll
@@ -569,10 +606,13 @@ struct ItemState {
 struct LaneSmem {
     uint32_t k0, k1;  // K bytes [16c, 16c+16) of tokens tau(g), tau(g)+1
     uint32_t v0, v1;  // V bytes [8g, 8g+8) of tokens 2c, 2c+1 (2c+8, 2c+9: + 1024)
-    uint32_t meta;    // knorm pair of tokens tau(g), tau(g)+1 (vscale +32, vzero +64)
+    uint32_t meta;    // SoA: knorm pair of tokens tau(g), tau(g)+1 (vscale +32, vzero +64);
+                      // AoS: knorm of token tau(g) (token tau(g)+1: + row)
+    uint32_t row;     // AoS: bytes between consecutive tokens of a page
+    uint32_t row8;    // bytes between tokens t and t + 8
 };
 
-template <int NT>
+template <int NT, int LAYOUT>
 __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, const LaneSmem& o, bool page_ok,
                                           int tok0, int start, int end, uint32_t lut_sel_src, int g,
                                           int c, int src_a, uint32_t release_bar) {
@@ -580,14 +620,33 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     // its next page is fetched while this one is computed.  The arrive has
     // release semantics: the reads above it are performed before the
     // producer can observe the arrival.
-    const uint4 k0 = lds128(sb + o.k0), k1 = lds128(sb + o.k1);
-    const uint32_t kn = lds32(sb + o.meta);
-    const uint32_t vsp = lds32(sb + o.meta + 32), vzp = lds32(sb + o.meta + 64);
+    uint4 k0, k1;
+    uint32_t kn, vsp, vzp;
     uint2 v[4];
-    v[0] = lds64(sb + o.v0);
-    v[1] = lds64(sb + o.v1);
-    v[2] = lds64(sb + o.v0 + 8 * kDataBytes);
-    v[3] = lds64(sb + o.v1 + 8 * kDataBytes);
+    if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
+        k0 = lds128(sb + o.k0);
+        k1 = lds128(sb + o.k1);
+        kn = lds32(sb + o.meta);
+        vsp = lds32(sb + o.meta + 32);
+        vzp = lds32(sb + o.meta + 64);
+        v[0] = lds64(sb + o.v0);
+        v[1] = lds64(sb + o.v1);
+        v[2] = lds64(sb + o.v0 + o.row8);
+        v[3] = lds64(sb + o.v1 + o.row8);
+    } else {
+        // AoS slot [K 64 | knorm | V 64 | vscale | vzero]; o.meta = knorm of
+        // token tau(g), token tau(g)+1 one row (o.row) further
+        k0 = lds128_a2(sb + o.k0);
+        k1 = lds128_a2(sb + o.k1);
+        const uint32_t m0 = sb + o.meta, m1 = m0 + o.row;
+        kn = __byte_perm(lds16(m0), lds16(m1), 0x5410);
+        vsp = __byte_perm(lds16(m0 + 2 + kVBytes), lds16(m1 + 2 + kVBytes), 0x5410);
+        vzp = __byte_perm(lds16(m0 + 4 + kVBytes), lds16(m1 + 4 + kVBytes), 0x5410);
+        v[0] = lds64_a2(sb + o.v0);
+        v[1] = lds64_a2(sb + o.v1);
+        v[2] = lds64_a2(sb + o.v0 + o.row8);
+        v[3] = lds64_a2(sb + o.v1 + o.row8);
+    }
     mbar_arrive(release_bar);
     const bool va = page_ok && tok0 >= start && tok0 < end;
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
@@ -600,22 +659,46 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
             for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
+    float csq0 = 0.0f, csq1 = 0.0f;  // AoS: this lane's part of the tokens' sum of c^2
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(k0, ks >> 1), w1 = word_of(k1, ks >> 1);
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // address 0x10000 | (K byte << 8) | lane copy offset, in one PRMT
-        const uint2 e0 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jA << 4)));
-        const uint2 e1 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jB << 4)));
-        const uint2 e2 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jA << 4)));
-        const uint2 e3 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jB << 4)));
+        const uint32_t aA0 = prmt(w0, lut_sel_src, 0x6504u | (jA << 4));
+        const uint32_t aB0 = prmt(w0, lut_sel_src, 0x6504u | (jB << 4));
+        const uint32_t aA1 = prmt(w1, lut_sel_src, 0x6504u | (jA << 4));
+        const uint32_t aB1 = prmt(w1, lut_sel_src, 0x6504u | (jB << 4));
+        uint2 e0, e1, e2, e3;
+        if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
+            e0 = lut_ld(aA0);
+            e1 = lut_ld(aB0);
+            e2 = lut_ld(aA1);
+            e3 = lut_ld(aB1);
+        } else {
+            const uint4 f0 = lut_ld4(aA0), f1 = lut_ld4(aB0), f2 = lut_ld4(aA1), f3 = lut_ld4(aB1);
+            e0 = make_uint2(f0.x, f0.y);
+            e1 = make_uint2(f1.x, f1.y);
+            e2 = make_uint2(f2.x, f2.y);
+            e3 = make_uint2(f3.x, f3.y);
+            csq0 += __uint_as_float(f0.z) + __uint_as_float(f1.z);
+            csq1 += __uint_as_float(f2.z) + __uint_as_float(f3.z);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
             mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
     }
-    const float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
+    float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
+    if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
+        // norm correction c / |c| (reference/aos_decode.py:199-206): the four
+        // lanes of a token (c = 0..3) hold its 128 dims between them
+        csq0 = warp_sum_xor(csq0, 1, 2);
+        csq1 = warp_sum_xor(csq1, 1, 2);
+        kn0 *= rsqrtf(csq0 + 1e-16f);
+        kn1 *= rsqrtf(csq1 + 1e-16f);
+    }
     const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
     const float vs1 = vb ? half_bits_to_float(vsp >> 16) : 0.0f;
     const float vz0 = va ? half_bits_to_float(vzp) : 0.0f;
@@ -758,7 +841,7 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
 
 // One page from ring slot S (a compile-time constant, so every shared and
 // barrier address below is a register plus an immediate).
-template <int NT, int S>
+template <int NT, int LAYOUT, int S>
 __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
                                           int k, int my_np, int w, int tok_first, int start, int end,
                                           uint32_t lut_sel_src, int g, int c, int src_a) {
@@ -768,7 +851,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
     // all 32 lanes arrive on the slot's release barrier (no branch on the lane)
     if (k < my_np) {
         const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
-        page_math<NT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
+        page_math<NT, LAYOUT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
                       lut_sel_src, g, c, src_a, gs.empty<NS>(S));
     } else {
         mbar_arrive(gs.empty<NS>(S));
@@ -776,7 +859,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
     return true;
 }
 
-template <int NT>
+template <int NT, int LAYOUT>
 __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& gs, int gi, int w, int lane,
                                         int ec) {
     using C = Cfg<NT>;
@@ -784,16 +867,35 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     const int g = lane >> 2, c = lane & 3;
     const uint32_t t_first = lds32(gs.tiles()), t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     // PRMT source: byte 0 = this lane's copy offset, byte 1 = table page 0x01, byte 2 = 0
-    const uint32_t lut_sel_src = (uint32_t)(lane % kLutCopies) * 8u | ((uint32_t)(kLutAddr >> 16) << 8);
+    using L = Lut<LAYOUT>;
+    const uint32_t lut_sel_src = (uint32_t)(lane % L::kCopies) * (uint32_t)L::kEntry |
+                                 ((uint32_t)(kLutAddr >> 16) << 8);
     const int tau = 8 * (g >> 2) + 2 * ((g >> 1) & 1) + 4 * (g & 1);
-    auto sw = [](int t, int chunk) { return (uint32_t)(t * kDataBytes + ((chunk ^ (t & 7)) << 4)); };
-    const uint32_t colw = gs.ring + (uint32_t)w * kColBytes;  // shared address of this warp's column
     LaneSmem o;
-    o.k0 = colw + sw(tau, c);
-    o.k1 = colw + sw(tau + 1, c);
-    o.v0 = colw + sw(2 * c, 4 + (g >> 1)) + 8u * (g & 1);
-    o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
-    o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
+    if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
+        auto sw = [](int t, int chunk) { return (uint32_t)(t * kDataBytes + ((chunk ^ (t & 7)) << 4)); };
+        const uint32_t colw = gs.ring + (uint32_t)w * kColBytes;  // shared address of this warp's column
+        o.k0 = colw + sw(tau, c);
+        o.k1 = colw + sw(tau + 1, c);
+        o.v0 = colw + sw(2 * c, 4 + (g >> 1)) + 8u * (g & 1);
+        o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
+        o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
+        o.row = 0;
+        o.row8 = 8u * kDataBytes;
+    } else {
+        // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
+        // (w - kvh) * 2144 bytes of the stage: [16 tokens][Hk][134-byte slot].
+        const int kvh = w % P.Hk;
+        const uint32_t row = (uint32_t)P.Hk * kAosSlot;
+        const uint32_t head = gs.ring + (uint32_t)(w - kvh) * kAosHead + (uint32_t)kvh * kAosSlot;
+        o.k0 = head + (uint32_t)tau * row + 16u * c;
+        o.k1 = o.k0 + row;
+        o.v0 = head + (uint32_t)(2 * c) * row + kKBytes + 2 + 8u * g;
+        o.v1 = o.v0 + row;
+        o.meta = head + (uint32_t)tau * row + kKBytes;
+        o.row = row;
+        o.row8 = 8u * row;
+    }
     // Owner of token 2c in the Q.K layout: tau(g') = 2c for g' = bitswap(c).
     const int src_a = 4 * (((c & 1) << 1) | (c >> 1)) + (g >> 1);
     uint32_t tq = 0;     // tiles done (query-barrier phase)
@@ -867,12 +969,12 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
         const int tok_first = (start / kBlockSize) * kBlockSize + tau;
         for (int k = 0; k < np_tile; k += NS) {
-            if (!page_step<NT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a))
+            if (!page_step<NT, LAYOUT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a))
                 return;
-            if (k + 1 < np_tile && !page_step<NT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
+            if (k + 1 < np_tile && !page_step<NT, LAYOUT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
                                                      lut_sel_src, g, c, src_a))
                 return;
-            if (k + 2 < np_tile && !page_step<NT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
+            if (k + 2 < np_tile && !page_step<NT, LAYOUT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
                                                      lut_sel_src, g, c, src_a))
                 return;
         }
@@ -880,7 +982,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     }
 }
 
-template <int NT>
+template <int NT, int LAYOUT>
 __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     stage1_ring_kernel(const Stage1Params P, const __grid_constant__ RingMaps M) {
     using C = Cfg<NT>;
@@ -901,12 +1003,17 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     if (planner >= 0)
         tile_walk(P, planner, C::kGroups, num_tiles, walk, lane);
     else
-        for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
-        const int byte = e / kLutCopies;
-        const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
+        for (int e = tid; e < 256 * Lut<LAYOUT>::kCopies; e += C::kThreads - 32 * C::kGroups) {
+        const int byte = e / Lut<LAYOUT>::kCopies;
+        const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
+        const float clo = a * cscale, chi = b * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
-        *reinterpret_cast<uint2*>(smem + C::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
+        uint8_t* dst = smem + C::kLutOff + (size_t)e * Lut<LAYOUT>::kEntry;
+        if constexpr (LAYOUT == TQB_LAYOUT_SOA)
+            *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
+        else
+            *reinterpret_cast<uint4*>(dst) = make_uint4(h2_as_u32(h), h2_as_u32(l), __float_as_uint(a * a + b * b), 0u);
         }
 
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -947,23 +1054,23 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     if (producer) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::kProducerRegs));
         const int pj = (warp - C::kComputeWarps) / C::kGroups;
-        if (pj < kProducersPerGroup) produce<NT>(P, M, gs, gi, lane, pj, kProducersPerGroup);
+        if (pj < kProducersPerGroup) produce<NT, LAYOUT>(P, M, gs, gi, lane, pj, kProducersPerGroup);
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::kComputeRegs));
-        consume<NT>(P, gs, gi, warp % kGroupWarps, lane, ec);
+        consume<NT, LAYOUT>(P, gs, gi, warp % kGroupWarps, lane, ec);
     }
 }
 
 // True when the compiled kernel launches with enough registers per thread
 // for its setmaxnreg split (otherwise a setmaxnreg.inc could wait forever,
 // so the ring kernel is not used).
-template <int NT>
+template <int NT, int LAYOUT>
 bool ring_registers_ok() {
     using C = Cfg<NT>;
     static int ok = -1;
     if (ok < 0) {
         cudaFuncAttributes a{};
-        ok = cudaFuncGetAttributes(&a, stage1_ring_kernel<NT>) == cudaSuccess &&
+        ok = cudaFuncGetAttributes(&a, stage1_ring_kernel<NT, LAYOUT>) == cudaSuccess &&
              (int64_t)a.numRegs * C::kThreads >=
                  (int64_t)C::kComputeWarps * 32 * C::kComputeRegs + 128 * C::kProducerRegs &&
              a.maxThreadsPerBlock >= C::kThreads;
@@ -994,22 +1101,25 @@ EncodeTiledFn encoder() {
     return fn;
 }
 
-// Tensor maps of the page data and query rows of one launch; false when the
-// driver rejects them.
+// Tensor maps of the page data (SoA) and query rows of one launch; false
+// when the driver rejects them.
 bool encode_maps(const Stage1Params& P, RingMaps& M) {
     EncodeTiledFn enc = encoder();
     if (!enc) return false;
-    const cuuint64_t nblk = P.num_blocks > 0 ? (cuuint64_t)P.num_blocks : (cuuint64_t)0x7fffffff;
-    const cuuint64_t dims[4] = {(cuuint64_t)kDataBytes, (cuuint64_t)kBlockSize, (cuuint64_t)P.Hk, nblk};
-    const cuuint64_t strides[3] = {(cuuint64_t)P.Hk * kDataBytes, (cuuint64_t)kDataBytes, (cuuint64_t)P.block_bytes};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
-    for (int i = 0; i < 4; i++) {
-        const int heads = (kGroupWarps >> i) < P.Hk ? (kGroupWarps >> i) : P.Hk;
-        const cuuint32_t box[4] = {(cuuint32_t)kDataBytes, (cuuint32_t)kBlockSize, (cuuint32_t)heads, 1};
-        if (enc(&M.page[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(P.cache), dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
+    if (P.layout == TQB_LAYOUT_SOA) {  // AoS pages are plain bulk copies
+        const cuuint64_t nblk = P.num_blocks > 0 ? (cuuint64_t)P.num_blocks : (cuuint64_t)0x7fffffff;
+        const cuuint64_t dims[4] = {(cuuint64_t)kDataBytes, (cuuint64_t)kBlockSize, (cuuint64_t)P.Hk, nblk};
+        const cuuint64_t strides[3] = {(cuuint64_t)P.Hk * kDataBytes, (cuuint64_t)kDataBytes,
+                                       (cuuint64_t)P.block_bytes};
+        for (int i = 0; i < 4; i++) {
+            const int heads = (kGroupWarps >> i) < P.Hk ? (kGroupWarps >> i) : P.Hk;
+            const cuuint32_t box[4] = {(cuuint32_t)kDataBytes, (cuuint32_t)kBlockSize, (cuuint32_t)heads, 1};
+            if (enc(&M.page[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(P.cache), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return false;
+        }
     }
     const cuuint64_t qdims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)P.Hq, (cuuint64_t)P.B};
     const cuuint64_t qstr[2] = {(cuuint64_t)P.qsh * 4, (cuuint64_t)P.qsb * 4};
@@ -1019,10 +1129,10 @@ bool encode_maps(const Stage1Params& P, RingMaps& M) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT>
+template <int NT, int LAYOUT>
 int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream, int num_sms) {
     using C = Cfg<NT>;
-    auto kern = stage1_ring_kernel<NT>;
+    auto kern = stage1_ring_kernel<NT, LAYOUT>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1042,9 +1152,15 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
 }  // namespace
 
 bool stage1_ring_supported(const Stage1Params& P) {
-    const bool regs_ok = P.G <= 4 ? ring_registers_ok<1>() : ring_registers_ok<2>();
+    const bool soa = P.layout == TQB_LAYOUT_SOA;
+    const bool regs_ok = soa ? (P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>())
+                             : (P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>());
+    // AoS: a tile's runs are whole blocks (Hk divides 8) of packed slots, each
+    // copied as one run of Hk * 2144 bytes.
+    const bool aos_ok = P.layout == TQB_LAYOUT_AOS && kGroupWarps % P.Hk == 0 && P.head_stride == kAosSlot &&
+                        P.pos_stride == (int64_t)P.Hk * kAosSlot;
     // Query rows are copied by a tensor map: 16-byte row strides, >= one row.
-    return regs_ok && P.layout == TQB_LAYOUT_SOA && P.G >= 1 && P.G <= 8 &&
+    return regs_ok && (soa || aos_ok) && P.G >= 1 && P.G <= 8 &&
            (reinterpret_cast<uintptr_t>(P.cache) & 15) == 0 && (P.block_bytes & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(P.q) & 15) == 0 && P.qsh >= kHeadDim && (P.qsh & 3) == 0 &&
            P.qsb >= P.qsh && (P.qsb & 3) == 0 && encoder() != nullptr;
@@ -1053,7 +1169,11 @@ bool stage1_ring_supported(const Stage1Params& P) {
 int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     RingMaps M;
     if (!encode_maps(P, M)) return TQB_ERR_UNSUPPORTED;
-    return P.G <= 4 ? launch_ring_t<1>(P, M, stream, num_sms) : launch_ring_t<2>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA)
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_SOA>(P, M, stream, num_sms);
+    return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS>(P, M, stream, num_sms)
+                    : launch_ring_t<2, TQB_LAYOUT_AOS>(P, M, stream, num_sms);
 }
 
 int read_wait_timeouts(unsigned int* count, bool reset) {
