@@ -704,8 +704,8 @@ def main():
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
                      "algorithmic_bytes_per_launch": alg,
-                     "kernel": ("tqb stage1_ring_kernel (TMA page ring)" if args.layout == "soa"
-                                else "tqb stage1_kernel (register ring)")},
+                     "kernel": ("tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)" if args.layout == "soa"
+                                else "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)")},
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "e2e": e2e,

@@ -56,14 +56,7 @@ static_assert(kMetaOff + kGroupWarps * kMetaSlot <= kStageBytes && kStageBytes %
 constexpr int kQRowBytes = kHeadDim * 4;                       // one fp32 query row
 constexpr int kStgBytes = 2 * kQRowBytes;                      // per-warp output staging
 constexpr int kLutStride = 256;                                // bytes per table entry
-// K table entry: SoA {C_hi pair, C_lo pair} with one copy per lane; AoS adds
-// the byte's squared centroid sum (for the in-kernel norm correction) in a
-// 16-byte entry with 16 copies (128-bit loads are served 8 lanes at a time).
-template <int LAYOUT>
-struct Lut {
-    static constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
-    static constexpr int kCopies = 256 / kEntry;
-};
+constexpr int kLutCopies = 32;                                 // one copy per lane
 constexpr int kAosSlot = 134;                                   // AoS bytes per (token, head)
 constexpr int kAosHead = kBlockSize * kAosSlot;                 // 2144: one head's slots of a page
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
@@ -205,11 +198,7 @@ __device__ __forceinline__ uint2 lut_ld(uint32_t a) {
     asm("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(a));
     return r;
 }
-__device__ __forceinline__ uint4 lut_ld4(uint32_t a) {
-    uint4 r;
-    asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
-    return r;
-}
+
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 r;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
@@ -609,13 +598,12 @@ struct LaneSmem {
     uint32_t meta;    // SoA: knorm pair of tokens tau(g), tau(g)+1 (vscale +32, vzero +64);
                       // AoS: knorm of token tau(g) (token tau(g)+1: + row)
     uint32_t row;     // AoS: bytes between consecutive tokens of a page
-    uint32_t row8;    // bytes between tokens t and t + 8
 };
 
 template <int NT, int LAYOUT>
 __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, const LaneSmem& o, bool page_ok,
                                           int tok0, int start, int end, uint32_t lut_sel_src, int g,
-                                          int c, int src_a, uint32_t release_bar) {
+                                          int c, int src_a, uint32_t release_bar, float csq_unscale) {
     // Every ring byte this lane uses is read first and the slot released, so
     // its next page is fetched while this one is computed.  The arrive has
     // release semantics: the reads above it are performed before the
@@ -631,8 +619,8 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         vzp = lds32(sb + o.meta + 64);
         v[0] = lds64(sb + o.v0);
         v[1] = lds64(sb + o.v1);
-        v[2] = lds64(sb + o.v0 + o.row8);
-        v[3] = lds64(sb + o.v1 + o.row8);
+        v[2] = lds64(sb + o.v0 + 8u * kDataBytes);
+        v[3] = lds64(sb + o.v1 + 8u * kDataBytes);
     } else {
         // AoS slot [K 64 | knorm | V 64 | vscale | vzero]; o.meta = knorm of
         // token tau(g), token tau(g)+1 one row (o.row) further
@@ -642,12 +630,10 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         kn = __byte_perm(lds16(m0), lds16(m1), 0x5410);
         vsp = __byte_perm(lds16(m0 + 2 + kVBytes), lds16(m1 + 2 + kVBytes), 0x5410);
         vzp = __byte_perm(lds16(m0 + 4 + kVBytes), lds16(m1 + 4 + kVBytes), 0x5410);
-        v[0] = lds64_a2(sb + o.v0);
-        v[1] = lds64_a2(sb + o.v1);
-        v[2] = lds64_a2(sb + o.v0 + o.row8);
-        v[3] = lds64_a2(sb + o.v1 + o.row8);
+        // V is read (and the slot released) after Q.K: the Gram accumulators
+        // take its registers during the Q.K loop
     }
-    mbar_arrive(release_bar);
+    if constexpr (LAYOUT == TQB_LAYOUT_SOA) mbar_arrive(release_bar);
     const bool va = page_ok && tok0 >= start && tok0 < end;
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
 
@@ -659,45 +645,50 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
             for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
-    float csq0 = 0.0f, csq1 = 0.0f;  // AoS: this lane's part of the tokens' sum of c^2
+    // AoS: Gram products of each M tile with its own C_hi rows (the A
+    // fragment's C_hi registers are exactly the B fragment of A_hi^T):
+    // D[g][g] = sum C_hi^2 and D[g+8][g] = sum C_lo C_hi of token row g.
+    float dcs[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) dcs[mt][k] = 0.0f;
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(k0, ks >> 1), w1 = word_of(k1, ks >> 1);
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // address 0x10000 | (K byte << 8) | lane copy offset, in one PRMT
-        const uint32_t aA0 = prmt(w0, lut_sel_src, 0x6504u | (jA << 4));
-        const uint32_t aB0 = prmt(w0, lut_sel_src, 0x6504u | (jB << 4));
-        const uint32_t aA1 = prmt(w1, lut_sel_src, 0x6504u | (jA << 4));
-        const uint32_t aB1 = prmt(w1, lut_sel_src, 0x6504u | (jB << 4));
-        uint2 e0, e1, e2, e3;
-        if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
-            e0 = lut_ld(aA0);
-            e1 = lut_ld(aB0);
-            e2 = lut_ld(aA1);
-            e3 = lut_ld(aB1);
-        } else {
-            const uint4 f0 = lut_ld4(aA0), f1 = lut_ld4(aB0), f2 = lut_ld4(aA1), f3 = lut_ld4(aB1);
-            e0 = make_uint2(f0.x, f0.y);
-            e1 = make_uint2(f1.x, f1.y);
-            e2 = make_uint2(f2.x, f2.y);
-            e3 = make_uint2(f3.x, f3.y);
-            csq0 += __uint_as_float(f0.z) + __uint_as_float(f1.z);
-            csq1 += __uint_as_float(f2.z) + __uint_as_float(f3.z);
-        }
+        const uint2 e0 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jA << 4)));
+        const uint2 e1 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jB << 4)));
+        const uint2 e2 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jA << 4)));
+        const uint2 e3 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jB << 4)));
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
             mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
+        if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
+            mma_16816(dcs[0], e0.x, e0.y, e1.x, e1.y, e0.x, e1.x);
+            mma_16816(dcs[1], e2.x, e2.y, e3.x, e3.y, e2.x, e3.x);
+        }
     }
     float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
     if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
-        // norm correction c / |c| (reference/aos_decode.py:199-206): the four
-        // lanes of a token (c = 0..3) hold its 128 dims between them
-        csq0 = warp_sum_xor(csq0, 1, 2);
-        csq1 = warp_sum_xor(csq1, 1, 2);
+        // norm correction c / |c| (reference/aos_decode.py:199-206), with
+        // sum c^2 = sum (C_hi + C_lo)^2 = D[g][g] + 2 D[g+8][g] (+ sum C_lo^2,
+        // 2^-22 of it, dropped); lane 4g + g/2 holds column g, element g & 1
+        const int j = g & 1, owner = 4 * g + (g >> 1);
+        const float o0 = (j ? dcs[0][1] : dcs[0][0]) + 2.0f * (j ? dcs[0][3] : dcs[0][2]);
+        const float o1 = (j ? dcs[1][1] : dcs[1][0]) + 2.0f * (j ? dcs[1][3] : dcs[1][2]);
+        const float csq0 = __shfl_sync(0xffffffffu, o0, owner) * csq_unscale;
+        const float csq1 = __shfl_sync(0xffffffffu, o1, owner) * csq_unscale;
         kn0 *= rsqrtf(csq0 + 1e-16f);
         kn1 *= rsqrtf(csq1 + 1e-16f);
+        v[0] = lds64_a2(sb + o.v0);
+        v[1] = lds64_a2(sb + o.v1);
+        v[2] = lds64_a2(sb + o.v0 + (o.row << 3));
+        v[3] = lds64_a2(sb + o.v1 + (o.row << 3));
+        mbar_arrive(release_bar);
     }
     const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
     const float vs1 = vb ? half_bits_to_float(vsp >> 16) : 0.0f;
@@ -844,7 +835,7 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
 template <int NT, int LAYOUT, int S>
 __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
                                           int k, int my_np, int w, int tok_first, int start, int end,
-                                          uint32_t lut_sel_src, int g, int c, int src_a) {
+                                          uint32_t lut_sel_src, int g, int c, int src_a, float csq_unscale) {
     constexpr int NS = Cfg<NT>::kStages;
     if (!mbar_wait(gs.full(S), (cbits >> S) & 1u)) return false;
     cbits ^= 1u << S;
@@ -852,7 +843,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
     if (k < my_np) {
         const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
         page_math<NT, LAYOUT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
-                      lut_sel_src, g, c, src_a, gs.empty<NS>(S));
+                      lut_sel_src, g, c, src_a, gs.empty<NS>(S), csq_unscale);
     } else {
         mbar_arrive(gs.empty<NS>(S));
     }
@@ -867,9 +858,9 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     const int g = lane >> 2, c = lane & 3;
     const uint32_t t_first = lds32(gs.tiles()), t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     // PRMT source: byte 0 = this lane's copy offset, byte 1 = table page 0x01, byte 2 = 0
-    using L = Lut<LAYOUT>;
-    const uint32_t lut_sel_src = (uint32_t)(lane % L::kCopies) * (uint32_t)L::kEntry |
-                                 ((uint32_t)(kLutAddr >> 16) << 8);
+    const uint32_t lut_sel_src = (uint32_t)(lane % kLutCopies) * 8u | ((uint32_t)(kLutAddr >> 16) << 8);
+    // the table's centroids are scaled by 2^ec: sums of their squares by 2^(2 ec)
+    const float csq_unscale = exp2i(-2 * ec);
     const int tau = 8 * (g >> 2) + 2 * ((g >> 1) & 1) + 4 * (g & 1);
     LaneSmem o;
     if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
@@ -881,7 +872,6 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
         o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
         o.row = 0;
-        o.row8 = 8u * kDataBytes;
     } else {
         // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
         // (w - kvh) * 2144 bytes of the stage: [16 tokens][Hk][134-byte slot].
@@ -894,7 +884,6 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.v1 = o.v0 + row;
         o.meta = head + (uint32_t)tau * row + kKBytes;
         o.row = row;
-        o.row8 = 8u * row;
     }
     // Owner of token 2c in the Q.K layout: tau(g') = 2c for g' = bitswap(c).
     const int src_a = 4 * (((c & 1) << 1) | (c >> 1)) + (g >> 1);
@@ -969,13 +958,13 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
         const int tok_first = (start / kBlockSize) * kBlockSize + tau;
         for (int k = 0; k < np_tile; k += NS) {
-            if (!page_step<NT, LAYOUT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a))
+            if (!page_step<NT, LAYOUT, 0>(st, gs, o, cbits, k, my_np, w, tok_first, start, end, lut_sel_src, g, c, src_a, csq_unscale))
                 return;
             if (k + 1 < np_tile && !page_step<NT, LAYOUT, 1>(st, gs, o, cbits, k + 1, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a))
+                                                     lut_sel_src, g, c, src_a, csq_unscale))
                 return;
             if (k + 2 < np_tile && !page_step<NT, LAYOUT, 2>(st, gs, o, cbits, k + 2, my_np, w, tok_first, start, end,
-                                                     lut_sel_src, g, c, src_a))
+                                                     lut_sel_src, g, c, src_a, csq_unscale))
                 return;
         }
         if (my_np > 0) epilogue<NT>(P, st, gs.stg + (uint32_t)w * kStgBytes, b, s, kvh, g, c, lane);
@@ -1003,17 +992,12 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     if (planner >= 0)
         tile_walk(P, planner, C::kGroups, num_tiles, walk, lane);
     else
-        for (int e = tid; e < 256 * Lut<LAYOUT>::kCopies; e += C::kThreads - 32 * C::kGroups) {
-        const int byte = e / Lut<LAYOUT>::kCopies;
-        const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
-        const float clo = a * cscale, chi = b * cscale;
+        for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
+        const int byte = e / kLutCopies;
+        const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
-        uint8_t* dst = smem + C::kLutOff + (size_t)e * Lut<LAYOUT>::kEntry;
-        if constexpr (LAYOUT == TQB_LAYOUT_SOA)
-            *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
-        else
-            *reinterpret_cast<uint4*>(dst) = make_uint4(h2_as_u32(h), h2_as_u32(l), __float_as_uint(a * a + b * b), 0u);
+        *reinterpret_cast<uint2*>(smem + C::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
         }
 
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
