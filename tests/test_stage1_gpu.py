@@ -21,7 +21,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN_CASES, assert_close, random_case
+from conftest import GOLDEN_CASES, RTOL, assert_close, random_case
 from oracle import oracle as O
 import tqb
 from tqb import layout as L
@@ -205,3 +205,43 @@ def test_errors_raise(cuda_device, golden):
         tqb.stage1(q, kv, bt, sl, c, torch.empty(2, 32, 4, 128, device=dev))
     with pytest.raises(tqb.TqbError):
         tqb.stage1(q[:, :30], kv, bt, sl, c, torch.empty(2, 30, 4, 129, device=dev))
+
+
+@pytest.mark.parametrize("layout,qdtype", [("soa", torch.float32), ("soa", torch.bfloat16),
+                                            ("aos", torch.float32), ("aos", torch.float16)])
+def test_decode_launcher_vs_oracle(cuda_device, layout, qdtype):
+    """The production launchers (reference/soa_decode_v1.py and
+    reference/aos_decode.py ``triton_turboquant_decode_attention``): fused
+    query cast + rotation, Stage1, Stage2 into the query's dtype, against the
+    oracle's Stage1 + Stage2 on ``query.float() @ PiT``."""
+    from tqb import compat, compat_aos
+    dev = cuda_device
+    lens = [300, 17, 1024, 0, 555]
+    z = random_case(41 + (layout == "aos"), len(lens), 32, 8, lens, layout=layout)
+    rng = np.random.default_rng(3)
+    Pi = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    query = torch.from_numpy(rng.standard_normal((len(lens), 32, 128)).astype(np.float32)).to(qdtype)
+    q_rot = (query.float() @ torch.from_numpy(Pi).T).numpy()
+    S = 8
+    mid = O.stage1(q_rot, z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                   layout=O.LAYOUT_SOA if layout == "soa" else O.LAYOUT_AOS)
+    ref_out, ref_lse = O.stage2(mid, z["seq_lens"])
+    fn = compat.triton_turboquant_decode_attention if layout == "soa" else \
+        compat_aos.triton_turboquant_decode_attention
+    lse = torch.empty(len(lens), 32, device=dev)
+    out = fn(query.to(dev), _to(dev, z, "kv_cache"), _to(dev, z, "block_table"), _to(dev, z, "seq_lens"),
+             torch.from_numpy(Pi).to(dev), _to(dev, z, "centroids"), 1.0 / math.sqrt(128), 4, 66, 4,
+             norm_correction=True, max_num_kv_splits=S, lse_buf=lse)
+    torch.cuda.synchronize()
+    assert out.dtype == qdtype and tuple(out.shape) == (len(lens), 32, 128)
+    live = np.asarray(lens) > 0
+    got = out.float().cpu().numpy()
+    ref = ref_out.astype(np.float32)
+    if qdtype == torch.float32:
+        assert_close(got[live], ref[live], what=f"{layout} decode out")
+    else:  # the fp32 result rounded to 16 bits: one unit in the last place more
+        ulp = 2.0 ** -7 if qdtype == torch.bfloat16 else 2.0 ** -10
+        assert_close(got[live], torch.from_numpy(ref[live]).to(qdtype).float().numpy(),
+                     rtol=RTOL + ulp, what=f"{layout} decode out")
+    assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"{layout} decode lse")
+    assert np.all(np.isnan(got[~live])), "a sequence without tokens gets NaN, as in the reference"

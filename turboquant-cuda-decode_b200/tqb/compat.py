@@ -133,6 +133,17 @@ def triton_turboquant_decode_attention(
         raise NotImplementedError("only the turboquant_4bit_nc preset (4-bit K and V) is supported")
     if sinks is not None:
         raise NotImplementedError("attention sinks are not supported yet")
+    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, "soa", PiT=PiT,
+                            mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
+                            max_num_kv_splits=max_num_kv_splits)
+
+
+def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, *, PiT=None,
+                     mid_o_buf=None, output_buf=None, lse_buf=None, buf_holder=None,
+                     max_num_kv_splits: int = 32) -> torch.Tensor:
+    """Query rotation, Stage1 on the ``layout`` ("soa"/"aos") cache, Stage2;
+    the body of both reference launchers (reference/soa_decode_v1.py:486-643,
+    reference/aos_decode.py:486-...) with the buffer reuse they offer."""
     B, Hq, D = query.shape
     if PiT is None:
         PiT = Pi.T.contiguous()
@@ -149,7 +160,7 @@ def triton_turboquant_decode_attention(
         mid_o = torch.empty(B, Hq, S, D + 1, dtype=torch.float32, device=query.device)
         if buf_holder is not None:
             buf_holder._tq_mid_o_buf = mid_o
-    ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout="soa",
+    ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout=layout,
                attn_scale=scale)
     if query.dtype in (torch.float16, torch.bfloat16):
         # Stage2 writes the query's dtype directly (the reference merges into
