@@ -51,8 +51,8 @@ CONFIGS = {
                workload="Llama-3-70B-shaped decode: B256 x 8192 ctx, Hq64/Hk8 (GQA-8), 32 splits; "
                         "TP by KV head"),
     "c4": dict(B=4, L=131072, Hq=32, Hk=8, S=74, parallel="sp",
-               workload="long-context decode: B4 x 131072 ctx, Hq32/Hk8; SP split-KV, NCCL all-gather of "
-                        "partials + merge kernel; 74 local splits per GPU: 4 x 74 x 8 KV heads = 296 tiles, "
+               workload="long-context decode: B4 x 131072 ctx, Hq32/Hk8; SP split-KV, merged rows exchanged "
+                        "over peer memory (NVLink P2P) and merged; 74 local splits per GPU: 4 x 74 x 8 KV heads = 296 tiles, "
                         "one per Stage1 group on 148 SMs (the reference config's 16 leave most SMs idle; "
                         "the merge kernel combines any split count)"),
 }
@@ -456,13 +456,20 @@ def run_sharded(args, world, rank, local):
     mid = torch.empty(B, Hq, S, 129, device=dev)
     out = torch.empty(B, Hq, 128, device=dev)
     lse = torch.empty(B, Hq, device=dev)
-    part = torch.empty(B, Hq, 129, device=dev)
     fout = torch.empty(B, Hq, 128, device=dev)
     flse = torch.empty(B, Hq, device=dev)
 
+    sp = cfg["parallel"] == "sp"
+    # SP: the local Stage2, the exchange of the merged rows and the
+    # cross-range merge are the peer-memory exchange (tqb_sp_exchange +
+    # tqb_sp_merge: rows stored straight into every rank's buffer over
+    # NVLink), not Stage2 + NCCL all-gather + merge kernel.
+    ex = sharding.P2PExchange(B, Hq, dev) if sp else None
+
     def local_step():
         tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, num_splits_per_seq=w["nsplits"])
-        tqb.stage2(mid, w["seq_lens"], out, lse, num_splits_per_seq=w["nsplits"])
+        if not sp:
+            tqb.stage2(mid, w["seq_lens"], out, lse, num_splits_per_seq=w["nsplits"])
 
     cap = torch.cuda.Stream(dev)
     with torch.cuda.stream(cap):
@@ -475,11 +482,8 @@ def run_sharded(args, world, rank, local):
 
     def step():
         g.replay()
-        if cfg["parallel"] == "sp":
-            part[..., :128] = out
-            part[..., 128] = lse
-            parts = sharding.gather_partials(part)
-            tqb.merge_partials(parts, fout, flse)
+        if sp:
+            ex.step(mid, w["seq_lens"], fout, flse, num_splits_per_seq=w["nsplits"])
 
     for _ in range(args.warmup):
         step()
@@ -519,13 +523,15 @@ def run_sharded(args, world, rank, local):
             "rank0_stage1_hbm_gbs": cache_bytes / (s1_ms * 1e-3) / 1e9,
             "rank0_stage1_frac_of_peak": cache_bytes / (s1_ms * 1e-3) / 1e9 / peak,
             "peak_source": peak_kind,
-            "timing": "step = CUDA-graph replay of the local Stage1+Stage2" +
-                      (" + NCCL all-gather + merge kernel" if cfg["parallel"] == "sp" else "") +
-                      ", CUDA events, max over ranks",
+            "timing": ("step = CUDA-graph replay of the local Stage1 + the peer-memory exchange "
+                       "(Stage2 rows to every rank over NVLink, then the merge)" if sp else
+                       "step = CUDA-graph replay of the local Stage1+Stage2") + ", CUDA events, max over ranks",
             "e2e": None, "e2e_note": "the end-to-end leg is measured on the c1 headline config",
         }
         print(json.dumps(line), flush=True)
     del g
+    if ex is not None:
+        ex.close()
 
 
 def main():

@@ -226,6 +226,57 @@ typedef struct tqb_decode_static_args {
 
 int tqb_decode_static(const tqb_decode_static_args* args, cudaStream_t stream);
 
+/*
+ * Sequence-parallel exchange over peer memory (no reference counterpart: the
+ * reference is single-GPU).  Each rank of one node allocates an exchange
+ * buffer of tqb_p2p_buffer_bytes(world, cap_rows) bytes with tqb_p2p_alloc,
+ * exports it with tqb_ipc_export, and maps every other rank's buffer with
+ * tqb_ipc_import (the handles travel over the caller's own channel).  Per
+ * decode step, after the local Stage1:
+ *   tqb_sp_exchange: Stage2 of this rank's splits, each merged (O, LSE) row
+ *     stored straight into every rank's buffer over NVLink, then the step's
+ *     epoch published to every rank;
+ *   tqb_sp_merge: waits (bounded, about a second) for every rank's epoch and
+ *     merges the G rows per (b, h) into output / lse (the cross-range merge
+ *     of tqb_merge_partials).
+ * epoch is 1 on the first step and grows by one per step, identically on all
+ * ranks; consecutive steps alternate between two row sets, so a rank may run
+ * one step ahead of another.  A merge whose wait gives up writes NaN and
+ * counts in tqb_wait_timeouts.  Every rank must call both, in the same order.
+ */
+#define TQB_P2P_MAX_RANKS 8
+#define TQB_IPC_HANDLE_BYTES 64
+
+int64_t tqb_p2p_buffer_bytes(int32_t world, int64_t cap_rows); /* -1 when out of range */
+int tqb_p2p_alloc(int64_t bytes, void** ptr);                   /* zero-filled device memory */
+int tqb_p2p_free(void* ptr);
+int tqb_ipc_export(const void* ptr, void* handle);              /* handle: TQB_IPC_HANDLE_BYTES */
+int tqb_ipc_import(const void* handle, void** ptr);
+int tqb_ipc_close(void* ptr);
+
+typedef struct tqb_sp_exchange_args {
+    tqb_stage2_args stage2;            /* this rank's Stage2 inputs; output/lse ignored */
+    int32_t rank, world;               /* world <= TQB_P2P_MAX_RANKS */
+    int64_t cap_rows;                  /* rows per slot, >= batch * num_q_heads, same on all ranks */
+    void* buffers[TQB_P2P_MAX_RANKS];  /* every rank's buffer as mapped in this process */
+    uint64_t epoch;
+} tqb_sp_exchange_args;
+
+int tqb_sp_exchange(const tqb_sp_exchange_args* args, cudaStream_t stream);
+
+typedef struct tqb_sp_merge_args {
+    void* buffer;                      /* this rank's exchange buffer */
+    int32_t world, batch, num_q_heads, head_dim;
+    int64_t cap_rows;
+    uint64_t epoch;
+    float* output;                     /* [B, Hq, D] */
+    int64_t out_stride_b, out_stride_h;
+    float* lse;                        /* [B, Hq], may be NULL */
+    int64_t lse_stride_b;
+} tqb_sp_merge_args;
+
+int tqb_sp_merge(const tqb_sp_merge_args* args, cudaStream_t stream);
+
 /* Diagnostics (no reference counterpart).  The SoA Stage1 kernel paces its
  * TMA page ring with mbarrier waits that give up after about a second; each
  * wait that gives up adds one to a per-device counter (the kernel then ends

@@ -87,3 +87,39 @@ def sp_nccl_worker(rank: int, world: int, port: int, case_path: str, out_dir: st
         np.savez(os.path.join(out_dir, f"nccl{rank}.npz"), out=out.cpu().numpy(), lse=lse.cpu().numpy())
     finally:
         dist.destroy_process_group()
+
+
+def sp_p2p_worker(rank: int, world: int, port: int, case_path: str, out_dir: str, local_splits: int):
+    """SP on GPUs with the exchange over peer memory (sp_decode_p2p), three steps."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import tqb
+    from tqb import sharding
+
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    try:
+        dev = torch.device("cuda", rank)
+        with np.load(case_path) as z:
+            c = {k: z[k] for k in z.files}
+        bt, lens, _ = sharding.sp_shard(torch.from_numpy(c["block_table"]), c["seq_lens"].tolist(), world, rank)
+        B = lens.shape[0]
+        ex = sharding.P2PExchange(B, 32, dev)
+        tqb.wait_timeouts(reset=True)
+        outs, lses = [], []
+        try:
+            for _ in range(3):
+                out, lse = sharding.sp_decode_p2p(ex, torch.from_numpy(c["q_rot"]).to(dev),
+                                                  torch.from_numpy(c["kv_cache"]).to(dev), bt.to(dev), lens.to(dev),
+                                                  torch.from_numpy(c["centroids"]).to(dev),
+                                                  local_splits=local_splits)
+                outs.append(out.cpu().numpy())
+                lses.append(lse.cpu().numpy())
+            timeouts = tqb.wait_timeouts(reset=True)
+        finally:
+            ex.close()
+        np.savez(os.path.join(out_dir, f"p2p{rank}.npz"), out=np.stack(outs), lse=np.stack(lses), timeouts=timeouts)
+    finally:
+        dist.destroy_process_group()

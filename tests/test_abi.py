@@ -108,6 +108,8 @@ int main(void) {
   printf("tqb_store_args %zu\n", sizeof(tqb_store_args));
   printf("tqb_decode_static_args %zu\n", sizeof(tqb_decode_static_args));
   printf("tqb_rotate_args %zu\n", sizeof(tqb_rotate_args));
+  printf("tqb_sp_exchange_args %zu\n", sizeof(tqb_sp_exchange_args));
+  printf("tqb_sp_merge_args %zu\n", sizeof(tqb_sp_merge_args));
   %FIELDS%
   return 0;
 }
@@ -117,7 +119,8 @@ int main(void) {
 def test_ctypes_structs_match_c_layout(tmp_path: Path):
     structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
                "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs,
-               "tqb_decode_static_args": _lib.DecodeStaticArgs, "tqb_rotate_args": _lib.RotateArgs}
+               "tqb_decode_static_args": _lib.DecodeStaticArgs, "tqb_rotate_args": _lib.RotateArgs,
+               "tqb_sp_exchange_args": _lib.SpExchangeArgs, "tqb_sp_merge_args": _lib.SpMergeArgs}
     fields = "\n".join(f"F({c}, {f})" for c, py in structs.items() for f, _ in py._fields_)
     src = tmp_path / "probe.c"
     src.write_text(C_LAYOUT_PROBE.replace("%FIELDS%", fields))

@@ -83,6 +83,45 @@ def test_dp_ranks_reassembled(cuda_device):
     assert_close(got[..., 128], ref_lse, what="DP lse")
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sp_p2p_exchange_emulated(cuda_device, world):
+    """The peer-memory SP exchange with every rank of one process on one GPU
+    (local buffers, no IPC): all ranks send, then all merge; three steps, so
+    both row sets and growing epochs are used."""
+    lens = [1000, 17, 4100, 1, 0]
+    c = random_case(200 + world, len(lens), 32, 8, lens)
+    dev = cuda_device
+    ranks = sharding.P2PExchange.emulated(world, len(lens), 32, dev)
+    ref_out, ref_lse = _full_ref(c)
+    live = np.asarray(lens) > 0
+    try:
+        mids = []
+        for r in range(world):
+            bt, sl, _ = sharding.sp_shard(_dev(c, "block_table", dev), lens, world, r)
+            mid = torch.empty(len(lens), 32, 16, 129, device=dev)
+            tqb.stage1(_dev(c, "q_rot", dev), _dev(c, "kv_cache", dev), bt, sl, _dev(c, "centroids", dev), mid)
+            mids.append((mid, sl))
+        tqb.wait_timeouts(reset=True)
+        for step in range(3):
+            for r in range(world):
+                ranks[r].send(*mids[r])
+            outs = []
+            for r in range(world):
+                out = torch.full((len(lens), 32, 128), -1.0, device=dev)
+                lse = torch.empty(len(lens), 32, device=dev)
+                ranks[r].recv(out, lse)
+                outs.append((out, lse))
+            torch.cuda.synchronize()
+            assert tqb.wait_timeouts(reset=True) == 0
+            for r, (out, lse) in enumerate(outs):
+                got = out.cpu().numpy()
+                assert_close(got[live], ref_out[live], what=f"P2P SP{world} step {step} rank {r} output")
+                assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"P2P SP{world} rank {r} lse")
+                assert np.all(np.isnan(got[~live])), "a sequence without tokens merges to NaN"
+    finally:
+        ranks[0].close()
+
+
 @pytest.mark.multigpu
 def test_sp_nccl_two_gpus(tmp_path):
     if torch.cuda.device_count() < 2:
@@ -105,3 +144,31 @@ def test_sp_nccl_two_gpus(tmp_path):
         with np.load(tmp_path / f"nccl{r}.npz") as z:
             assert_close(z["out"], ref_out, what=f"NCCL SP rank {r} output")
             assert_close(z["lse"], ref_lse, what=f"NCCL SP rank {r} lse")
+
+
+@pytest.mark.multigpu
+def test_sp_p2p_two_gpus(tmp_path):
+    """The peer-memory SP exchange between two processes on two GPUs (IPC
+    handles swapped over NCCL, rows stored over NVLink), three steps."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import _dist_workers as W
+
+    lens = [2000, 33, 700]
+    c = random_case(401, len(lens), 32, 8, lens)
+    case = tmp_path / "case.npz"
+    np.savez(case, **c)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(W.sp_p2p_worker, args=(2, port, str(case), str(tmp_path), 8), nprocs=2,
+                       start_method="spawn", join=True)
+    ref_out, ref_lse = _full_ref(c)
+    for r in range(2):
+        with np.load(tmp_path / f"p2p{r}.npz") as z:
+            assert int(z["timeouts"]) == 0
+            for step in range(3):
+                assert_close(z["out"][step], ref_out, what=f"P2P SP rank {r} step {step} output")
+                assert_close(z["lse"][step], ref_lse, what=f"P2P SP rank {r} step {step} lse")

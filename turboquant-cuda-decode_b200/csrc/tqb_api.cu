@@ -80,8 +80,11 @@ int tqb_version(void) { return TQB_VERSION; }
 int tqb_wait_timeouts(unsigned int* count, int reset) {
     g_detail[0] = '\0';
     TQB_REQUIRE(count != nullptr, TQB_ERR_INVALID_ARG, "count is NULL");
-    const int rc = tqb::read_wait_timeouts(count, reset != 0);
-    return rc == TQB_OK ? TQB_OK : TQB_ERR_CUDA;
+    unsigned int ring = 0, p2p = 0;
+    if (tqb::read_wait_timeouts(&ring, reset != 0) != TQB_OK) return TQB_ERR_CUDA;
+    if (tqb::read_p2p_timeouts(&p2p, reset != 0) != TQB_OK) return TQB_ERR_CUDA;
+    *count = ring + p2p;
+    return TQB_OK;
 }
 
 const char* tqb_strerror(int status) {
@@ -221,6 +224,150 @@ int tqb_stage2(const tqb_stage2_args* a, cudaStream_t stream) {
 
 int tqb_stage2_typed(const tqb_stage2_args* a, int out_dtype, void* output, cudaStream_t stream) {
     return stage2_impl(a, output, out_dtype, stream);
+}
+
+// ---- sequence-parallel exchange over peer memory --------------------------
+
+int64_t tqb_p2p_buffer_bytes(int32_t world, int64_t cap_rows) {
+    if (world < 1 || world > tqb::kP2PMaxRanks || cap_rows < 0) return -1;
+    return tqb::p2p_buffer_bytes(world, cap_rows);
+}
+
+int tqb_p2p_alloc(int64_t bytes, void** ptr) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(ptr != nullptr && bytes > 0, TQB_ERR_INVALID_ARG, "ptr is NULL or bytes <= 0");
+    *ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        cudaGetLastError();
+        tqb::set_error_detail(cudaGetErrorString(e));
+        return TQB_ERR_CUDA;
+    }
+    *ptr = p;
+    return TQB_OK;
+}
+
+int tqb_p2p_free(void* ptr) {
+    g_detail[0] = '\0';
+    if (!ptr) return TQB_OK;
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tqb::set_error_detail(cudaGetErrorString(e));
+        return TQB_ERR_CUDA;
+    }
+    return TQB_OK;
+}
+
+int tqb_ipc_export(const void* ptr, void* handle) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(ptr && handle, TQB_ERR_INVALID_ARG, "ptr or handle is NULL");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tqb::set_error_detail(cudaGetErrorString(e));
+        return TQB_ERR_CUDA;
+    }
+    static_assert(sizeof(h) == TQB_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return TQB_OK;
+}
+
+int tqb_ipc_import(const void* handle, void** ptr) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(ptr && handle, TQB_ERR_INVALID_ARG, "ptr or handle is NULL");
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tqb::set_error_detail(cudaGetErrorString(e));
+        return TQB_ERR_CUDA;
+    }
+    return TQB_OK;
+}
+
+int tqb_ipc_close(void* ptr) {
+    g_detail[0] = '\0';
+    if (!ptr) return TQB_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tqb::set_error_detail(cudaGetErrorString(e));
+        return TQB_ERR_CUDA;
+    }
+    return TQB_OK;
+}
+
+int tqb_sp_exchange(const tqb_sp_exchange_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    const tqb_stage2_args* s = &a->stage2;
+    TQB_REQUIRE(a->world >= 1 && a->world <= TQB_P2P_MAX_RANKS && a->rank >= 0 && a->rank < a->world,
+                TQB_ERR_INVALID_ARG, "rank/world out of range");
+    TQB_REQUIRE(a->epoch >= 1, TQB_ERR_INVALID_ARG, "epoch must start at 1");
+    TQB_REQUIRE(s->batch >= 0 && s->num_q_heads > 0 && s->num_splits > 0, TQB_ERR_INVALID_ARG,
+                "batch/heads/num_splits must be positive");
+    TQB_REQUIRE(s->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE((int64_t)s->batch * s->num_q_heads <= a->cap_rows && a->cap_rows < (int64_t(1) << 31),
+                TQB_ERR_INVALID_ARG, "batch * num_q_heads exceeds cap_rows");
+    if (s->batch == 0) return TQB_OK;
+    TQB_REQUIRE(s->mid_o && s->seq_lens, TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    for (int r = 0; r < a->world; r++)
+        TQB_REQUIRE(a->buffers[r] && aligned(a->buffers[r], 8), TQB_ERR_INVALID_ARG,
+                    "every rank's exchange buffer must be given (8-byte aligned)");
+    DeviceGuard guard(a->buffers[a->rank]);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning this rank's buffer");
+    tqb::SpExchangeParams p{};
+    p.s2.mid = s->mid_o;
+    p.s2.msb = s->mid_stride_b;
+    p.s2.msh = s->mid_stride_h;
+    p.s2.mss = s->mid_stride_s;
+    p.s2.seq_lens = s->seq_lens;
+    p.s2.nsplits = s->num_splits_per_seq;
+    p.s2.B = s->batch;
+    p.s2.Hq = s->num_q_heads;
+    p.s2.S = s->num_splits;
+    p.rank = a->rank;
+    p.world = a->world;
+    p.cap_rows = a->cap_rows;
+    for (int r = 0; r < a->world; r++) p.buffers[r] = a->buffers[r];
+    p.epoch = a->epoch;
+    return tqb::launch_sp_exchange(p, stream);
+}
+
+int tqb_sp_merge(const tqb_sp_merge_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->world >= 1 && a->world <= TQB_P2P_MAX_RANKS, TQB_ERR_INVALID_ARG, "world out of range");
+    TQB_REQUIRE(a->epoch >= 1, TQB_ERR_INVALID_ARG, "epoch must start at 1");
+    TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0, TQB_ERR_INVALID_ARG, "batch/heads must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE((int64_t)a->batch * a->num_q_heads <= a->cap_rows && a->cap_rows < (int64_t(1) << 31),
+                TQB_ERR_INVALID_ARG, "batch * num_q_heads exceeds cap_rows");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->buffer && a->output && aligned(a->buffer, 8) && aligned(a->output, 4), TQB_ERR_INVALID_ARG,
+                "buffer/output NULL or misaligned");
+    DeviceGuard guard(a->output);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning output");
+    tqb::SpMergeParams p{};
+    p.buffer = a->buffer;
+    p.world = a->world;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    p.cap_rows = a->cap_rows;
+    p.epoch = a->epoch;
+    p.out = a->output;
+    p.osb = a->out_stride_b;
+    p.osh = a->out_stride_h;
+    p.lse = a->lse;
+    p.lsb = a->lse_stride_b;
+    return tqb::launch_sp_merge(p, stream);
 }
 
 int tqb_rotate_query(const tqb_rotate_args* a, cudaStream_t stream) {

@@ -60,6 +60,26 @@ struct Stage2Params {
     int B, Hq, S;
 };
 
+// Sequence-parallel exchange over peer memory (tqb_p2p.cu).
+constexpr int kP2PMaxRanks = 8;
+struct SpExchangeParams {
+    Stage2Params s2;  // this rank's splits (out/lse unused)
+    int rank, world;
+    int64_t cap_rows;
+    void* buffers[kP2PMaxRanks];  // every rank's exchange buffer, mapped here
+    unsigned long long epoch;
+};
+struct SpMergeParams {
+    void* buffer;  // this rank's exchange buffer
+    int world, B, Hq;
+    int64_t cap_rows;
+    unsigned long long epoch;
+    float* out;
+    int64_t osb, osh;
+    float* lse;
+    int64_t lsb;
+};
+
 // q_rot[b, h, :] = float(q[b, h, :]) @ rot (rot [D, D] row-major fp32).
 struct RotateParams {
     const void* q;
@@ -109,6 +129,10 @@ int read_wait_timeouts(unsigned int* count, bool reset);
 int launch_stage2(const Stage2Params& p, cudaStream_t stream);
 int launch_merge(const MergeParams& p, cudaStream_t stream);
 int launch_rotate(const RotateParams& p, cudaStream_t stream);
+int64_t p2p_buffer_bytes(int world, int64_t cap_rows);
+int launch_sp_exchange(const SpExchangeParams& p, cudaStream_t stream);
+int launch_sp_merge(const SpMergeParams& p, cudaStream_t stream);
+int read_p2p_timeouts(unsigned int* count, bool reset);
 int launch_store(const StoreParams& p, cudaStream_t stream);
 
 }  // namespace tqb

@@ -12,13 +12,13 @@
 
 #include "tqb_common.cuh"
 #include "tqb_internal.h"
+#include "tqb_merge_row.cuh"
 
 namespace tqb {
 
 namespace {
 
 constexpr int kWarpsPerCta = 8;
-constexpr int kSplitsPerPass = 8;  // splits whose loads a warp keeps in flight at once
 
 // Output element conversion (round to nearest even, as torch's .to(dtype)).
 template <typename T>
@@ -30,75 +30,17 @@ __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2hal
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
-// One CTA of 4 warps per (b, h).  Warp w merges the non-empty splits
-// s = w, w + 4, w + 8, ... of (b, h): lane l owns dims l, l+32, l+64, l+96,
-// so each split row is read as four coalesced 128-byte runs, and the warp
-// issues the loads of up to kSplitsPerPass splits before using any of them.
-// The four warps' (max, sum, acc) then combine through shared memory.  Same
-// log-sum-exp algebra as the reference's running merge.
+// One CTA of 4 warps per (b, h): merge_row (tqb_merge_row.cuh) merges the
+// row's non-empty splits; thread d writes output dim d, thread 0 the LSE.
 template <typename OutT>
 __global__ void __launch_bounds__(kHeadDim, 8) stage2_kernel(const Stage2Params P) {
-    constexpr int kParts = kHeadDim / 32;  // warps per CTA
-    __shared__ float s_acc[kParts][kHeadDim];
-    __shared__ float s_max[kParts], s_sum[kParts];
     const int64_t item = blockIdx.x;  // b * Hq + h
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nsp = P.nsplits ? min(__ldg(P.nsplits + b), P.S) : P.S;
-    const int L = __ldg(P.seq_lens + b);
-    const int split_len = nsp > 0 ? (L + nsp - 1) / nsp : 0;
-    // split s is non-empty iff split_len * s < L (its end is min(.., L))
-    const int nvalid = split_len > 0 ? min(nsp, (L + split_len - 1) / split_len) : 0;
-    const float* row0 = P.mid + (int64_t)b * P.msb + (int64_t)h * P.msh;
-
-    float m = -INFINITY, sum = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int s0 = warp; s0 < nvalid; s0 += kParts * kSplitsPerPass) {
-        float ls[kSplitsPerPass], os[kSplitsPerPass][4];
-#pragma unroll
-        for (int k = 0; k < kSplitsPerPass; k++) {
-            const int s = s0 + kParts * k;
-            const float* row = row0 + (int64_t)s * P.mss;
-            ls[k] = s < nvalid ? __ldg(row + kHeadDim) : -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; j++) os[k][j] = s < nvalid ? __ldg(row + lane + 32 * j) : 0.0f;
-        }
-        float mn = m;
-#pragma unroll
-        for (int k = 0; k < kSplitsPerPass; k++) mn = fmaxf(mn, ls[k]);
-        const float scale = m == -INFINITY ? 0.0f : expf(m - mn);
-        sum *= scale;
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[j] *= scale;
-#pragma unroll
-        for (int k = 0; k < kSplitsPerPass; k++) {
-            const float w = ls[k] == -INFINITY ? 0.0f : expf(ls[k] - mn);
-            sum += w;
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[j] += w * os[k][j];
-        }
-        m = mn;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; j++) s_acc[warp][lane + 32 * j] = acc[j];
-    if (lane == 0) {
-        s_max[warp] = m;
-        s_sum[warp] = sum;
-    }
-    __syncthreads();
-    const int d = threadIdx.x;
-    float gmax = -INFINITY;
-#pragma unroll
-    for (int p = 0; p < kParts; p++) gmax = fmaxf(gmax, s_max[p]);
-    float o = 0.0f, wsum = 0.0f;
-#pragma unroll
-    for (int p = 0; p < kParts; p++) {
-        const float w = s_max[p] == -INFINITY ? 0.0f : expf(s_max[p] - gmax);
-        o += w * s_acc[p][d];
-        wsum += w * s_sum[p];
-    }
+    float o, lse;
+    merge_row(P, b, h, &o, &lse);
     OutT* out = static_cast<OutT*>(P.out) + (int64_t)b * P.osb + (int64_t)h * P.osh;
-    out[d] = from_f32<OutT>(__fdiv_rn(o, wsum));
-    if (d == 0) P.lse[(int64_t)b * P.lsb + h] = gmax + logf(wsum);
+    out[threadIdx.x] = from_f32<OutT>(o);
+    if (threadIdx.x == 0) P.lse[(int64_t)b * P.lsb + h] = lse;
 }
 
 // Cross-GPU merge of G (O, LSE) partials laid out [G, B, Hq, D+1]; parts

@@ -20,8 +20,8 @@ INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libtqb.so"
 
 SOURCES = ["tqb_api.cu", "tqb_stage1.cu", "tqb_stage1_ring.cu", "tqb_stage2.cu", "tqb_store.cu", "tqb_noalloc.cu",
-           "tqb_rotate.cu"]
-HEADERS = ["tqb_common.cuh", "tqb_internal.h"]
+           "tqb_rotate.cu", "tqb_p2p.cu"]
+HEADERS = ["tqb_common.cuh", "tqb_internal.h", "tqb_merge_row.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -25,6 +25,9 @@ TQB_ERR_CUDA = -5
 TQB_LAYOUT_SOA = 0
 TQB_LAYOUT_AOS = 1
 
+TQB_P2P_MAX_RANKS = 8
+TQB_IPC_HANDLE_BYTES = 64
+
 TQB_DTYPE_F32 = 0
 TQB_DTYPE_F16 = 1
 TQB_DTYPE_BF16 = 2
@@ -42,6 +45,14 @@ EXPORTED_SYMBOLS = (
     "tqb_decode_static",
     "tqb_stage2_typed",
     "tqb_rotate_query",
+    "tqb_p2p_buffer_bytes",
+    "tqb_p2p_alloc",
+    "tqb_p2p_free",
+    "tqb_ipc_export",
+    "tqb_ipc_import",
+    "tqb_ipc_close",
+    "tqb_sp_exchange",
+    "tqb_sp_merge",
 )
 
 
@@ -115,6 +126,21 @@ class RotateArgs(ctypes.Structure):
     ]
 
 
+class SpExchangeArgs(ctypes.Structure):
+    _fields_ = [
+        ("stage2", Stage2Args), ("rank", _i32), ("world", _i32), ("cap_rows", _i64),
+        ("buffers", _vp * TQB_P2P_MAX_RANKS), ("epoch", ctypes.c_uint64),
+    ]
+
+
+class SpMergeArgs(ctypes.Structure):
+    _fields_ = [
+        ("buffer", _vp), ("world", _i32), ("batch", _i32), ("num_q_heads", _i32), ("head_dim", _i32),
+        ("cap_rows", _i64), ("epoch", ctypes.c_uint64), ("output", _vp), ("out_stride_b", _i64),
+        ("out_stride_h", _i64), ("lse", _vp), ("lse_stride_b", _i64),
+    ]
+
+
 class MergeArgs(ctypes.Structure):
     _fields_ = [
         ("partials", _vp), ("num_parts", _i32), ("batch", _i32), ("num_q_heads", _i32),
@@ -169,6 +195,18 @@ def load() -> ctypes.CDLL:
             lib.tqb_stage2_typed.restype = ctypes.c_int
             lib.tqb_rotate_query.argtypes = [ctypes.POINTER(RotateArgs), _vp]
             lib.tqb_rotate_query.restype = ctypes.c_int
+            lib.tqb_p2p_buffer_bytes.argtypes = [_i32, _i64]
+            lib.tqb_p2p_buffer_bytes.restype = _i64
+            lib.tqb_p2p_alloc.argtypes = [_i64, ctypes.POINTER(_vp)]
+            lib.tqb_p2p_free.argtypes = [_vp]
+            lib.tqb_ipc_export.argtypes = [_vp, _vp]
+            lib.tqb_ipc_import.argtypes = [_vp, ctypes.POINTER(_vp)]
+            lib.tqb_ipc_close.argtypes = [_vp]
+            lib.tqb_sp_exchange.argtypes = [ctypes.POINTER(SpExchangeArgs), _vp]
+            lib.tqb_sp_merge.argtypes = [ctypes.POINTER(SpMergeArgs), _vp]
+            for f in (lib.tqb_p2p_alloc, lib.tqb_p2p_free, lib.tqb_ipc_export, lib.tqb_ipc_import,
+                      lib.tqb_ipc_close, lib.tqb_sp_exchange, lib.tqb_sp_merge):
+                f.restype = ctypes.c_int
             _lib = lib
     return _lib
 

@@ -24,6 +24,8 @@ follow the single-GPU split merge (reference baseline/stage2.py:37-52).
 
 from __future__ import annotations
 
+import ctypes
+
 import heapq
 import math
 from typing import Optional, Sequence
@@ -189,6 +191,175 @@ def sp_decode(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Te
         lse = torch.empty(B, Hq, device=q_rot.device)
     ops.merge_partials(parts, output, lse)
     return output, lse
+
+
+def sp_decode_p2p(exchange: "P2PExchange", q_rot: torch.Tensor, kv_cache: torch.Tensor,
+                  block_table: torch.Tensor, seq_lens: torch.Tensor, centroids: torch.Tensor, *,
+                  local_splits: int = 16, layout: str = "soa", attn_scale: Optional[float] = None,
+                  mid_o: Optional[torch.Tensor] = None, output: Optional[torch.Tensor] = None,
+                  lse: Optional[torch.Tensor] = None):
+    """``sp_decode`` with the exchange over peer memory: local Stage1, then
+    ``exchange.step`` (Stage2 rows straight into every rank's buffer, merge of
+    all ranks' rows).  Every rank returns the full (O [B, Hq, D], LSE [B, Hq])."""
+    from . import ops
+
+    B, Hq, D = q_rot.shape
+    if mid_o is None:
+        mid_o = torch.empty(B, Hq, local_splits, D + 1, device=q_rot.device)
+    if output is None:
+        output = torch.empty(B, Hq, D, device=q_rot.device)
+    if lse is None:
+        lse = torch.empty(B, Hq, device=q_rot.device)
+    ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout=layout, attn_scale=attn_scale)
+    return exchange.step(mid_o, seq_lens, output, lse)
+
+
+class P2PExchange:
+    """Per-rank state of the sequence-parallel exchange over peer memory
+    (``tqb_sp_exchange`` / ``tqb_sp_merge``): this rank's exchange buffer,
+    every rank's buffer mapped into this process (CUDA IPC handles swapped
+    over the process group once), and the step epoch.  ``step`` replaces
+    Stage2 + all-gather + merge: each rank's merged rows go straight into
+    every rank's buffer over NVLink and every rank merges the G rows.
+
+    ``emulated(world, ...)`` builds the ``world`` ranks of one process on one
+    GPU (the buffers are local; ranks are stepped one after another), for
+    testing the data path without IPC."""
+
+    def __init__(self, batch: int, num_q_heads: int, device: torch.device, group=None, *,
+                 _local: Optional[dict] = None):
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.device = torch.device(device)
+        self.cap_rows = batch * num_q_heads
+        self.epoch = 0
+        self._imported = []
+        self._owned = None
+        if _local is not None:  # emulated rank: buffers shared inside one process
+            self.world, self.rank, self.buffers = _local["world"], _local["rank"], _local["buffers"]
+            return
+        self.world, self.rank = _world(group)
+        self.group = group
+        nbytes = self._lib.tqb_p2p_buffer_bytes(self.world, self.cap_rows)
+        _lib.check(_lib.TQB_OK if nbytes > 0 else _lib.TQB_ERR_INVALID_ARG)
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.tqb_p2p_alloc(nbytes, ctypes.byref(own)))
+        self._owned = own.value
+        buffers = [None] * self.world
+        buffers[self.rank] = own.value
+        if self.world > 1:
+            import torch.distributed as dist
+
+            h = (ctypes.c_char * _lib.TQB_IPC_HANDLE_BYTES)()
+            _lib.check(self._lib.tqb_ipc_export(ctypes.c_void_p(own.value), h))
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            with torch.cuda.device(self.device):
+                for r in range(self.world):
+                    if r == self.rank:
+                        continue
+                    ptr = ctypes.c_void_p()
+                    hr = (ctypes.c_char * _lib.TQB_IPC_HANDLE_BYTES).from_buffer_copy(handles[r])
+                    _lib.check(self._lib.tqb_ipc_import(hr, ctypes.byref(ptr)))
+                    self._imported.append(ptr.value)
+                    buffers[r] = ptr.value
+        self.buffers = buffers
+
+    @classmethod
+    def emulated(cls, world: int, batch: int, num_q_heads: int, device: torch.device) -> list["P2PExchange"]:
+        from . import _lib
+
+        lib = _lib.load()
+        nbytes = lib.tqb_p2p_buffer_bytes(world, batch * num_q_heads)
+        bufs = []
+        with torch.cuda.device(device):
+            for _ in range(world):
+                p = ctypes.c_void_p()
+                _lib.check(lib.tqb_p2p_alloc(nbytes, ctypes.byref(p)))
+                bufs.append(p.value)
+        ranks = [cls(batch, num_q_heads, device, _local={"world": world, "rank": r, "buffers": bufs})
+                 for r in range(world)]
+        ranks[0]._owned_list = bufs  # freed by ranks[0].close()
+        return ranks
+
+    def step(self, mid_o: torch.Tensor, seq_lens: torch.Tensor, output: torch.Tensor,
+             lse: Optional[torch.Tensor] = None, *, num_splits_per_seq: Optional[torch.Tensor] = None,
+             stream: Optional[int] = None):
+        """This rank's Stage2 rows to every rank (``send``), then the merge of
+        all ranks' rows into ``output [B, Hq, D]`` and ``lse [B, Hq]`` (``recv``)."""
+        self.send(mid_o, seq_lens, num_splits_per_seq=num_splits_per_seq, stream=stream)
+        return self.recv(output, lse, stream=stream)
+
+    def _stream(self, stream):
+        return stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+
+    def send(self, mid_o: torch.Tensor, seq_lens: torch.Tensor, *,
+             num_splits_per_seq: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> None:
+        """Stage2 of this rank's splits, each row stored into every rank's
+        buffer, and the new epoch published (``tqb_sp_exchange``)."""
+        from . import _lib
+
+        B, Hq, S, D1 = mid_o.shape
+        if B * Hq > self.cap_rows:
+            raise _lib.TqbError(_lib.TQB_ERR_INVALID_ARG, "batch * num_q_heads exceeds the exchange capacity")
+        self.epoch += 1
+        self._shape = (B, Hq, D1 - 1)
+        a = _lib.SpExchangeArgs()
+        s2 = a.stage2
+        s2.mid_o = mid_o.data_ptr()
+        s2.mid_stride_b, s2.mid_stride_h, s2.mid_stride_s = mid_o.stride(0), mid_o.stride(1), mid_o.stride(2)
+        s2.seq_lens = seq_lens.data_ptr()
+        if num_splits_per_seq is not None:
+            s2.num_splits_per_seq = num_splits_per_seq.data_ptr()
+        s2.batch, s2.num_q_heads, s2.head_dim, s2.num_splits = B, Hq, D1 - 1, S
+        a.rank, a.world, a.cap_rows, a.epoch = self.rank, self.world, self.cap_rows, self.epoch
+        for r, p in enumerate(self.buffers):
+            a.buffers[r] = p
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.tqb_sp_exchange(ctypes.byref(a), ctypes.c_void_p(self._stream(stream))))
+
+    def recv(self, output: torch.Tensor, lse: Optional[torch.Tensor] = None, *, stream: Optional[int] = None):
+        """Wait for every rank's rows of the current epoch and merge them
+        (``tqb_sp_merge``)."""
+        from . import _lib
+
+        B, Hq, D = self._shape
+        m = _lib.SpMergeArgs()
+        m.buffer, m.world, m.batch, m.num_q_heads, m.head_dim = self.buffers[self.rank], self.world, B, Hq, D
+        m.cap_rows, m.epoch = self.cap_rows, self.epoch
+        m.output, m.out_stride_b, m.out_stride_h = output.data_ptr(), output.stride(0), output.stride(1)
+        if lse is not None:
+            m.lse, m.lse_stride_b = lse.data_ptr(), lse.stride(0)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.tqb_sp_merge(ctypes.byref(m), ctypes.c_void_p(self._stream(stream))))
+        return output, lse
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers and free this rank's (collective:
+        every rank calls it)."""
+        from . import _lib
+
+        torch.cuda.synchronize(self.device)
+        if self._owned is not None and self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._imported:
+                self._lib.tqb_ipc_close(ctypes.c_void_p(p))
+            self._imported = []
+            if self._owned is not None and self.world > 1:
+                import torch.distributed as dist
+
+                dist.barrier(group=self.group)
+            if self._owned is not None:
+                self._lib.tqb_p2p_free(ctypes.c_void_p(self._owned))
+                self._owned = None
+            for p in getattr(self, "_owned_list", []):
+                self._lib.tqb_p2p_free(ctypes.c_void_p(p))
+            self._owned_list = []
 
 
 def tp_shard_cache(kv_cache: torch.Tensor, world: int, rank: int, layout: str = "soa") -> torch.Tensor:
