@@ -116,6 +116,33 @@ int main(void) {
 """
 
 
+def test_p2p_entry_points_reject_on_the_host(lib):
+    """The SP exchange validates rank, world, epoch and capacity before any
+    device call, and sizes its buffer as rows + flags + counter."""
+    row = 129 * 4
+    assert lib.tqb_p2p_buffer_bytes(2, 128) == 2 * 2 * 128 * row + 2 * 2 * 8 + 8
+    assert lib.tqb_p2p_buffer_bytes(0, 128) == -1
+    assert lib.tqb_p2p_buffer_bytes(_lib.TQB_P2P_MAX_RANKS + 1, 128) == -1
+    a = _lib.SpExchangeArgs()
+    a.stage2.batch, a.stage2.num_q_heads, a.stage2.head_dim, a.stage2.num_splits = 2, 32, 128, 4
+    a.rank, a.world, a.cap_rows, a.epoch = 0, 2, 64, 1
+    a.rank = 2  # not below world
+    assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    a.rank, a.epoch = 0, 0  # epochs start at 1
+    assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    a.epoch, a.cap_rows = 1, 63  # batch * heads = 64 rows do not fit
+    assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    assert b"cap_rows" in lib.tqb_last_error_detail()
+    a.cap_rows = 64  # rows fit, but no mid_o / buffers given
+    assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    m = _lib.SpMergeArgs()
+    m.world, m.batch, m.num_q_heads, m.head_dim, m.cap_rows, m.epoch = 2, 2, 32, 128, 64, 1
+    assert lib.tqb_sp_merge(ctypes.byref(m), None) == _lib.TQB_ERR_INVALID_ARG  # no buffer / output
+    m.world = 0
+    assert lib.tqb_sp_merge(ctypes.byref(m), None) == _lib.TQB_ERR_INVALID_ARG
+    assert lib.tqb_p2p_free(None) == _lib.TQB_OK and lib.tqb_ipc_close(None) == _lib.TQB_OK
+
+
 def test_ctypes_structs_match_c_layout(tmp_path: Path):
     structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
                "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs,
