@@ -3,7 +3,9 @@
 //
 // Online log-sum-exp merge over the non-empty splits of mid_o
 // (baseline/stage2.py:8-55): out = sum_s w_s O_s / sum_s w_s with
-// w_s = exp(lse_s - max), lse = max + ln(sum_s w_s).  Called by all 128
+// w_s = exp(lse_s - max), lse = max + ln(sum_s w_s); the exponentials and the
+// logarithm run on the hardware base-2 units (as Triton's tl.exp / tl.log in
+// the reference's Stage2 do).  Called by all 128
 // threads of a CTA (4 warps; warp w merges splits w, w + 4, ... with the loads
 // of kSplitsPerPass splits in flight, lane l owning dims l, l+32, l+64, l+96;
 // the four partial states combine through shared memory).  Thread d returns
@@ -43,13 +45,13 @@ __device__ __forceinline__ void merge_row(const Stage2Params& P, int b, int h, f
         float mn = m;
 #pragma unroll
         for (int k = 0; k < kSplitsPerPass; k++) mn = fmaxf(mn, ls[k]);
-        const float scale = m == -INFINITY ? 0.0f : expf(m - mn);
+        const float scale = m == -INFINITY ? 0.0f : ex2_approx((m - mn) * kLog2e);
         sum *= scale;
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[j] *= scale;
 #pragma unroll
         for (int k = 0; k < kSplitsPerPass; k++) {
-            const float w = ls[k] == -INFINITY ? 0.0f : expf(ls[k] - mn);
+            const float w = ls[k] == -INFINITY ? 0.0f : ex2_approx((ls[k] - mn) * kLog2e);
             sum += w;
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[j] += w * os[k][j];
@@ -70,12 +72,12 @@ __device__ __forceinline__ void merge_row(const Stage2Params& P, int b, int h, f
     float acc_d = 0.0f, wsum = 0.0f;
 #pragma unroll
     for (int p = 0; p < kParts; p++) {
-        const float w = s_max[p] == -INFINITY ? 0.0f : expf(s_max[p] - gmax);
+        const float w = s_max[p] == -INFINITY ? 0.0f : ex2_approx((s_max[p] - gmax) * kLog2e);
         acc_d += w * s_acc[p][d];
         wsum += w * s_sum[p];
     }
     *o = __fdiv_rn(acc_d, wsum);
-    *lse_out = gmax + logf(wsum);
+    *lse_out = gmax + lg2_approx(wsum) * kLn2;
 }
 
 }  // namespace tqb
