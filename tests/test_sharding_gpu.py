@@ -122,6 +122,38 @@ def test_sp_p2p_exchange_emulated(cuda_device, world):
         ranks[0].close()
 
 
+def test_sp_p2p_merge_gives_up_on_a_missing_rank(cuda_device):
+    """A rank whose peer never sends: the merge's bounded wait (about a
+    second) gives up, the rows come out NaN, the device counter read by
+    tqb_wait_timeouts counts it, and the context stays usable."""
+    dev = cuda_device
+    B, Hq = 2, 32
+    ranks = sharding.P2PExchange.emulated(2, B, Hq, dev)
+    try:
+        lens = [40, 9]
+        c = random_case(321, len(lens), Hq, 8, lens)
+        mid = torch.empty(B, Hq, 4, 129, device=dev)
+        sl = _dev(c, "seq_lens", dev)
+        tqb.stage1(_dev(c, "q_rot", dev), _dev(c, "kv_cache", dev), _dev(c, "block_table", dev), sl,
+                   _dev(c, "centroids", dev), mid)
+        tqb.wait_timeouts(reset=True)
+        ranks[0].send(mid, sl)  # rank 1 never sends this epoch
+        out = torch.zeros(B, Hq, 128, device=dev)
+        lse = torch.zeros(B, Hq, device=dev)
+        ranks[0].recv(out, lse)
+        torch.cuda.synchronize()
+        assert tqb.wait_timeouts(reset=True) >= 1
+        assert torch.isnan(out).all() and torch.isnan(lse).all()
+        # the device is still fine: a full step of both ranks completes
+        ranks[1].epoch = ranks[0].epoch - 1  # resynchronise the ranks' step counters
+        ranks[1].send(mid, sl)
+        ranks[0].recv(out, lse)
+        torch.cuda.synchronize()
+        assert tqb.wait_timeouts(reset=True) == 0 and torch.isfinite(out).all()
+    finally:
+        ranks[0].close()
+
+
 @pytest.mark.multigpu
 def test_sp_nccl_two_gpus(tmp_path):
     if torch.cuda.device_count() < 2:
