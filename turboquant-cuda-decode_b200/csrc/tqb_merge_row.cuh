@@ -17,7 +17,7 @@
 
 namespace tqb {
 
-constexpr int kSplitsPerPass = 8;  // splits whose loads a warp keeps in flight at once
+constexpr int kSplitsPerPass = 4;  // splits whose loads a warp keeps in flight at once
 
 __device__ __forceinline__ void merge_row(const Stage2Params& P, int b, int h, float* o, float* lse_out) {
     constexpr int kParts = kHeadDim / 32;  // warps per CTA
