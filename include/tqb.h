@@ -137,6 +137,25 @@ int tqb_stage2(const tqb_stage2_args* args, cudaStream_t stream);
 int tqb_stage2_typed(const tqb_stage2_args* args, int out_dtype, void* output, cudaStream_t stream);
 
 /*
+ * Attention sinks: folds the per-head sink logit sinks[h] (natural-log units,
+ * like the scaled scores) into split 0 of mid_o for every sequence with
+ * seq_len > 0, as one extra token of value 0.  Stage1 followed by this call
+ * equals the reference Stage1 with USE_SINKS (reference/soa_decode_v1.py:
+ * 134-145, 565-605: split 0 starts its online softmax at m = sinks[h],
+ * l = 1); a sink of -inf leaves the row unchanged.  Stream-ordered after
+ * Stage1, before Stage2 (or the cross-GPU merge).
+ */
+typedef struct tqb_sink_args {
+    float* mid_o;                      /* [B, Hq, S, D + 1]; split 0 rewritten in place */
+    int64_t mid_stride_b, mid_stride_h; /* elements */
+    const int32_t* seq_lens;           /* [B] */
+    const float* sinks;                /* [Hq] fp32 */
+    int32_t batch, num_q_heads, head_dim;
+} tqb_sink_args;
+
+int tqb_fold_sinks(const tqb_sink_args* args, cudaStream_t stream);
+
+/*
  * Query rotation: q_rot[b, h, :] = float(query[b, h, :]) @ rotation, with
  * rotation = Pi^T, a [D, D] row-major fp32 matrix, accumulated in fp32 (the
  * launcher's cast + GEMM + copy, reference/soa_decode_v1.py:535-538, in one

@@ -205,8 +205,12 @@ def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
 
 
 def stage1_np(q_rot, cache, block_table, seq_lens, centroids, num_splits, *,
-              layout=LAYOUT_SOA, num_splits_per_seq=None, attn_scale=None):
-    """float64 restatement of Stage1 (two-pass softmax per split)."""
+              layout=LAYOUT_SOA, num_splits_per_seq=None, attn_scale=None, sinks=None):
+    """float64 restatement of Stage1 (two-pass softmax per split).
+
+    ``sinks`` ([Hq] logits): split 0 starts its softmax at m = sinks[h],
+    l = 1 with a zero accumulator (reference/soa_decode_v1.py:134-145), i.e.
+    one extra token of logit sinks[h] and value 0 in split 0."""
     q = np.asarray(q_rot, np.float64)
     B, Hq, D = q.shape
     Hk = cache.shape[2]
@@ -228,8 +232,14 @@ def stage1_np(q_rot, cache, block_table, seq_lens, centroids, num_splits, *,
                 qs = q[b, kvh * G : (kvh + 1) * G]  # [G, D]
                 sc = qs @ K.T * scale  # [G, n]
                 m = sc.max(-1, keepdims=True)
+                sk = None
+                if sinks is not None and s == 0:
+                    sk = np.asarray(sinks, np.float64)[kvh * G : (kvh + 1) * G, None]
+                    m = np.maximum(m, sk)
                 p = np.exp(sc - m)
                 l = p.sum(-1, keepdims=True)
+                if sk is not None:
+                    l = l + np.exp(sk - m)
                 mid[b, kvh * G : (kvh + 1) * G, s, :D] = (p @ V) / l
                 mid[b, kvh * G : (kvh + 1) * G, s, D] = (m + np.log(l))[:, 0]
     return mid

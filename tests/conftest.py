@@ -47,6 +47,12 @@ def golden_store():
     return load_golden("store_small")
 
 
+@pytest.fixture(scope="session")
+def golden_sinks():
+    """SoA Stage1 of the reference with and without attention sinks."""
+    return load_golden("sinks_gqa4")
+
+
 def assert_close(got, ref, atol=ATOL, rtol=RTOL, what=""):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)

@@ -133,12 +133,12 @@ def soa_meta_offset(hk: int) -> int:
     return BLOCK_SIZE * hk * (MSE_BYTES + VAL_BYTES)
 
 
-def run_soa_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits):
+def run_soa_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits, sinks=None):
     B, Hq, D = q_rot.shape
     Hk = kv.shape[2]
     mid = torch.full((B, Hq, num_splits, D + 1), float("nan"), dtype=torch.float32)
     ref.soa_dec._tq_decode_stage1[(B, Hq, num_splits)](
-        q_rot, kv, kv.view(torch.uint16), bt, seq_lens, cents, mid, None,
+        q_rot, kv, kv.view(torch.uint16), bt, seq_lens, cents, mid, sinks,
         q_rot.stride(0), q_rot.stride(1), kv.stride(0), bt.stride(0),
         mid.stride(0), mid.stride(1), mid.stride(2),
         NUM_KV_HEADS=Hk, HEAD_DIM=D, BLOCK_SIZE=BLOCK_SIZE,
@@ -148,7 +148,8 @@ def run_soa_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits):
         META_REGION_OFFSET=soa_meta_offset(Hk), NUM_SOA_FIELDS=3,
         SOA_K_NORM=0, SOA_V_SCALE=1, SOA_V_ZERO=2,
         ATTN_SCALE=1.0 / math.sqrt(D), BLOCK_D=triton.next_power_of_2(D),
-        BLOCK_KV=4, KEY_FP8=0, NORM_CORRECTION=1, FP8_E4B15=0, USE_SINKS=0,
+        BLOCK_KV=4, KEY_FP8=0, NORM_CORRECTION=1, FP8_E4B15=0,
+        USE_SINKS=0 if sinks is None else 1,
         num_warps=1, num_stages=1,
     )
     return mid
@@ -225,9 +226,11 @@ def orthogonal(seed: int, d: int = HEAD_DIM) -> torch.Tensor:
 
 
 def build_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits,
-               pool_blocks, aos=True, v2=True):
+               pool_blocks, aos=True, v2=True, sinks=False):
     """Store seeded K/V with the reference SoA (and AoS) store, then run the
-    reference Stage1 kernels and Stage2 on the result."""
+    reference Stage1 kernels and Stage2 on the result.  ``sinks=True`` adds a
+    run of the SoA Stage1 with per-head sink logits (``USE_SINKS=1``,
+    ``reference/soa_decode_v1.py:134-145``) and its Stage2."""
     t0 = time.time()
     B = len(seq_lens)
     g = torch.Generator().manual_seed(seed)
@@ -279,6 +282,15 @@ def build_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits,
     print(f"[{name}] SoA V1 done {time.time() - t0:.1f}s", flush=True)
     o2, l2 = run_stage2(ref, mid_v1, sl)
     out["out_stage2"], out["lse_stage2"] = o2, l2
+    if sinks:
+        # one head without a sink (-inf), one whose sink dominates its scores
+        sk = torch.randn(hq, generator=g, dtype=torch.float32) * 2.0
+        sk[0] = float("-inf")
+        sk[1] = 12.0
+        mid_s = run_soa_v1(ref, q_rot, kv_soa, bt, sl, cents, num_splits, sinks=sk)
+        out["sinks"], out["mid_o_soa_v1_sinks"] = sk, mid_s
+        out["out_stage2_sinks"], out["lse_stage2_sinks"] = run_stage2(ref, mid_s, sl)
+        print(f"[{name}] SoA V1 with sinks done {time.time() - t0:.1f}s", flush=True)
     if aos:
         out["kv_cache_aos"] = kv_aos
         out["mid_o_aos_v1"] = run_aos_v1(ref, q_rot, kv_aos, bt, sl, cents, num_splits)
@@ -352,6 +364,9 @@ CASES = {
     # GQA-8 with two KV heads and uneven splits.
     "ragged_gqa8_hk2": dict(seed=13, seq_lens=[160, 33], hq=16, hk=2, num_splits=3,
                             pool_blocks=16, aos=False),
+    # Attention sinks (per-head logits folded into split 0), ragged lengths.
+    "sinks_gqa4": dict(seed=17, seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4,
+                       pool_blocks=16, aos=False, v2=False, sinks=True),
 }
 
 

@@ -86,6 +86,14 @@ def test_argument_validation_without_launch(lib):
     t.batch, t.num_q_heads, t.head_dim, t.num_splits = 1, 32, 128, 4
     assert lib.tqb_stage2_typed(ctypes.byref(t), 5, None, None) == _lib.TQB_ERR_INVALID_ARG
     assert b"out_dtype" in lib.tqb_last_error_detail()
+    k = _lib.SinkArgs()
+    k.batch, k.num_q_heads, k.head_dim = 1, 32, 64
+    assert lib.tqb_fold_sinks(ctypes.byref(k), None) == _lib.TQB_ERR_UNSUPPORTED
+    k.head_dim = 128
+    assert lib.tqb_fold_sinks(ctypes.byref(k), None) == _lib.TQB_ERR_INVALID_ARG  # NULL pointers
+    assert lib.tqb_fold_sinks(None, None) == _lib.TQB_ERR_INVALID_ARG
+    k.batch = 0
+    assert lib.tqb_fold_sinks(ctypes.byref(k), None) == _lib.TQB_OK  # empty batch: no-op
     s = _lib.StoreArgs()
     s.num_tokens, s.num_kv_heads, s.head_dim, s.block_size, s.n_centroids = 1, 8, 128, 16, 8
     assert lib.tqb_store(ctypes.byref(s), None) == _lib.TQB_ERR_UNSUPPORTED
@@ -108,6 +116,7 @@ int main(void) {
   printf("tqb_store_args %zu\n", sizeof(tqb_store_args));
   printf("tqb_decode_static_args %zu\n", sizeof(tqb_decode_static_args));
   printf("tqb_rotate_args %zu\n", sizeof(tqb_rotate_args));
+  printf("tqb_sink_args %zu\n", sizeof(tqb_sink_args));
   printf("tqb_sp_exchange_args %zu\n", sizeof(tqb_sp_exchange_args));
   printf("tqb_sp_merge_args %zu\n", sizeof(tqb_sp_merge_args));
   %FIELDS%
@@ -147,7 +156,7 @@ def test_ctypes_structs_match_c_layout(tmp_path: Path):
     structs = {"tqb_stage1_args": _lib.Stage1Args, "tqb_stage2_args": _lib.Stage2Args,
                "tqb_merge_args": _lib.MergeArgs, "tqb_store_args": _lib.StoreArgs,
                "tqb_decode_static_args": _lib.DecodeStaticArgs, "tqb_rotate_args": _lib.RotateArgs,
-               "tqb_sp_exchange_args": _lib.SpExchangeArgs, "tqb_sp_merge_args": _lib.SpMergeArgs}
+               "tqb_sink_args": _lib.SinkArgs, "tqb_sp_exchange_args": _lib.SpExchangeArgs, "tqb_sp_merge_args": _lib.SpMergeArgs}
     fields = "\n".join(f"F({c}, {f})" for c, py in structs.items() for f, _ in py._fields_)
     src = tmp_path / "probe.c"
     src.write_text(C_LAYOUT_PROBE.replace("%FIELDS%", fields))

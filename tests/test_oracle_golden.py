@@ -68,6 +68,27 @@ def test_stage2_matches_reference(golden, name):
     assert_close(o2, z["out_stage2"], atol=1e-6, rtol=0, what="stage2_np out")
 
 
+def test_numpy_sinks_match_reference(golden_sinks):
+    """Attention sinks: the float64 restatement with sinks against the
+    reference Stage1 run with USE_SINKS=1 (a -inf sink, a dominating sink,
+    ragged lengths with empty splits), and Stage2 on it."""
+    z = golden_sinks
+    S = int(z["num_splits"])
+    got = O.stage1_np(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                      sinks=z["sinks"])
+    ref = z["mid_o_soa_v1_sinks"]
+    w = _written(ref)
+    assert np.array_equal(~np.isnan(got[..., 0]), w)
+    assert np.abs(got - ref)[w].max() <= ORACLE_ATOL
+    # only split 0 moves; the -inf sink leaves its head's rows unchanged
+    plain = z["mid_o_soa_v1"]
+    assert np.array_equal(np.nan_to_num(plain[:, :, 1:]), np.nan_to_num(ref[:, :, 1:]))
+    assert np.array_equal(plain[:, 0, 0], ref[:, 0, 0])
+    o2, l2 = O.stage2_np(ref, z["seq_lens"])
+    assert_close(o2, z["out_stage2_sinks"], atol=1e-6, rtol=0, what="stage2_np out (sinks)")
+    assert_close(l2, z["lse_stage2_sinks"], atol=1e-6, rtol=0, what="stage2_np lse (sinks)")
+
+
 def test_store_bit_exact(golden_store):
     z = golden_store
     for layout, key, nc in ((O.LAYOUT_SOA, "kv_cache_soa", True), (O.LAYOUT_AOS, "kv_cache_aos", False)):

@@ -50,13 +50,14 @@ def _to(dev, z, key, dtype=None):
     return t.to(dev) if dtype is None else t.to(dev, dtype)
 
 
-def _run(dev, z, cache_key="kv_cache", layout="soa", nsp=None, S=None):
+def _run(dev, z, cache_key="kv_cache", layout="soa", nsp=None, S=None, sinks=None):
     S = int(z["num_splits"]) if S is None else S
     q = _to(dev, z, "q_rot")
     mid = torch.full((q.shape[0], q.shape[1], S, q.shape[2] + 1), SENTINEL, device=dev)
     tqb.stage1(q, _to(dev, z, cache_key), _to(dev, z, "block_table"), _to(dev, z, "seq_lens"),
                _to(dev, z, "centroids"), mid, layout=layout,
-               num_splits_per_seq=None if nsp is None else torch.tensor(nsp, dtype=torch.int32, device=dev))
+               num_splits_per_seq=None if nsp is None else torch.tensor(nsp, dtype=torch.int32, device=dev),
+               sinks=None if sinks is None else _to(dev, z, sinks))
     torch.cuda.synchronize()
     return mid.cpu().numpy()
 
@@ -72,6 +73,26 @@ def _check(got, ref, what):
 def test_soa_vs_reference_golden(cuda_device, golden, name):
     z = golden[name]
     _check(_run(cuda_device, z), z["mid_o_soa_v1"], f"{name} SoA")
+
+
+def test_soa_sinks_vs_reference_golden(cuda_device, golden_sinks):
+    """Attention sinks against the reference Stage1 run with USE_SINKS=1
+    (reference/soa_decode_v1.py:134-145): a -inf sink, a sink that dominates
+    its head's scores, ragged lengths with empty splits; then Stage2."""
+    z = golden_sinks
+    got = _run(cuda_device, z, sinks="sinks")
+    _check(got, z["mid_o_soa_v1_sinks"], "SoA with sinks")
+    # without sinks the same case matches the plain reference run
+    _check(_run(cuda_device, z), z["mid_o_soa_v1"], "SoA without sinks")
+    dev = cuda_device
+    mid = torch.from_numpy(np.where(np.isnan(z["mid_o_soa_v1_sinks"]), 0.0, got).astype(np.float32)).to(dev)
+    B, Hq = mid.shape[:2]
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, _to(dev, z, "seq_lens"), out, lse)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), z["out_stage2_sinks"], what="Stage2 with sinks out")
+    assert_close(lse.cpu().numpy(), z["lse_stage2_sinks"], what="Stage2 with sinks lse")
 
 
 @pytest.mark.parametrize("name", [n for n in GOLDEN_CASES if n != "ragged_gqa8_hk2"])
@@ -245,3 +266,35 @@ def test_decode_launcher_vs_oracle(cuda_device, layout, qdtype):
                      rtol=RTOL + ulp, what=f"{layout} decode out")
     assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"{layout} decode lse")
     assert np.all(np.isnan(got[~live])), "a sequence without tokens gets NaN, as in the reference"
+
+
+@pytest.mark.parametrize("layout", ["soa", "aos"])
+def test_decode_launcher_sinks_vs_oracle(cuda_device, layout):
+    """``triton_turboquant_decode_attention(..., sinks=...)`` with bf16 sink
+    logits (cast to float32 as the reference does) against the float64
+    oracle with the sinks in split 0, then Stage2; an empty sequence stays
+    NaN (no split is written, so no sink either)."""
+    from tqb import compat
+    dev = cuda_device
+    lens = [300, 17, 0, 555]
+    z = random_case(43 + (layout == "aos"), len(lens), 32, 8, lens, layout=layout)
+    rng = np.random.default_rng(5)
+    Pi = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    query = torch.from_numpy(rng.standard_normal((len(lens), 32, 128)).astype(np.float32))
+    sinks = torch.from_numpy((rng.standard_normal(32) * 3.0).astype(np.float32)).to(torch.bfloat16)
+    sinks[5] = float("-inf")
+    q_rot = (query @ torch.from_numpy(Pi).T).numpy()
+    S = 6
+    mid = O.stage1_np(q_rot, z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], S,
+                      layout=O.LAYOUT_SOA if layout == "soa" else O.LAYOUT_AOS, sinks=sinks.float().numpy())
+    ref_out, ref_lse = O.stage2_np(mid, z["seq_lens"])
+    lse = torch.empty(len(lens), 32, device=dev)
+    out = compat.decode_attention(query.to(dev), _to(dev, z, "kv_cache"), _to(dev, z, "block_table"),
+                                  _to(dev, z, "seq_lens"), torch.from_numpy(Pi).to(dev), _to(dev, z, "centroids"),
+                                  1.0 / math.sqrt(128), layout, max_num_kv_splits=S, lse_buf=lse,
+                                  sinks=sinks.to(dev))
+    torch.cuda.synchronize()
+    live = np.asarray(lens) > 0
+    assert_close(out.cpu().numpy()[live], ref_out[live], what=f"{layout} decode with sinks out")
+    assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"{layout} decode with sinks lse")
+    assert np.all(np.isnan(out.cpu().numpy()[~live]))

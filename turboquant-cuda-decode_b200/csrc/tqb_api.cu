@@ -226,6 +226,30 @@ int tqb_stage2_typed(const tqb_stage2_args* a, int out_dtype, void* output, cuda
     return stage2_impl(a, output, out_dtype, stream);
 }
 
+int tqb_fold_sinks(const tqb_sink_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0, TQB_ERR_INVALID_ARG, "batch/heads must be positive");
+    TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
+    TQB_REQUIRE((int64_t)a->batch * a->num_q_heads < (int64_t(1) << 31), TQB_ERR_UNSUPPORTED,
+                "batch * num_q_heads must be < 2^31");
+    if (a->batch == 0) return TQB_OK;
+    TQB_REQUIRE(a->mid_o && a->seq_lens && a->sinks, TQB_ERR_INVALID_ARG, "a required pointer is NULL");
+    TQB_REQUIRE(aligned(a->mid_o, 4) && aligned(a->seq_lens, 4) && aligned(a->sinks, 4), TQB_ERR_ALIGNMENT,
+                "buffers must be aligned to their element size");
+    DeviceGuard guard(a->mid_o);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
+    tqb::SinkParams p{};
+    p.mid = a->mid_o;
+    p.msb = a->mid_stride_b;
+    p.msh = a->mid_stride_h;
+    p.seq_lens = a->seq_lens;
+    p.sinks = a->sinks;
+    p.B = a->batch;
+    p.Hq = a->num_q_heads;
+    return tqb::launch_fold_sinks(p, stream);
+}
+
 // ---- sequence-parallel exchange over peer memory --------------------------
 
 int64_t tqb_p2p_buffer_bytes(int32_t world, int64_t cap_rows) {

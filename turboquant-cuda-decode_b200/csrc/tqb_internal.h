@@ -60,6 +60,15 @@ struct Stage2Params {
     int B, Hq, S;
 };
 
+// Attention sinks folded into split 0 of mid_o (tqb_stage2.cu).
+struct SinkParams {
+    float* mid;
+    int64_t msb, msh;
+    const int32_t* seq_lens;
+    const float* sinks;  // [Hq]
+    int B, Hq;
+};
+
 // Sequence-parallel exchange over peer memory (tqb_p2p.cu).
 constexpr int kP2PMaxRanks = 8;
 struct SpExchangeParams {
@@ -128,6 +137,7 @@ int launch_stage1_ring(const Stage1Params& p, cudaStream_t stream, int num_sms);
 int read_wait_timeouts(unsigned int* count, bool reset);
 int launch_stage2(const Stage2Params& p, cudaStream_t stream);
 int launch_merge(const MergeParams& p, cudaStream_t stream);
+int launch_fold_sinks(const SinkParams& p, cudaStream_t stream);
 int launch_rotate(const RotateParams& p, cudaStream_t stream);
 int64_t p2p_buffer_bytes(int world, int64_t cap_rows);
 int launch_sp_exchange(const SpExchangeParams& p, cudaStream_t stream);

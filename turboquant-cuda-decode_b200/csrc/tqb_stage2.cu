@@ -70,6 +70,34 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) merge_kernel(const MergePar
     if (lane == 0 && P.lse) P.lse[item] = rmax + logf(rsum);
 }
 
+// Attention sinks (reference/soa_decode_v1.py:134-145): split 0 of a
+// non-empty sequence starts its online softmax at m = s, l = 1, i.e. counts
+// one more token of logit s = sinks[h] and value 0.  From split 0's (O, LSE)
+// that is LSE' = ln(e^LSE + e^s), O' = O e^(LSE - LSE').  One warp per
+// (b, h); split 0 is unwritten, and left alone, when seq_len <= 0.  A sink of
+// -inf leaves the row bit-identical (factor 1, LSE + ln 1).
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sink_fold_kernel(const SinkParams P) {
+    const int lane = threadIdx.x & 31;
+    const int64_t item = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    if (item >= (int64_t)P.B * P.Hq) return;
+    const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
+    if (P.seq_lens[b] <= 0) return;
+    float* row = P.mid + (int64_t)b * P.msb + (int64_t)h * P.msh;  // split 0
+    const float lse0 = row[kHeadDim];
+    const float s = __ldg(P.sinks + h);
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) v[j] = row[lane + 32 * j];
+    __syncwarp();  // every lane has read the LSE before lane 0 rewrites it
+    const float mx = fmaxf(lse0, s);
+    const float e0 = expf(lse0 - mx), es = expf(s - mx);
+    const float sum = e0 + es;
+    const float f = __fdiv_rn(e0, sum);
+#pragma unroll
+    for (int j = 0; j < 4; j++) row[lane + 32 * j] = v[j] * f;
+    if (lane == 0) row[kHeadDim] = mx + logf(sum);
+}
+
 }  // namespace
 
 int launch_stage2(const Stage2Params& P, cudaStream_t stream) {
@@ -89,6 +117,14 @@ int launch_merge(const MergeParams& P, cudaStream_t stream) {
     if (items == 0) return TQB_OK;
     const int64_t grid = (items + kWarpsPerCta - 1) / kWarpsPerCta;
     merge_kernel<<<(unsigned)grid, kWarpsPerCta * 32, 0, stream>>>(P);
+    return report_launch(cudaGetLastError());
+}
+
+int launch_fold_sinks(const SinkParams& P, cudaStream_t stream) {
+    const int64_t items = (int64_t)P.B * P.Hq;
+    if (items == 0) return TQB_OK;
+    const int64_t grid = (items + kWarpsPerCta - 1) / kWarpsPerCta;
+    sink_fold_kernel<<<(unsigned)grid, kWarpsPerCta * 32, 0, stream>>>(P);
     return report_launch(cudaGetLastError());
 }
 

@@ -23,5 +23,5 @@ from .compat import (  # noqa: F401
     triton_turboquant_decode_attention,
     triton_turboquant_store,
 )
-from .ops import merge_partials, rotate_query, stage1, stage2, store  # noqa: F401
+from .ops import fold_sinks, merge_partials, rotate_query, stage1, stage2, store  # noqa: F401
 from . import compat_aos  # noqa: F401

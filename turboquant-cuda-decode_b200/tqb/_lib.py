@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "tqb_wait_timeouts",
     "tqb_decode_static",
     "tqb_stage2_typed",
+    "tqb_fold_sinks",
     "tqb_rotate_query",
     "tqb_p2p_buffer_bytes",
     "tqb_p2p_alloc",
@@ -104,6 +105,14 @@ class Stage2Args(ctypes.Structure):
         ("output", _vp), ("out_stride_b", _i64), ("out_stride_h", _i64),
         ("lse", _vp), ("lse_stride_b", _i64),
         ("batch", _i32), ("num_q_heads", _i32), ("head_dim", _i32), ("num_splits", _i32),
+    ]
+
+
+class SinkArgs(ctypes.Structure):
+    _fields_ = [
+        ("mid_o", _vp), ("mid_stride_b", _i64), ("mid_stride_h", _i64),
+        ("seq_lens", _vp), ("sinks", _vp),
+        ("batch", _i32), ("num_q_heads", _i32), ("head_dim", _i32),
     ]
 
 
@@ -193,6 +202,8 @@ def load() -> ctypes.CDLL:
             lib.tqb_decode_static.restype = ctypes.c_int
             lib.tqb_stage2_typed.argtypes = [ctypes.POINTER(Stage2Args), ctypes.c_int, _vp, _vp]
             lib.tqb_stage2_typed.restype = ctypes.c_int
+            lib.tqb_fold_sinks.argtypes = [ctypes.POINTER(SinkArgs), _vp]
+            lib.tqb_fold_sinks.restype = ctypes.c_int
             lib.tqb_rotate_query.argtypes = [ctypes.POINTER(RotateArgs), _vp]
             lib.tqb_rotate_query.restype = ctypes.c_int
             lib.tqb_p2p_buffer_bytes.argtypes = [_i32, _i64]

@@ -127,22 +127,23 @@ def triton_turboquant_decode_attention(
 ) -> torch.Tensor:
     """Production decode (q rotation, Stage1, Stage2) for the
     ``turboquant_4bit_nc`` preset; returns ``[B, Hq, D]`` in query's dtype.
-    FP8 keys, 3-bit codes and attention sinks are other presets/features of
-    the reference and raise ``NotImplementedError`` here."""
+    ``sinks`` ([Hq] per-head sink logits, cast to float32) enters split 0 of
+    every sequence as the reference's ``USE_SINKS`` does
+    (reference/soa_decode_v1.py:134-145, 565-605).  FP8 keys and 3-bit codes
+    are other presets of the reference and raise ``NotImplementedError``."""
     if key_fp8 or mse_bits != 4 or value_quant_bits != 4:
         raise NotImplementedError("only the turboquant_4bit_nc preset (4-bit K and V) is supported")
-    if sinks is not None:
-        raise NotImplementedError("attention sinks are not supported yet")
     return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, "soa", PiT=PiT,
                             mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
-                            max_num_kv_splits=max_num_kv_splits)
+                            max_num_kv_splits=max_num_kv_splits, sinks=sinks)
 
 
 def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, *, PiT=None,
                      mid_o_buf=None, output_buf=None, lse_buf=None, buf_holder=None,
-                     max_num_kv_splits: int = 32) -> torch.Tensor:
-    """Query rotation, Stage1 on the ``layout`` ("soa"/"aos") cache, Stage2;
-    the body of both reference launchers (reference/soa_decode_v1.py:486-643,
+                     max_num_kv_splits: int = 32, sinks=None) -> torch.Tensor:
+    """Query rotation, Stage1 on the ``layout`` ("soa"/"aos") cache (with the
+    optional attention ``sinks`` folded into split 0), Stage2; the body of
+    both reference launchers (reference/soa_decode_v1.py:486-643,
     reference/aos_decode.py:486-...) with the buffer reuse they offer."""
     B, Hq, D = query.shape
     if PiT is None:
@@ -160,8 +161,10 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
         mid_o = torch.empty(B, Hq, S, D + 1, dtype=torch.float32, device=query.device)
         if buf_holder is not None:
             buf_holder._tq_mid_o_buf = mid_o
+    if sinks is not None:
+        sinks = sinks.to(device=query.device, dtype=torch.float32).contiguous()
     ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout=layout,
-               attn_scale=scale)
+               attn_scale=scale, sinks=sinks)
     if query.dtype in (torch.float16, torch.bfloat16):
         # Stage2 writes the query's dtype directly (the reference merges into
         # fp32 and then casts: reference/soa_decode_v1.py:643; same rounding)

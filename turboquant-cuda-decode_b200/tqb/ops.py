@@ -16,7 +16,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import MergeArgs, RotateArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
+from ._lib import MergeArgs, RotateArgs, SinkArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
 from .layout import BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, layout_id
 
 
@@ -43,13 +43,16 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
            seq_lens: torch.Tensor, centroids: torch.Tensor, mid_o: torch.Tensor, *,
            layout="soa", num_splits_per_seq: Optional[torch.Tensor] = None,
            pair_lut: Optional[torch.Tensor] = None, attn_scale: Optional[float] = None,
-           stream: Optional[int] = None) -> torch.Tensor:
+           sinks: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> torch.Tensor:
     """Decode Stage1 into ``mid_o [B, Hq, S, D+1]`` (S = ``mid_o.shape[2]``).
 
     ``kv_cache`` is the ``[num_blocks, 16, Hk, 134]`` uint8 cache (a view
     with a non-unit block stride is accepted; SoA needs the inner three dims
     contiguous).  ``num_splits_per_seq`` (int32 ``[B]``, each <= S) switches
-    from the uniform split count S to per-sequence counts.
+    from the uniform split count S to per-sequence counts.  ``sinks``
+    (float32 ``[Hq]`` logits) adds the reference's attention sinks
+    (``USE_SINKS``, reference/soa_decode_v1.py:134-145) to split 0, through
+    :func:`fold_sinks` on the same stream.
     """
     lay = layout_id(layout)
     _cuda(q_rot, "q_rot", torch.float32)
@@ -80,6 +83,10 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
         _require(num_splits_per_seq.shape == (B,) and num_splits_per_seq.is_contiguous(),
                  "num_splits_per_seq must be a contiguous [B] tensor")
         nsp = num_splits_per_seq
+    if sinks is not None:
+        _cuda(sinks, "sinks", torch.float32)
+        _require(sinks.shape == (Hq,) and sinks.is_contiguous() and sinks.device == mid_o.device,
+                 "sinks must be a contiguous [Hq] float32 tensor on mid_o's device")
     a = Stage1Args()
     a.q_rot = q_rot.data_ptr()
     a.q_stride_b, a.q_stride_h = q_rot.stride(0), q_rot.stride(1)
@@ -102,7 +109,36 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     a.block_size, a.num_splits = bs, mid_o.shape[2]
     a.attn_scale = float(attn_scale) if attn_scale is not None else 1.0 / math.sqrt(D)
     with torch.cuda.device(mid_o.device):
-        _lib.check(_lib.load().tqb_stage1(a, stream if stream is not None else _stream(mid_o.device)))
+        st = stream if stream is not None else _stream(mid_o.device)
+        _lib.check(_lib.load().tqb_stage1(a, st))
+    if sinks is not None:
+        fold_sinks(mid_o, seq_lens, sinks, stream=stream)
+    return mid_o
+
+
+def fold_sinks(mid_o: torch.Tensor, seq_lens: torch.Tensor, sinks: torch.Tensor, *,
+               stream: Optional[int] = None) -> torch.Tensor:
+    """Fold per-head sink logits ``sinks [Hq]`` (float32) into split 0 of
+    ``mid_o [B, Hq, S, D+1]`` in place, for every sequence with seq_len > 0:
+    one extra token of logit ``sinks[h]`` and value 0, as the reference
+    Stage1 with ``USE_SINKS`` (reference/soa_decode_v1.py:134-145)."""
+    _cuda(mid_o, "mid_o", torch.float32)
+    _cuda(seq_lens, "seq_lens", torch.int32)
+    _cuda(sinks, "sinks", torch.float32)
+    _require(mid_o.dim() == 4 and mid_o.stride(3) == 1, "mid_o must be [B, Hq, S, D+1] with unit inner stride")
+    B, Hq, _, D1 = mid_o.shape
+    _require(seq_lens.shape == (B,) and seq_lens.is_contiguous(), "seq_lens must be a contiguous [B] tensor")
+    _require(sinks.shape == (Hq,) and sinks.is_contiguous(), "sinks must be a contiguous [Hq] tensor")
+    devs = {t.device for t in (mid_o, seq_lens, sinks)}
+    _require(len(devs) == 1, f"all tensors must be on one device, got {devs}")
+    a = SinkArgs()
+    a.mid_o = mid_o.data_ptr()
+    a.mid_stride_b, a.mid_stride_h = mid_o.stride(0), mid_o.stride(1)
+    a.seq_lens = seq_lens.data_ptr()
+    a.sinks = sinks.data_ptr()
+    a.batch, a.num_q_heads, a.head_dim = B, Hq, D1 - 1
+    with torch.cuda.device(mid_o.device):
+        _lib.check(_lib.load().tqb_fold_sinks(a, stream if stream is not None else _stream(mid_o.device)))
     return mid_o
 
 
