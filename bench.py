@@ -642,7 +642,7 @@ def main():
         dq, dbt, dsl = views(dbuf)
         hout = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
         mbuf = torch.empty(B, Hq, S, 129, device=dev)
-        obuf = torch.empty(B, Hq, 128, device=dev)
+        obuf = torch.empty(B, Hq, 128, dtype=w["query"].dtype, device=dev)  # vLLM's workspace: query dtype
         lbuf = torch.empty(B, Hq, device=dev)
 
         def e2e_step():

@@ -202,6 +202,39 @@ def test_strided_views(cuda_device):
     assert torch.all(midbig[:, :, 4:] == SENTINEL) and torch.all(midbig[..., 129:] == SENTINEL)
 
 
+@pytest.mark.parametrize("name", ["c0", "ragged_gqa4"])
+@pytest.mark.parametrize("layout", ["soa", "aos"])
+def test_vllm_transposed_cache_view(cuda_device, golden, name, layout):
+    """The cache as vLLM hands it over: ``(blocks, H, N, C)`` storage seen
+    through ``kv_cache.transpose(1, 2)`` (reference/turboquant_attn.py:565),
+    through the reference-named launcher.  An SoA block is raw bytes from its
+    base (the reference reads only ``kv_cache.stride(0)``), so the reference
+    bytes under the transposed view give the reference output; AoS reads
+    slot (t, h) through the view's strides (head-major here), so the
+    head-major copy of the reference AoS cache gives the reference AoS
+    output."""
+    z = golden[name]
+    dev = cuda_device
+    if layout == "soa":
+        kv = z["kv_cache"]
+        nb, bs, hk, slot = kv.shape
+        storage = torch.from_numpy(kv.reshape(nb, hk, bs, slot).copy()).to(dev)
+        ref = z["mid_o_soa_v1"]
+    else:
+        kv = z["kv_cache_aos"]
+        storage = torch.from_numpy(kv.transpose(0, 2, 1, 3).copy()).to(dev)
+        ref = z["mid_o_aos_v1"]
+    view = storage.transpose(1, 2)
+    assert not view.is_contiguous() and tuple(view.shape) == kv.shape
+    S = int(z["num_splits"])
+    q = _to(dev, z, "q_rot")
+    mid = torch.full((q.shape[0], q.shape[1], S, q.shape[2] + 1), SENTINEL, device=dev)
+    tqb.stage1(q, view, _to(dev, z, "block_table"), _to(dev, z, "seq_lens"), _to(dev, z, "centroids"), mid,
+               layout=layout)
+    torch.cuda.synchronize()
+    _check(mid.cpu().numpy(), ref, f"{name} {layout} vLLM view")
+
+
 def test_large_magnitudes(cuda_device):
     """Query magnitudes far from 1 (power-of-two scaling keeps the fp16
     operand split exact) and large V scales."""
@@ -298,3 +331,62 @@ def test_decode_launcher_sinks_vs_oracle(cuda_device, layout):
     assert_close(out.cpu().numpy()[live], ref_out[live], what=f"{layout} decode with sinks out")
     assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"{layout} decode with sinks lse")
     assert np.all(np.isnan(out.cpu().numpy()[~live]))
+
+
+def test_decode_launcher_cuda_graph_workspace(cuda_device):
+    """vLLM's decode use of ``triton_turboquant_decode_attention``
+    (reference/turboquant_attn.py:1125-1141, 368-373): workspace buffers for
+    mid_o, the output (in the query's dtype) and the LSE, a fixed split
+    count, the call captured once in a CUDA graph and replayed with new
+    queries and sequence lengths written into the captured input tensors.
+    The result lands in the caller's output buffer, and every replay matches
+    the oracle for that replay's inputs."""
+    from tqb import compat
+    dev = cuda_device
+    lens = [300, 17, 1024, 555]
+    B, Hq, S = len(lens), 32, 8
+    z = random_case(47, B, Hq, 8, lens)
+    rng = np.random.default_rng(9)
+    Pi = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    PiT = torch.from_numpy(Pi).T.contiguous()
+    kv, bt, cents = _to(dev, z, "kv_cache"), _to(dev, z, "block_table"), _to(dev, z, "centroids")
+    Pi_d, PiT_d = torch.from_numpy(Pi).to(dev), PiT.to(dev)
+    q_in = torch.zeros(B, Hq, 128, dtype=torch.bfloat16, device=dev)
+    sl_in = _to(dev, z, "seq_lens")
+    mid_ws = torch.empty(B, Hq, S, 129, device=dev)
+    out_ws = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=dev)
+    lse_ws = torch.empty(B, Hq, device=dev)
+
+    def call():
+        return compat.triton_turboquant_decode_attention(
+            q_in, kv, bt, sl_in, Pi_d, cents, 1.0 / math.sqrt(128), 4, 66, 4,
+            norm_correction=True, PiT=PiT_d, mid_o_buf=mid_ws, output_buf=out_ws, lse_buf=lse_ws,
+            max_num_kv_splits=S)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        call()  # eager warm-up (one-time kernel attribute set-up)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = call()
+    assert out.data_ptr() == out_ws.data_ptr(), "the result must land in the workspace buffer"
+    # each replay's lengths stay within the tokens stored for that sequence
+    # (slots past them hold random bytes, NaN norms included)
+    for trial, new_lens in enumerate(([300, 17, 1024, 555], [129, 1, 700, 0], [16, 9, 1023, 300])):
+        query = torch.from_numpy(rng.standard_normal((B, Hq, 128)).astype(np.float32)).to(torch.bfloat16)
+        q_in.copy_(query.to(dev))
+        sl_in.copy_(torch.tensor(new_lens, dtype=torch.int32))
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        q_rot = (query.float() @ PiT).numpy()
+        mid = O.stage1(q_rot, z["kv_cache"], z["block_table"], np.asarray(new_lens, np.int32), z["centroids"], S)
+        ref_out, ref_lse = O.stage2(mid, np.asarray(new_lens, np.int32))
+        live = np.asarray(new_lens) > 0
+        got = out_ws.float().cpu().numpy()
+        ref = torch.from_numpy(ref_out[live].astype(np.float32)).to(torch.bfloat16).float().numpy()
+        assert_close(got[live], ref, rtol=RTOL + 2.0 ** -7, what=f"graph replay {trial} out")
+        assert_close(lse_ws.cpu().numpy()[live], ref_lse[live], what=f"graph replay {trial} lse")
+    del graph

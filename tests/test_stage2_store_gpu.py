@@ -81,6 +81,35 @@ def test_store_bit_exact_vs_reference(cuda_device, golden_store, layout, key):
     assert np.array_equal(got, z[key]), f"{(got != z[key]).sum()} bytes differ"
 
 
+@pytest.mark.parametrize("layout,key", [("soa", "kv_cache_soa"), ("aos", "kv_cache_aos")])
+def test_store_through_vllm_view(cuda_device, golden_store, layout, key):
+    """The store into vLLM's cache view, ``kv_cache.transpose(1, 2)`` of
+    ``(blocks, H, N, C)`` storage (reference/turboquant_attn.py:565).  SoA
+    writes a block's raw bytes from its base, so the storage holds exactly
+    the reference bytes; AoS writes slot (t, h) through the view's strides,
+    so the view reads back as the reference cache."""
+    z = golden_store
+    dev = cuda_device
+    before = z["cache_before"]
+    nb, bs, hk, slot = before.shape
+    if layout == "soa":
+        storage = torch.from_numpy(before.reshape(nb, hk, bs, slot).copy()).to(dev)  # same bytes
+    else:
+        storage = torch.from_numpy(before.transpose(0, 2, 1, 3).copy()).to(dev)  # head-major slots
+    view = storage.transpose(1, 2)
+    assert not view.is_contiguous()
+    tqb.store(torch.from_numpy(z["y"]).to(dev), torch.from_numpy(z["norms"]).to(dev),
+              torch.from_numpy(z["value"].reshape(-1, 128).copy()).to(dev), view,
+              torch.from_numpy(z["slot_mapping"]).to(dev), torch.from_numpy(z["midpoints"]).to(dev),
+              torch.from_numpy(z["centroids"]).to(dev), layout=layout, norm_correction=(layout == "soa"))
+    torch.cuda.synchronize()
+    if layout == "soa":
+        got = storage.cpu().numpy().reshape(nb, bs, hk, slot)
+    else:
+        got = view.cpu().numpy()
+    assert np.array_equal(got, z[key]), f"{(got != z[key]).sum()} bytes differ"
+
+
 def test_store_bit_exact_vs_oracle_large(cuda_device):
     """Thousands of random token-heads, including near-midpoint values."""
     rng = np.random.default_rng(7)

@@ -73,6 +73,17 @@ int report_launch(cudaError_t e) {
 }
 }  // namespace tqb
 
+// AoS slot strides (bytes): token-major ([16][Hk][slot], the reference's own
+// cache) or head-major ([Hk][16][slot]: vLLM's (blocks, H, N, C) storage seen
+// through kv_cache.transpose(1, 2), reference/turboquant_attn.py:565), with
+// every slot of a block inside the block stride.
+static bool aos_strides_ok(int64_t block, int64_t ps, int64_t hs, int64_t hk) {
+    const bool token_major = hs >= tqb::kSlotBytes && ps >= hk * hs;
+    const bool head_major = ps >= tqb::kSlotBytes && hs >= tqb::kBlockSize * ps;
+    const int64_t extent = (tqb::kBlockSize - 1) * ps + (hk - 1) * hs + tqb::kSlotBytes;
+    return (token_major || head_major) && block >= extent && extent < (int64_t(1) << 31);
+}
+
 extern "C" {
 
 int tqb_version(void) { return TQB_VERSION; }
@@ -136,10 +147,8 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
         TQB_REQUIRE(aligned(a->kv_cache, 2) && a->cache_stride_block % 2 == 0 &&
                         a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0,
                     TQB_ERR_ALIGNMENT, "AoS cache pointer and strides must be even");
-        TQB_REQUIRE(a->cache_stride_head >= tqb::kSlotBytes &&
-                        a->cache_stride_pos >= hk * a->cache_stride_head &&
-                        a->cache_stride_block >= tqb::kBlockSize * a->cache_stride_pos,
-                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134]");
+        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk),
+                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134] slots, token- or head-major");
     }
     DeviceGuard guard(a->mid_o);
     TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
@@ -473,9 +482,10 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
         TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes,
                     TQB_ERR_INVALID_ARG, "SoA block stride must be >= 16*Hk*134 bytes");
     } else {
-        TQB_REQUIRE(a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0 &&
-                        a->cache_stride_head >= tqb::kSlotBytes,
-                    TQB_ERR_ALIGNMENT, "AoS strides must be even and describe >=134-byte slots");
+        TQB_REQUIRE(a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0, TQB_ERR_ALIGNMENT,
+                    "AoS strides must be even");
+        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk),
+                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134] slots, token- or head-major");
     }
     DeviceGuard guard(a->kv_cache);
     TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning kv_cache");

@@ -165,12 +165,15 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
         sinks = sinks.to(device=query.device, dtype=torch.float32).contiguous()
     ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout=layout,
                attn_scale=scale, sinks=sinks)
-    if query.dtype in (torch.float16, torch.bfloat16):
+    if output_buf is not None and output_buf.shape[0] >= B:
+        # the caller's workspace, in its own dtype (vLLM hands it out in the
+        # query's dtype, reference/turboquant_attn.py:1133-1141); Stage2
+        # writes float32, float16 or bfloat16 directly
+        output = output_buf[:B, :Hq, :D]
+    elif query.dtype in (torch.float16, torch.bfloat16):
         # Stage2 writes the query's dtype directly (the reference merges into
         # fp32 and then casts: reference/soa_decode_v1.py:643; same rounding)
         output = torch.empty(B, Hq, D, dtype=query.dtype, device=query.device)
-    elif output_buf is not None and output_buf.shape[0] >= B:
-        output = output_buf[:B, :Hq, :D]
     else:
         output = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
         if buf_holder is not None:

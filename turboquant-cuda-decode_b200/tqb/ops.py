@@ -39,6 +39,25 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _block_dense(kv_cache: torch.Tensor) -> bool:
+    """True when the inner dims ``[16, Hk, slot]`` cover one block's bytes
+    densely with the slot bytes innermost, in either order of the token and
+    head dims: the cache as allocated, or vLLM's ``(blocks, H, N, C)`` storage
+    seen through ``kv_cache.transpose(1, 2)`` (reference/turboquant_attn.py:
+    565).  An SoA block is raw bytes from its base (the reference kernels use
+    only ``kv_cache.stride(0)``, reference/soa_decode_v1.py:579), so either
+    view reads the same block."""
+    if kv_cache.stride(3) != 1:
+        return False
+    dims = sorted((kv_cache.stride(i), kv_cache.shape[i]) for i in (1, 2, 3) if kv_cache.shape[i] > 1)
+    expect = 1
+    for st, n in dims:
+        if st != expect:
+            return False
+        expect *= n
+    return True
+
+
 def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
            seq_lens: torch.Tensor, centroids: torch.Tensor, mid_o: torch.Tensor, *,
            layout="soa", num_splits_per_seq: Optional[torch.Tensor] = None,
@@ -73,8 +92,7 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
              f"mid_o shape {tuple(mid_o.shape)} does not match q_rot {tuple(q_rot.shape)}")
     _require(block_table.shape[0] == B and seq_lens.shape[0] == B, "batch mismatch")
     if lay == LAYOUT_SOA:
-        _require(kv_cache.stride(3) == 1 and kv_cache.stride(2) == slot and kv_cache.stride(1) == Hk * slot,
-                 "SoA cache needs each block's bytes contiguous")
+        _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
     devs = {t.device for t in (q_rot, kv_cache, block_table, seq_lens, centroids, mid_o)}
     _require(len(devs) == 1, f"all tensors must be on one device, got {devs}")
     nsp = None
@@ -250,8 +268,7 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
     _require(y.numel() == N * H * HEAD_DIM and value.numel() == N * H * HEAD_DIM and norms.numel() == N * H,
              "y/value must be [N*H, 128] and norms [N*H]")
     if lay == LAYOUT_SOA:
-        _require(kv_cache.stride(3) == 1 and kv_cache.stride(2) == slot and kv_cache.stride(1) == H * slot,
-                 "SoA cache needs each block's bytes contiguous")
+        _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
     if norm_correction:
         _require(centroids is not None, "norm_correction=True requires centroids")
     if centroids is not None:
