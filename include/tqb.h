@@ -63,8 +63,13 @@ typedef enum tqb_dtype {
 } tqb_dtype;
 
 typedef enum tqb_layout {
-    TQB_LAYOUT_SOA = 0, /* block = [16 tok][Hk][K64|V64] + [Hk][3][16] fp16 meta */
-    TQB_LAYOUT_AOS = 1  /* slot  = [K64 | knorm | V64 | vscale | vzero] */
+    TQB_LAYOUT_SOA = 0,    /* block = [16 tok][Hk][K64|V64] + [Hk][3][16] fp16 meta */
+    TQB_LAYOUT_AOS = 1,    /* slot  = [K64 | knorm | V64 | vscale | vzero] */
+    /* turboquant_k8v4 (FP8 keys, reference/config.py:21-25, SoA form of
+     * reference/soa_store.py:125-221): block = [16 tok][Hk][K128 e4m3 | V64]
+     * + [Hk][2][16] fp16 meta (vscale, vzero); 196 bytes per token-head.  The
+     * query is not rotated and the centroids are unused (may be NULL). */
+    TQB_LAYOUT_SOA_K8 = 2
 } tqb_layout;
 
 /*

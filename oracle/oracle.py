@@ -31,6 +31,7 @@ LIB_PATH = HERE / "libtqoracle.so"
 
 LAYOUT_SOA = 0
 LAYOUT_AOS = 1
+LAYOUT_SOA_K8 = 2  # turboquant_k8v4: [16][Hk][K128 e4m3 | V64] + [Hk][2][16] fp16 meta
 HEAD_DIM = 128
 BLOCK_SIZE = 16
 SLOT_BYTES = 134  # 64 K + 64 V + 3 fp16 metadata
@@ -170,6 +171,76 @@ def stage2(mid_o, seq_lens, num_splits_per_seq=None, nthreads=0):
 # ---------------------------------------------------------------------------
 
 
+def _e4m3_values() -> np.ndarray:
+    """Value of every e4m3 (OCP "fn" variant) byte: 1 sign, 4 exponent bits
+    (bias 7), 3 mantissa bits; exponent 0 is subnormal (m / 8 * 2^-6);
+    0x7F / 0xFF are NaN, no infinities."""
+    b = np.arange(256)
+    e, m = (b >> 3) & 0xF, b & 7
+    mag = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
+    v = np.where(b & 0x80, -mag, mag)
+    v[(b & 0x7F) == 0x7F] = np.nan
+    return v
+
+
+E4M3 = _e4m3_values()
+
+
+def e4m3_encode(x) -> np.ndarray:
+    """float -> e4m3 byte, round to nearest, ties to the even code, finite
+    values beyond 448 saturated to +-448 (the "rn.satfinite" conversion the
+    compiled reference store issues, reference/soa_store.py:192-193)."""
+    x = np.asarray(x, np.float64)
+    mags = E4M3[:0x7F]                  # codes 0..126, increasing
+    a = np.minimum(np.abs(x), 448.0)
+    hi = np.clip(np.searchsorted(mags, a, side="left"), 1, 126)
+    lo = hi - 1
+    dlo, dhi = a - mags[lo], mags[hi] - a
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo)
+    code = np.where(a == 0.0, 0, code)
+    sign = np.signbit(x).astype(np.int64)  # values rounding to zero keep their sign
+    out = (code | (sign << 7)).astype(np.uint8)
+    return np.where(np.isnan(x), np.uint8(0x7F), out).astype(np.uint8)
+
+
+def _quantise_value_np(v):
+    """4-bit value quantiser of the reference store in fp32
+    (reference/soa_store.py:85-116): returns codes and the fp16 scale/zero."""
+    v = np.asarray(v, np.float32)
+    vmin, vmax = v.min(-1, keepdims=True), v.max(-1, keepdims=True)
+    scale = (vmax - vmin) / np.float32(15.0)
+    scale = np.where(scale > np.float32(1e-8), scale, np.float32(1e-8)).astype(np.float32)
+    t = ((v - vmin) / scale + np.float32(0.5)).astype(np.float32)
+    q = np.clip(np.trunc(t), 0, 15).astype(np.uint8)
+    return q, scale[..., 0].astype(np.float16), vmin[..., 0].astype(np.float16)
+
+
+def store_k8_np(key, value, slot_mapping, cache):
+    """FP8-key store (turboquant_k8v4, reference/soa_store.py:125-221) into
+    ``cache [nb, 16, H, 196]`` in place: e4m3 key bytes, 4-bit values
+    (low nibble = even dim), fp16 vscale/vzero in the meta region."""
+    nb, bs, H, slot = cache.shape
+    flat = cache.reshape(nb, bs * H * slot)
+    D = HEAD_DIM
+    dps = D + D // 2
+    key = np.asarray(key, np.float32).reshape(-1, H, D)
+    value = np.asarray(value, np.float32).reshape(-1, H, D)
+    meta_off = bs * H * dps
+    for t, s in enumerate(np.asarray(slot_mapping)):
+        if s < 0:
+            continue
+        blk, off = int(s) // bs, int(s) % bs
+        q, sc, zr = _quantise_value_np(value[t])
+        for h in range(H):
+            base = off * H * dps + h * dps
+            flat[blk, base : base + D] = e4m3_encode(key[t, h])
+            flat[blk, base + D : base + dps] = q[h, 0::2] | (q[h, 1::2] << 4)
+            m = meta_off + h * 2 * bs * 2
+            flat[blk, m + 2 * off : m + 2 * off + 2] = np.frombuffer(sc[h].tobytes(), np.uint8)
+            flat[blk, m + 2 * bs + 2 * off : m + 2 * bs + 2 * off + 2] = np.frombuffer(zr[h].tobytes(), np.uint8)
+
+
 def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
     """Dequantise tokens (block_ids[i], offs[i]) of KV head ``kvh``.
     Returns ``K [n, D]`` (centroid*norm, norm correction applied for AoS) and
@@ -177,6 +248,16 @@ def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
     nb, bs, Hk, slot = cache.shape
     D = HEAD_DIM
     flat = cache.reshape(nb, bs * Hk * slot)
+    if layout == LAYOUT_SOA_K8:
+        dps = D + D // 2  # 128 e4m3 key bytes + 64 V bytes
+        base = offs * Hk * dps + kvh * dps
+        kb = flat[block_ids[:, None], base[:, None] + np.arange(D)]
+        vb = flat[block_ids[:, None], base[:, None] + D + np.arange(D // 2)]
+        meta = flat[:, bs * Hk * dps :].copy().view(np.float16).reshape(nb, Hk, 2, bs)
+        vsc = meta[block_ids, kvh, 0, offs].astype(np.float64)
+        vz = meta[block_ids, kvh, 1, offs].astype(np.float64)
+        vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
+        return E4M3[kb], vidx * vsc[:, None] + vz[:, None]
     c = np.asarray(centroids, np.float64)
     if layout == LAYOUT_SOA:
         dps = D  # 64 K + 64 V bytes

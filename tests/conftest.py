@@ -48,6 +48,12 @@ def golden_store():
 
 
 @pytest.fixture(scope="session")
+def golden_k8():
+    """turboquant_k8v4 (FP8 keys): the reference FP8 store and SoA Stage1."""
+    return load_golden("k8v4_ragged")
+
+
+@pytest.fixture(scope="session")
 def golden_sinks():
     """SoA Stage1 of the reference with and without attention sinks."""
     return load_golden("sinks_gqa4")

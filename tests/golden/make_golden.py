@@ -155,6 +155,72 @@ def run_soa_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits, sinks=None)
     return mid
 
 
+def run_soa_k8(ref: Ref, query, kv, bt, seq_lens, cents, num_splits):
+    """SoA V1 Stage1 with FP8 (e4m3) keys: the query goes in unrotated."""
+    B, Hq, D = query.shape
+    Hk = kv.shape[2]
+    mid = torch.full((B, Hq, num_splits, D + 1), float("nan"), dtype=torch.float32)
+    ref.soa_dec._tq_decode_stage1[(B, Hq, num_splits)](
+        query, kv, kv.view(torch.uint16), bt, seq_lens, cents, mid, None,
+        query.stride(0), query.stride(1), kv.stride(0), bt.stride(0),
+        mid.stride(0), mid.stride(1), mid.stride(2),
+        NUM_KV_HEADS=Hk, HEAD_DIM=D, BLOCK_SIZE=BLOCK_SIZE,
+        NUM_KV_SPLITS=num_splits, KV_GROUP_SIZE=Hq // Hk,
+        MSE_BITS=MSE_BITS, MSE_BYTES=MSE_BYTES, VQB=VALUE_BITS,
+        VAL_DATA_BYTES=VAL_BYTES, KEY_DATA_BYTES=HEAD_DIM,
+        META_REGION_OFFSET=BLOCK_SIZE * Hk * (HEAD_DIM + VAL_BYTES), NUM_SOA_FIELDS=2,
+        SOA_K_NORM=0, SOA_V_SCALE=0, SOA_V_ZERO=1,
+        ATTN_SCALE=1.0 / math.sqrt(D), BLOCK_D=triton.next_power_of_2(D),
+        BLOCK_KV=4, KEY_FP8=1, NORM_CORRECTION=0, FP8_E4B15=0, USE_SINKS=0,
+        num_warps=1, num_stages=1,
+    )
+    return mid
+
+
+def build_k8_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_blocks):
+    """turboquant_k8v4: fp16 keys cast to e4m3 by the reference FP8 store
+    (``reference/soa_store.py:125-221``), 4-bit values, then the reference
+    SoA Stage1 with ``KEY_FP8=1`` on the fp16 query (no rotation) and
+    Stage2."""
+    t0 = time.time()
+    B = len(seq_lens)
+    g = torch.Generator().manual_seed(seed)
+    pages = [max(1, math.ceil(L / BLOCK_SIZE)) for L in seq_lens]
+    perm = torch.randperm(pool_blocks, generator=g)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]].to(torch.int32)
+        k += pages[b]
+    slot = HEAD_DIM + VAL_BYTES + 4  # 196: fp8 key, 4-bit value, v-scale, v-zero
+    kv = torch.randint(0, 256, (pool_blocks, BLOCK_SIZE, hk, slot), generator=g, dtype=torch.uint8)
+    ntok = sum(seq_lens)
+    # keys spread over the e4m3 range (a few beyond 448 saturate), fp16 inputs
+    key = (torch.randn(ntok, hk, HEAD_DIM, generator=g) * 3.0).to(torch.float16)
+    key[0, 0, :8] = torch.tensor([500.0, -600.0, 448.0, 0.001, -0.0001, 17.0, 19.0, 0.0])
+    val = torch.randn(ntok, hk, HEAD_DIM, generator=g).to(torch.float16)
+    slots = []
+    for b in range(B):
+        for t in range(seq_lens[b]):
+            slots.append(int(bt[b, t // BLOCK_SIZE]) * BLOCK_SIZE + t % BLOCK_SIZE)
+    slot_mapping = torch.tensor(slots, dtype=torch.int32)
+    before = kv.clone()
+    cents = ref.centroids_mod.get_centroids(HEAD_DIM, MSE_BITS).to(torch.float32)
+    mids = ((cents[:-1] + cents[1:]) * 0.5).contiguous()
+    ref.soa_store.triton_turboquant_store(
+        key, val, kv, slot_mapping, torch.eye(HEAD_DIM), mids, MSE_BITS, HEAD_DIM, VALUE_BITS,
+        key_fp8=True)
+    query = (torch.randn(B, hq, HEAD_DIM, generator=g) * 0.5).to(torch.float16)
+    sl = torch.tensor(seq_lens, dtype=torch.int32)
+    print(f"[{name}] store done {time.time() - t0:.1f}s", flush=True)
+    mid = run_soa_k8(ref, query, kv, bt, sl, cents, num_splits)
+    print(f"[{name}] SoA K8 Stage1 done {time.time() - t0:.1f}s", flush=True)
+    o2, l2 = run_stage2(ref, mid, sl)
+    save(name, dict(key=key.float(), value=val.float(), slot_mapping=slot_mapping, cache_before=before,
+                    kv_cache=kv, block_table=bt, seq_lens=sl, query=query.float(),
+                    num_splits=np.int32(num_splits), mid_o=mid, out_stage2=o2, lse_stage2=l2))
+
+
 def run_aos_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits):
     B, Hq, D = q_rot.shape
     Hk = kv.shape[2]
@@ -373,10 +439,15 @@ CASES = {
 def main(argv):
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = Ref()
-    wanted = argv or list(CASES) + ["store"]
+    wanted = argv or list(CASES) + ["store", "k8v4_ragged"]
     for name in wanted:
         if name == "store":
             build_store_case(ref, "store_small", seed=99, ntok=48, hk=4, pool_blocks=5)
+        elif name == "k8v4_ragged":
+            # FP8-key preset: ragged lengths (an empty-split sequence, splits
+            # starting mid-page), GQA-4
+            build_k8_case(ref, name, seed=23, seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4,
+                          pool_blocks=16)
         else:
             build_case(ref, name, **CASES[name])
 

@@ -118,3 +118,58 @@ def test_v2_fixed_fails_the_parity_bar(golden):
     w = _written(ref)
     frac = (np.abs(v2 - ref) > 1e-4 + 2e-3 * np.abs(ref))[w].mean()
     assert frac > 0.001
+
+
+def test_e4m3_encode_matches_torch_cast():
+    """The FP8 key cast of the oracle (round to nearest even, saturate to
+    +-448) against torch's float8_e4m3fn conversion of the clamped value,
+    ties, subnormals, signed zeros and out-of-range values included."""
+    import torch
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100000) * 50, rng.standard_normal(50000) * 0.01,
+                        [0.0, -0.0, 448, 449, 464, 465, 500, -600, 1e-9, -2e-4, 2.0 ** -10, 3 * 2.0 ** -10,
+                         17.0, 19.0, -17.0]]).astype(np.float32)
+    ref = torch.from_numpy(np.clip(x, -448, 448)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(O.e4m3_encode(x), ref)
+
+
+def test_k8v4_store_oracle_against_reference(golden_k8):
+    """FP8-key store: value codes and the fp16 scale/zero are bit-identical
+    to the reference store's; the key bytes are the e4m3 cast with
+    round-to-nearest-even and saturation (the compiled reference's
+    conversion on sm_90+).  The fixture's own key bytes came from the Triton
+    interpreter, whose FP8 cast rounds ties up, flushes subnormals and wraps
+    on overflow, so they are not compared."""
+    import torch
+    z = golden_k8
+    cache = z["cache_before"].copy()
+    O.store_k8_np(z["key"], z["value"], z["slot_mapping"], cache)
+    nb, bs, hk, slot = cache.shape
+    keymask = np.zeros(bs * hk * slot, bool)
+    for o in range(bs):
+        for h in range(hk):
+            keymask[o * hk * 192 + h * 192 : o * hk * 192 + h * 192 + 128] = True
+    got, ref = cache.reshape(nb, -1), z["kv_cache"].reshape(nb, -1)
+    assert np.array_equal(got[:, ~keymask], ref[:, ~keymask])
+    sm = z["slot_mapping"]
+    for t in range(len(sm)):
+        blk, off = int(sm[t]) // bs, int(sm[t]) % bs
+        for h in range(hk):
+            k = torch.from_numpy(np.clip(z["key"][t, h], -448, 448)).to(torch.float8_e4m3fn)
+            b0 = off * hk * 192 + h * 192
+            assert np.array_equal(got[blk, b0 : b0 + 128], k.view(torch.uint8).numpy())
+
+
+def test_k8v4_stage1_numpy_matches_reference(golden_k8):
+    """FP8-key Stage1 restatement against the reference SoA Stage1 run with
+    KEY_FP8=1 on the unrotated fp16 query; keys up to 448 make scores large,
+    so the bound is relative as well (float64 oracle vs fp32 reference)."""
+    z = golden_k8
+    mid = O.stage1_np(z["query"], z["kv_cache"], z["block_table"], z["seq_lens"], None, int(z["num_splits"]),
+                      layout=O.LAYOUT_SOA_K8)
+    ref = z["mid_o"]
+    w = _written(ref)
+    assert np.array_equal(~np.isnan(mid[..., 0]), w)
+    assert (np.abs(mid - ref)[w] <= ORACLE_ATOL + 1e-6 * np.abs(ref)[w]).all()
+    o2, l2 = O.stage2_np(ref, z["seq_lens"])
+    assert_close(o2, z["out_stage2"], atol=1e-6, rtol=0, what="stage2_np out (k8v4)")

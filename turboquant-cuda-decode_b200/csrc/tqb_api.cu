@@ -119,16 +119,17 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                 TQB_ERR_INVALID_ARG, "batch/heads/num_splits must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
-    TQB_REQUIRE(a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED,
+    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8;
+    TQB_REQUIRE(k8 || a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED,
                 "n_centroids must be 16 (4-bit keys)");
     TQB_REQUIRE(a->num_q_heads % a->num_kv_heads == 0, TQB_ERR_INVALID_ARG,
                 "num_q_heads must be a multiple of num_kv_heads");
     const int G = a->num_q_heads / a->num_kv_heads;
     TQB_REQUIRE(G <= 8, TQB_ERR_UNSUPPORTED, "GQA group size must be <= 8");
-    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS, TQB_ERR_INVALID_ARG,
-                "layout must be TQB_LAYOUT_SOA or TQB_LAYOUT_AOS");
+    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8, TQB_ERR_INVALID_ARG,
+                "layout must be TQB_LAYOUT_SOA, TQB_LAYOUT_AOS or TQB_LAYOUT_SOA_K8");
     if (a->batch == 0) return TQB_OK;
-    TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens && a->centroids && a->mid_o,
+    TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens && (a->centroids || k8) && a->mid_o,
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
     TQB_REQUIRE(aligned(a->q_rot, 16) && a->q_stride_b % 4 == 0 && a->q_stride_h % 4 == 0,
                 TQB_ERR_ALIGNMENT, "q_rot must be 16-byte aligned with strides multiple of 4");
@@ -138,7 +139,12 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
     TQB_REQUIRE(a->max_blocks_per_seq > 0 && a->block_table_stride >= a->max_blocks_per_seq,
                 TQB_ERR_INVALID_ARG, "block_table row stride must be >= max_blocks_per_seq");
     const int64_t hk = a->num_kv_heads;
-    if (a->layout == TQB_LAYOUT_SOA) {
+    if (k8) {
+        TQB_REQUIRE(aligned(a->kv_cache, 16), TQB_ERR_ALIGNMENT, "SoA kv_cache must be 16-byte aligned");
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytesK8 &&
+                        a->cache_stride_block % 16 == 0,
+                    TQB_ERR_ALIGNMENT, "FP8-key block stride must be >= 16*Hk*196 bytes and a multiple of 16");
+    } else if (a->layout == TQB_LAYOUT_SOA) {
         TQB_REQUIRE(aligned(a->kv_cache, 16), TQB_ERR_ALIGNMENT, "SoA kv_cache must be 16-byte aligned");
         TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes &&
                         a->cache_stride_block % 16 == 0,
@@ -465,11 +471,14 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
                 "num_tokens must be >= 0 and num_kv_heads > 0");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
-    TQB_REQUIRE(a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED, "n_centroids must be 16");
-    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS, TQB_ERR_INVALID_ARG,
-                "layout must be TQB_LAYOUT_SOA or TQB_LAYOUT_AOS");
+    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8;
+    TQB_REQUIRE(k8 || a->n_centroids == tqb::kNumCentroids, TQB_ERR_UNSUPPORTED, "n_centroids must be 16");
+    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8, TQB_ERR_INVALID_ARG,
+                "layout must be TQB_LAYOUT_SOA, TQB_LAYOUT_AOS or TQB_LAYOUT_SOA_K8");
+    TQB_REQUIRE(!(k8 && a->norm_correction), TQB_ERR_INVALID_ARG,
+                "the FP8-key layout has no norm correction");
     if (a->num_tokens == 0) return TQB_OK;
-    TQB_REQUIRE(a->y && a->norms && a->value && a->midpoints && a->slot_mapping && a->kv_cache,
+    TQB_REQUIRE(a->y && a->value && a->slot_mapping && a->kv_cache && (k8 || (a->norms && a->midpoints)),
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
     TQB_REQUIRE(!a->norm_correction || a->centroids, TQB_ERR_INVALID_ARG,
                 "norm_correction requires centroids");
@@ -478,7 +487,12 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
     TQB_REQUIRE(aligned(a->kv_cache, 2) && a->cache_stride_block % 2 == 0, TQB_ERR_ALIGNMENT,
                 "kv_cache and its block stride must be even");
     const int64_t hk = a->num_kv_heads;
-    if (a->layout == TQB_LAYOUT_SOA) {
+    if (k8) {
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytesK8 &&
+                        a->cache_stride_block % 4 == 0,
+                    TQB_ERR_INVALID_ARG, "FP8-key block stride must be >= 16*Hk*196 bytes and a multiple of 4");
+        TQB_REQUIRE(aligned(a->kv_cache, 4), TQB_ERR_ALIGNMENT, "FP8-key kv_cache must be 4-byte aligned");
+    } else if (a->layout == TQB_LAYOUT_SOA) {
         TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes,
                     TQB_ERR_INVALID_ARG, "SoA block stride must be >= 16*Hk*134 bytes");
     } else {

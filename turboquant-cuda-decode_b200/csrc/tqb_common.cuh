@@ -12,6 +12,11 @@ constexpr int kKBytes = kHeadDim / 2; // packed 4-bit K codes per token-head
 constexpr int kVBytes = kHeadDim / 2; // packed 4-bit V codes per token-head
 constexpr int kDataBytes = kKBytes + kVBytes;
 constexpr int kSlotBytes = kDataBytes + 6; // + knorm, vscale, vzero (fp16)
+// FP8-key layout (TQB_LAYOUT_SOA_K8): 128 e4m3 key bytes + 64 V bytes, then
+// vscale and vzero in the block's meta region.
+constexpr int kK8KeyBytes = kHeadDim;
+constexpr int kK8DataBytes = kK8KeyBytes + kVBytes;  // 192
+constexpr int kSlotBytesK8 = kK8DataBytes + 4;       // 196
 constexpr int kNumCentroids = 16;
 
 constexpr float kLog2e = 1.4426950408889634f;

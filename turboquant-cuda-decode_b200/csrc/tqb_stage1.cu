@@ -43,6 +43,7 @@
 //    W = p * vscale is split into fp16 hi/lo across the N columns, so the
 //    product is fp32-accurate; the vzero term sum_t p_t * vzero_t is added
 //    per head in fp32.
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdlib.h>
 #include <string.h>
@@ -109,6 +110,7 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
 // One page's worth of a lane's operands.
 struct PageRegs {
     uint4 k0, k1;         // K bytes [16c, 16c+16) of tokens 2g and 2g+1
+    uint4 k0b, k1b;       // FP8 keys: K bytes [32c, 32c+32) are k0|k0b and k1|k1b
     uint2 v[4];           // V bytes [8g, 8g+8) of tokens 4c .. 4c+3
     uint32_t kn, vs, vz;  // fp16 pairs (tokens 2g, 2g+1): knorm, vscale, vzero
 };
@@ -126,7 +128,14 @@ template <int LAYOUT>
 __device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int kvh, int lane) {
     const int g = lane >> 2, c = lane & 3;
     LaneOffsets o;
-    if (LAYOUT == TQB_LAYOUT_SOA) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+        const uint32_t tok = (uint32_t)P.Hk * kK8DataBytes;
+        const uint32_t head = (uint32_t)kvh * kK8DataBytes;
+        o.row = tok;
+        o.k0 = (2 * g) * tok + head + 32 * c;
+        o.v0 = (4 * c) * tok + head + kK8KeyBytes + 8 * g;
+        o.meta = kBlockSize * tok + (uint32_t)kvh * (2 * kBlockSize * 2) + 4 * g;
+    } else if (LAYOUT == TQB_LAYOUT_SOA) {
         const uint32_t tok = (uint32_t)P.Hk * kDataBytes;
         const uint32_t head = (uint32_t)kvh * kDataBytes;
         o.row = tok;
@@ -149,6 +158,12 @@ __device__ __forceinline__ void prefetch_block(const uint8_t* block, uint32_t by
     if (leader) prefetch_l2_bulk(block, bytes);
 }
 
+// Two e4m3 bytes (low byte first) to an exact f16x2 (low half first).
+__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
 // AoS slots are only 2-byte aligned: gather with 16-bit loads.
 __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
     return ld_stream_u16(p) | (ld_stream_u16(p + 2) << 16);
@@ -156,7 +171,20 @@ __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
 
 template <int LAYOUT>
 __device__ __forceinline__ void load_page(PageRegs& r, const uint8_t* base, const LaneOffsets& o) {
-    if (LAYOUT == TQB_LAYOUT_SOA) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+        const uint8_t* k = base + o.k0;
+        const uint8_t* v = base + o.v0;
+        const uint8_t* m = base + o.meta;
+        r.k0 = ld_stream_v4(k);
+        r.k0b = ld_stream_v4(k + 16);
+        r.k1 = ld_stream_v4(k + o.row);
+        r.k1b = ld_stream_v4(k + o.row + 16);
+#pragma unroll
+        for (int j = 0; j < 4; j++) r.v[j] = ld_stream_v2(v + j * o.row);
+        r.kn = 0x3C003C00u;  // no key norm: fp16 1.0 for both tokens
+        r.vs = ld_stream_u32(m);
+        r.vz = ld_stream_u32(m + 2 * kBlockSize);
+    } else if (LAYOUT == TQB_LAYOUT_SOA) {
         const uint8_t* k = base + o.k0;
         const uint8_t* v = base + o.v0;
         const uint8_t* m = base + o.meta;
@@ -225,6 +253,22 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
 #pragma unroll
             for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
     float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
+    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+        // FP8 keys convert exactly to fp16, so one M tile holds the whole
+        // page: row g = token 2g, row g+8 = token 2g+1; k columns map to the
+        // same dims 32c + 4ks + {0,1 | 2,3} as the query fragments.  Even and
+        // odd ks accumulate in the two tiles' registers (two chains).
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const uint32_t w0 = word_of(ks < 4 ? cur.k0 : cur.k0b, ks & 3);
+            const uint32_t w1 = word_of(ks < 4 ? cur.k1 : cur.k1b, ks & 3);
+            const uint32_t a0 = fp8x2_to_h2(w0 & 0xFFFFu), a1 = fp8x2_to_h2(w1 & 0xFFFFu);
+            const uint32_t a2 = fp8x2_to_h2(w0 >> 16), a3 = fp8x2_to_h2(w1 >> 16);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+                mma_16816(dq[nt][ks & 1], a0, a1, a2, a3, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+        }
+    } else {
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
@@ -258,6 +302,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
             mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
     }
+    }  // 4-bit keys
     float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
     if (LAYOUT == TQB_LAYOUT_AOS) {
         // Norm correction c / |c| (reference/aos_decode.py:199-206).
@@ -279,8 +324,14 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
     for (int nt = 0; nt < NT; nt++) {
         // columns 2c / 2c+1: Q_hi / Q_lo parts of head c; rows g / g+8:
         // C_hi / C_lo parts of the token
-        const float d0 = (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
-        const float d1 = (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
+        // FP8 keys: columns 2c / 2c+1 = Q_hi / Q_lo of head c, rows g / g+8
+        // = tokens 2g / 2g+1, chains ks even / odd
+        const float d0 = LAYOUT == TQB_LAYOUT_SOA_K8
+                             ? (dq[nt][0][0] + dq[nt][0][1]) + (dq[nt][1][0] + dq[nt][1][1])
+                             : (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
+        const float d1 = LAYOUT == TQB_LAYOUT_SOA_K8
+                             ? (dq[nt][0][2] + dq[nt][0][3]) + (dq[nt][1][2] + dq[nt][1][3])
+                             : (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
         float s0 = d0 * kn0 * st.kfac[nt];
         float s1 = d1 * kn1 * st.kfac[nt];
         s0 = va ? s0 : -INFINITY;
@@ -359,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     // copies of {C_hi pair, C_lo pair}; AoS keeps 16 copies that also carry
     // the byte's squared centroid sum for the in-kernel norm correction),
     // then one output staging row set per warp.
-    constexpr int kEntry = LAYOUT == TQB_LAYOUT_SOA ? 8 : 16;
+    constexpr int kEntry = LAYOUT == TQB_LAYOUT_AOS ? 16 : 8;
     constexpr int kCopies = kLutStride / kEntry;
     extern __shared__ __align__(1024) uint8_t smem[];
     float* stage_all = reinterpret_cast<float*>(smem + kLutBytes);
@@ -369,12 +420,15 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     const int g = lane >> 2, c = lane & 3;
 
     // ---- centroid table -------------------------------------------------
+    // (FP8 keys need no table: their fp16 form is exact, scale exponent 0.)
     float cmax = 0.0f;
+    if (LAYOUT != TQB_LAYOUT_SOA_K8) {
 #pragma unroll
-    for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
-    const int ec = fp16_scale_exp(cmax);
+        for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
+    }
+    const int ec = LAYOUT == TQB_LAYOUT_SOA_K8 ? 0 : fp16_scale_exp(cmax);
     const float cscale = exp2i(ec);
-    for (int e = tid; e < 256 * kCopies; e += kThreads) {
+    for (int e = tid; LAYOUT != TQB_LAYOUT_SOA_K8 && e < 256 * kCopies; e += kThreads) {
         const int byte = e / kCopies;
         const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
         const float clo = a * cscale, chi = b * cscale;
@@ -607,6 +661,9 @@ int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
         const int rc = launch_stage1_ring(P, stream, num_sms);
         if (rc != TQB_ERR_UNSUPPORTED) return rc;  // else: tensor maps refused, use the register kernel
     }
+    if (P.layout == TQB_LAYOUT_SOA_K8)
+        return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K8>(P, stream, num_sms)
+                        : launch_t<2, TQB_LAYOUT_SOA_K8>(P, stream, num_sms);
     const bool soa = P.layout == TQB_LAYOUT_SOA;
     if (P.G <= 4) return soa ? launch_t<1, TQB_LAYOUT_SOA>(P, stream, num_sms)
                              : launch_t<1, TQB_LAYOUT_AOS>(P, stream, num_sms);

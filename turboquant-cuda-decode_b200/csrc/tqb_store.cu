@@ -15,6 +15,7 @@
 // running sums combined pairwise, the order numpy applies when the reference
 // kernel runs interpreted), so the written bytes are bit-identical to the
 // reference store for the same kernel inputs.
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -36,8 +37,19 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     if (slot < 0) return;  // padding token (reference/soa_store.py:275-277)
     const int64_t blk = slot / kBlockSize, off = slot % kBlockSize;
 
-    // -- keys: bucketise + pack --
     const float4 yv = __ldg(reinterpret_cast<const float4*>(P.y + pid * kHeadDim) + lane);
+    const bool k8 = P.layout == TQB_LAYOUT_SOA_K8;
+    uint32_t kpack = 0;
+    float vn = 0.0f;
+    if (k8) {
+        // FP8 keys (reference/soa_store.py:187-194): the raw key cast to e4m3
+        // with round-to-nearest-even and saturation to +-448, the conversion
+        // the compiled reference issues on sm_90 and later.
+        const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(yv.x, yv.y), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(yv.z, yv.w), __NV_SATFINITE, __NV_E4M3);
+        kpack = (uint32_t)lo | ((uint32_t)hi << 16);
+    } else {
+    // -- keys: bucketise + pack --
     const float ys[4] = {yv.x, yv.y, yv.z, yv.w};
     int idx[4];
 #pragma unroll
@@ -53,9 +65,9 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
         }
         idx[j] = lo < kNumCentroids - 1 ? lo : kNumCentroids - 1;
     }
-    const uint32_t kpack = (uint32_t)(idx[0] | (idx[1] << 4) | (idx[2] << 8) | (idx[3] << 12));
+    kpack = (uint32_t)(idx[0] | (idx[1] << 4) | (idx[2] << 8) | (idx[3] << 12));
 
-    float vn = __ldg(P.norms + pid);
+    vn = __ldg(P.norms + pid);
     if (P.norm_correction) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -80,6 +92,7 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(nsq));
         vn = __fmul_rn(vn, inv);
     }
+    }  // 4-bit keys
 
     // -- values: quantise + pack --
     const float4 vv = __ldg(reinterpret_cast<const float4*>(P.value + pid * kHeadDim) + lane);
@@ -106,7 +119,17 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     const unsigned short vn_h = __half_as_ushort(__float2half_rn(vn));
     const unsigned short sc_h = __half_as_ushort(__float2half_rn(scale));
     const unsigned short zr_h = __half_as_ushort(__float2half_rn(vmin));
-    if (P.layout == TQB_LAYOUT_SOA) {
+    if (k8) {
+        uint8_t* dp = base + off * ((int64_t)P.H * kK8DataBytes) + (int64_t)h * kK8DataBytes;
+        reinterpret_cast<uint32_t*>(dp)[lane] = kpack;  // dims 4 lane .. 4 lane + 3
+        reinterpret_cast<unsigned short*>(dp + kK8KeyBytes)[lane] = (unsigned short)vpack;
+        if (lane == 0) {
+            unsigned short* meta = reinterpret_cast<unsigned short*>(
+                base + (int64_t)kBlockSize * P.H * kK8DataBytes) + (int64_t)h * 2 * kBlockSize;
+            meta[off] = sc_h;
+            meta[kBlockSize + off] = zr_h;
+        }
+    } else if (P.layout == TQB_LAYOUT_SOA) {
         uint8_t* dp = base + off * ((int64_t)P.H * kDataBytes) + (int64_t)h * kDataBytes;
         reinterpret_cast<unsigned short*>(dp)[lane] = (unsigned short)kpack;
         reinterpret_cast<unsigned short*>(dp + kKBytes)[lane] = (unsigned short)vpack;

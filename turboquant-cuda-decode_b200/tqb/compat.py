@@ -130,10 +130,14 @@ def triton_turboquant_decode_attention(
     ``sinks`` ([Hq] per-head sink logits, cast to float32) enters split 0 of
     every sequence as the reference's ``USE_SINKS`` does
     (reference/soa_decode_v1.py:134-145, 565-605).  FP8 keys and 3-bit codes
-    are other presets of the reference and raise ``NotImplementedError``."""
-    if key_fp8 or mse_bits != 4 or value_quant_bits != 4:
-        raise NotImplementedError("only the turboquant_4bit_nc preset (4-bit K and V) is supported")
-    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, "soa", PiT=PiT,
+    are other presets of the reference and raise ``NotImplementedError``.
+    ``key_fp8=True`` is the ``turboquant_k8v4`` preset: e4m3 keys, 4-bit
+    values, the query used unrotated (reference/soa_decode_v1.py:532-533)."""
+    if value_quant_bits != 4 or (not key_fp8 and mse_bits != 4):
+        raise NotImplementedError("supported presets: turboquant_4bit_nc (4-bit K and V) and "
+                                  "turboquant_k8v4 (FP8 keys, 4-bit V)")
+    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale,
+                            "soa_k8" if key_fp8 else "soa", PiT=PiT,
                             mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
                             max_num_kv_splits=max_num_kv_splits, sinks=sinks)
 
@@ -141,19 +145,25 @@ def triton_turboquant_decode_attention(
 def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, *, PiT=None,
                      mid_o_buf=None, output_buf=None, lse_buf=None, buf_holder=None,
                      max_num_kv_splits: int = 32, sinks=None) -> torch.Tensor:
-    """Query rotation, Stage1 on the ``layout`` ("soa"/"aos") cache (with the
+    """Query rotation, Stage1 on the ``layout`` ("soa"/"aos"/"soa_k8") cache (with the
     optional attention ``sinks`` folded into split 0), Stage2; the body of
     both reference launchers (reference/soa_decode_v1.py:486-643,
     reference/aos_decode.py:486-...) with the buffer reuse they offer."""
     B, Hq, D = query.shape
-    if PiT is None:
-        PiT = Pi.T.contiguous()
-    # cast + rotation in one kernel (the reference: query.float() @ PiT,
-    # reference/soa_decode_v1.py:535-538)
-    if query.dtype in (torch.float32, torch.float16, torch.bfloat16):
-        q_rot = ops.rotate_query(query if query.stride(2) == 1 else query.contiguous(), PiT.float().contiguous())
+    if layout in ("soa_k8", "k8v4"):
+        # FP8 keys score against the query itself, read as fp32
+        # (reference/soa_decode_v1.py:532-533)
+        q_rot = query.float().contiguous()
     else:
-        q_rot = (query.float() @ PiT).contiguous()
+        if PiT is None:
+            PiT = Pi.T.contiguous()
+        # cast + rotation in one kernel (the reference: query.float() @ PiT,
+        # reference/soa_decode_v1.py:535-538)
+        if query.dtype in (torch.float32, torch.float16, torch.bfloat16):
+            q_rot = ops.rotate_query(query if query.stride(2) == 1 else query.contiguous(),
+                                     PiT.float().contiguous())
+        else:
+            q_rot = (query.float() @ PiT).contiguous()
     S = max_num_kv_splits
     if mid_o_buf is not None and mid_o_buf.shape[0] >= B and mid_o_buf.shape[2] >= S:
         mid_o = mid_o_buf[:B, :Hq, :S, :]
@@ -205,10 +215,18 @@ def triton_turboquant_store(
 ) -> None:
     """Store raw ``key``/``value`` ``[N, H, D]`` into the cache.  The host
     part (norm, normalise, rotation GEMM) is the reference launcher's
-    (reference/soa_store.py:482-487); the quantise/pack kernel is sm_100a."""
-    if key_fp8 or mse_bits != 4 or value_quant_bits != 4:
-        raise NotImplementedError("only the turboquant_4bit_nc preset (4-bit K and V) is supported")
+    (reference/soa_store.py:482-487); the quantise/pack kernel is sm_100a.
+    ``key_fp8=True`` (``turboquant_k8v4``) casts the raw key to e4m3 in the
+    kernel, SoA layout with 196 bytes per token-head
+    (reference/soa_store.py:446-479)."""
+    if value_quant_bits != 4 or (not key_fp8 and mse_bits != 4):
+        raise NotImplementedError("supported presets: turboquant_4bit_nc (4-bit K and V) and "
+                                  "turboquant_k8v4 (FP8 keys, 4-bit V)")
     N, H, D = key.shape
+    if key_fp8:
+        ops.store(key.float().reshape(N * H, D).contiguous(), None, value.float().reshape(N * H, D).contiguous(),
+                  kv_cache, slot_mapping, None, None, layout="soa_k8", norm_correction=False)
+        return
     k_flat = key.float().reshape(N * H, D)
     norms = k_flat.norm(dim=1, keepdim=True)
     x_hat = k_flat / (norms + 1e-8)

@@ -37,6 +37,11 @@ AOS_KEY_PACKED_SIZE = MSE_BYTES + 2                    # 66
 
 LAYOUT_SOA = 0
 LAYOUT_AOS = 1
+# turboquant_k8v4: e4m3 keys (128 B) + 4-bit values (64 B) per token-head,
+# meta region [Hk][2][16] fp16 (vscale, vzero): 196 bytes per token-head
+LAYOUT_SOA_K8 = 2
+K8_KEY_BYTES = HEAD_DIM
+K8_SLOT_SIZE = HEAD_DIM + VAL_DATA_BYTES + 4  # 196
 
 
 def layout_id(layout) -> int:
@@ -44,7 +49,9 @@ def layout_id(layout) -> int:
         return LAYOUT_SOA
     if layout in (LAYOUT_AOS, "aos", "AoS", "AOS"):
         return LAYOUT_AOS
-    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa' or 'aos')")
+    if layout in (LAYOUT_SOA_K8, "soa_k8", "k8v4"):
+        return LAYOUT_SOA_K8
+    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos' or 'soa_k8')")
 
 
 def block_bytes(num_kv_heads: int, block_size: int = BLOCK_SIZE) -> int:

@@ -17,7 +17,7 @@ import torch
 
 from . import _lib
 from ._lib import MergeArgs, RotateArgs, SinkArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
-from .layout import BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, layout_id
+from .layout import BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, LAYOUT_SOA_K8, layout_id
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -78,22 +78,23 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     _cuda(kv_cache, "kv_cache", torch.uint8)
     _cuda(block_table, "block_table", torch.int32)
     _cuda(seq_lens, "seq_lens", torch.int32)
-    _cuda(centroids, "centroids", torch.float32)
+    if centroids is not None or lay != LAYOUT_SOA_K8:  # FP8 keys use no centroids
+        _cuda(centroids, "centroids", torch.float32)
     _cuda(mid_o, "mid_o", torch.float32)
     _require(q_rot.dim() == 3 and q_rot.stride(2) == 1, "q_rot must be [B, Hq, D] with unit inner stride")
     _require(kv_cache.dim() == 4, "kv_cache must be [num_blocks, block_size, Hk, slot]")
     _require(block_table.dim() == 2 and block_table.stride(1) == 1, "block_table must be [B, max_blocks] row-major")
     _require(seq_lens.dim() == 1 and seq_lens.is_contiguous(), "seq_lens must be a contiguous [B] tensor")
-    _require(centroids.is_contiguous(), "centroids must be contiguous")
+    _require(centroids is None or centroids.is_contiguous(), "centroids must be contiguous")
     _require(mid_o.dim() == 4 and mid_o.stride(3) == 1, "mid_o must be [B, Hq, S, D+1] with unit inner stride")
     B, Hq, D = q_rot.shape
     nb, bs, Hk, slot = kv_cache.shape
     _require(tuple(mid_o.shape[:2]) == (B, Hq) and mid_o.shape[3] == D + 1,
              f"mid_o shape {tuple(mid_o.shape)} does not match q_rot {tuple(q_rot.shape)}")
     _require(block_table.shape[0] == B and seq_lens.shape[0] == B, "batch mismatch")
-    if lay == LAYOUT_SOA:
+    if lay in (LAYOUT_SOA, LAYOUT_SOA_K8):
         _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
-    devs = {t.device for t in (q_rot, kv_cache, block_table, seq_lens, centroids, mid_o)}
+    devs = {t.device for t in (q_rot, kv_cache, block_table, seq_lens, centroids, mid_o) if t is not None}
     _require(len(devs) == 1, f"all tensors must be on one device, got {devs}")
     nsp = None
     if num_splits_per_seq is not None:
@@ -117,8 +118,8 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     a.block_table_stride = block_table.stride(0)
     a.max_blocks_per_seq = block_table.shape[1]
     a.seq_lens = seq_lens.data_ptr()
-    a.centroids = centroids.data_ptr()
-    a.n_centroids = centroids.numel()
+    a.centroids = centroids.data_ptr() if centroids is not None else None
+    a.n_centroids = centroids.numel() if centroids is not None else 0
     a.pair_lut = pair_lut.data_ptr() if pair_lut is not None else None
     a.num_splits_per_seq = nsp.data_ptr() if nsp is not None else None
     a.mid_o = mid_o.data_ptr()
@@ -254,28 +255,36 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
           slot_mapping: torch.Tensor, midpoints: torch.Tensor, centroids: Optional[torch.Tensor] = None, *,
           layout="soa", norm_correction: bool = True, stream: Optional[int] = None) -> None:
     """Quantise ``N*H`` token-heads into the cache (kernel stage of the
-    reference store; ``y``/``norms``/``value`` are its inputs)."""
+    reference store; ``y``/``norms``/``value`` are its inputs).  With
+    ``layout="soa_k8"`` (FP8 keys) ``y`` is the raw key, cast to e4m3, and
+    ``norms``/``midpoints``/``centroids`` are unused (may be None)."""
     lay = layout_id(layout)
+    k8 = lay == LAYOUT_SOA_K8
     _cuda(y, "y", torch.float32)
-    _cuda(norms, "norms", torch.float32)
     _cuda(value, "value", torch.float32)
     _cuda(kv_cache, "kv_cache", torch.uint8)
     _cuda(slot_mapping, "slot_mapping", torch.int32)
-    _cuda(midpoints, "midpoints", torch.float32)
+    if not k8:
+        _cuda(norms, "norms", torch.float32)
+        _cuda(midpoints, "midpoints", torch.float32)
     nb, bs, H, slot = kv_cache.shape
     N = slot_mapping.shape[0]
-    _require(y.is_contiguous() and value.is_contiguous() and norms.is_contiguous(), "inputs must be contiguous")
-    _require(y.numel() == N * H * HEAD_DIM and value.numel() == N * H * HEAD_DIM and norms.numel() == N * H,
+    _require(y.is_contiguous() and value.is_contiguous() and (k8 or norms.is_contiguous()),
+             "inputs must be contiguous")
+    _require(y.numel() == N * H * HEAD_DIM and value.numel() == N * H * HEAD_DIM and (k8 or norms.numel() == N * H),
              "y/value must be [N*H, 128] and norms [N*H]")
-    if lay == LAYOUT_SOA:
+    if k8:
+        _require(not norm_correction, "FP8 keys have no norm correction")
+    if lay in (LAYOUT_SOA, LAYOUT_SOA_K8):
         _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
     if norm_correction:
         _require(centroids is not None, "norm_correction=True requires centroids")
     if centroids is not None:
         _cuda(centroids, "centroids", torch.float32)
     a = StoreArgs()
-    a.y, a.norms, a.value = y.data_ptr(), norms.data_ptr(), value.data_ptr()
-    a.midpoints = midpoints.data_ptr()
+    a.y, a.value = y.data_ptr(), value.data_ptr()
+    a.norms = norms.data_ptr() if norms is not None else None
+    a.midpoints = midpoints.data_ptr() if midpoints is not None else None
     a.centroids = centroids.data_ptr() if centroids is not None else None
     a.slot_mapping = slot_mapping.data_ptr()
     a.kv_cache = kv_cache.data_ptr()
