@@ -66,7 +66,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
-    ap.add_argument("--layout", choices=["soa", "aos"], default="soa")
+    ap.add_argument("--layout", choices=["soa", "aos", "soa_k8"], default="soa",
+                    help="cache layout; soa_k8 = the turboquant_k8v4 preset (FP8 keys, 4-bit values), c1 only")
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
@@ -140,7 +141,8 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
     R = orthogonal(seed + 1).to(dev)
     perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
     bt = perm.reshape(B, pages).to(dev)
-    kv = torch.zeros(nblk, L.BLOCK_SIZE, Hk, L.SLOT_SIZE, dtype=torch.uint8, device=dev)
+    k8 = layout == "soa_k8"
+    kv = torch.zeros(nblk, L.BLOCK_SIZE, Hk, L.K8_SLOT_SIZE if k8 else L.SLOT_SIZE, dtype=torch.uint8, device=dev)
     chunk = 8192
     tok_b = torch.arange(Lc, device=dev)
     for b in range(B):
@@ -149,11 +151,16 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
             n = min(chunk, Lc - s0)
             key = torch.randn(n, Hk, 128, generator=gen, device=dev)
             val = torch.randn(n, Hk, 128, generator=gen, device=dev)
-            tqb.triton_turboquant_store(key, val, kv, slots_b[s0:s0 + n], R, mids, 4, 66, 4,
-                                        centroids=cents, norm_correction=(layout == "soa"),
-                                        layout=layout)
+            if k8:  # keys at 3x unit scale spread over the e4m3 range
+                tqb.triton_turboquant_store(key * 3.0, val, kv, slots_b[s0:s0 + n], None, None, 8, 128, 4,
+                                            key_fp8=True)
+            else:
+                tqb.triton_turboquant_store(key, val, kv, slots_b[s0:s0 + n], R, mids, 4, 66, 4,
+                                            centroids=cents, norm_correction=(layout == "soa"),
+                                            layout=layout)
     query = torch.randn(B, Hq, 128, generator=gen, device=dev).to(torch.bfloat16)
-    q_rot = (query.float() @ R).contiguous()
+    # FP8 keys score against the unrotated query
+    q_rot = query.float().contiguous() if k8 else (query.float() @ R).contiguous()
     seq_lens = torch.full((B,), Lc, dtype=torch.int32, device=dev)
     torch.cuda.synchronize(dev)
     return dict(kv=kv, bt=bt, seq_lens=seq_lens, cents=cents, R=R, query=query, q_rot=q_rot,
@@ -161,11 +168,11 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
 
 
 def algorithmic_bytes(w) -> int:
-    """Bytes Stage1 must move: the cache slots of every token-head (134 B),
-    the fp32 query, the block-table entries used, seq_lens, the centroid
-    table, and the fp32 mid_o write."""
+    """Bytes Stage1 must move: the cache slots of every token-head (134 B;
+    196 B with FP8 keys), the fp32 query, the block-table entries used,
+    seq_lens, the centroid table, and the fp32 mid_o write."""
     B, Hq, Hk, S, Lc = w["B"], w["Hq"], w["Hk"], w["S"], w["L"]
-    cache = B * Lc * Hk * 134
+    cache = B * Lc * Hk * (196 if w["layout"] == "soa_k8" else 134)
     q = B * Hq * 128 * 4
     bt = B * math.ceil(Lc / 16) * 4
     mid = B * Hq * S * 129 * 4
@@ -344,6 +351,10 @@ def run_reference(args, world, rank):
         return
     if args.config != "c1":
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm runs the c1 headline config only"}),
+              flush=True)
+        return
+    if args.layout == "soa_k8":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm restates the 4-bit key presets only"}),
               flush=True)
         return
     from oracle import oracle as O
@@ -538,6 +549,8 @@ def main():
     args = parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
+    if args.layout == "soa_k8" and args.config != "c1":
+        raise SystemExit("--layout soa_k8 runs the single-GPU c1 workload only")
     if args.impl == "ours" and args.config != "c1":
         run_sharded(args, world, rank, local)
         if world > 1:
@@ -648,9 +661,10 @@ def main():
         def e2e_step():
             dbuf.copy_(hbuf, non_blocking=True)
             o = tqb.triton_turboquant_decode_attention(
-                dq, w["kv"], dbt, dsl, w["R"].T, w["cents"], 1.0 / math.sqrt(128), 4, 66, 4,
-                norm_correction=True, PiT=w["R"], mid_o_buf=mbuf, output_buf=obuf, lse_buf=lbuf,
-                max_num_kv_splits=S)
+                dq, w["kv"], dbt, dsl, w["R"].T, w["cents"], 1.0 / math.sqrt(128),
+                8 if args.layout == "soa_k8" else 4, 128 if args.layout == "soa_k8" else 66, 4,
+                key_fp8=args.layout == "soa_k8", norm_correction=args.layout != "soa_k8", PiT=w["R"],
+                mid_o_buf=mbuf, output_buf=obuf, lse_buf=lbuf, max_num_kv_splits=S)
             hout.copy_(o, non_blocking=True)
 
         for _ in range(3):
@@ -695,7 +709,8 @@ def main():
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)",
+        "dtype": ("f32 (e4m3 K, 4-bit V codes, fp16 tensor-core MMA, fp32 accumulate)" if args.layout == "soa_k8"
+                  else "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"),
         "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
         "config": {"workload": cfg["workload"], "layout": args.layout,
                    "per_gpu_batch": B, "global_batch": world * B, "seq_len": w["L"],
@@ -711,12 +726,13 @@ def main():
                      else "fallback 6.65 TB/s",
                      "algorithmic_bytes_per_launch": alg,
                      "kernel": ("tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)" if args.layout == "soa"
+                                else "tqb stage1_kernel (register page ring, FP8 keys)" if args.layout == "soa_k8"
                                 else "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)")},
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
-    if not args.no_cpu_baseline and world == 1:
+    if not args.no_cpu_baseline and world == 1 and args.layout != "soa_k8":  # no C restatement of FP8 keys
         line["cpu_baseline"] = cpu_baseline(w)
     print(json.dumps(line), flush=True)
     if world > 1:
