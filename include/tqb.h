@@ -69,7 +69,12 @@ typedef enum tqb_layout {
      * reference/soa_store.py:125-221): block = [16 tok][Hk][K128 e4m3 | V64]
      * + [Hk][2][16] fp16 meta (vscale, vzero); 196 bytes per token-head.  The
      * query is not rotated and the centroids are unused (may be NULL). */
-    TQB_LAYOUT_SOA_K8 = 2
+    TQB_LAYOUT_SOA_K8 = 2,
+    /* turboquant_k3v4_nc (3-bit keys, reference/config.py:31-35): block =
+     * [16 tok][Hk][K48 | V64] + [Hk][3][16] fp16 meta (knorm, vscale, vzero),
+     * 118 bytes per token-head; key dim d at bits 3d..3d+2 of its 48 bytes
+     * (little-endian, reference/soa_store.py:330-340); 8 centroids. */
+    TQB_LAYOUT_SOA_K3 = 3
 } tqb_layout;
 
 /*

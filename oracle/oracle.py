@@ -32,6 +32,7 @@ LIB_PATH = HERE / "libtqoracle.so"
 LAYOUT_SOA = 0
 LAYOUT_AOS = 1
 LAYOUT_SOA_K8 = 2  # turboquant_k8v4: [16][Hk][K128 e4m3 | V64] + [Hk][2][16] fp16 meta
+LAYOUT_SOA_K3 = 3  # turboquant_k3v4_nc: [16][Hk][K48 3-bit | V64] + [Hk][3][16] fp16 meta
 HEAD_DIM = 128
 BLOCK_SIZE = 16
 SLOT_BYTES = 134  # 64 K + 64 V + 3 fp16 metadata
@@ -241,6 +242,53 @@ def store_k8_np(key, value, slot_mapping, cache):
             flat[blk, m + 2 * bs + 2 * off : m + 2 * bs + 2 * off + 2] = np.frombuffer(zr[h].tobytes(), np.uint8)
 
 
+def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache):
+    """3-bit-key store (turboquant_k3v4_nc; reference/soa_store.py:223-373
+    with MSE_BITS = 3) into ``cache [nb, 16, H, 118]`` in place, from the
+    kernel inputs (rotated unit keys ``y [N*H, D]``, key norms, values):
+    3-step binary search over the 7 midpoints with ``y >= mid`` going right,
+    codes packed little-endian at bit 3d, stored norm = fp16(|k| /
+    sqrt(sum c^2 + 1e-16)) in fp32 (the sum in numpy's float32 order, as the
+    interpreted reference computes it), 4-bit values as the 4-bit store."""
+    nb, bs, H, slot = cache.shape
+    flat = cache.reshape(nb, bs * H * slot)
+    D = HEAD_DIM
+    kbytes, dps = D * 3 // 8, D * 3 // 8 + D // 2
+    mids = np.asarray(midpoints, np.float32)
+    c = np.asarray(centroids, np.float32)
+    y = np.asarray(y, np.float32).reshape(-1, H, D)
+    norms = np.asarray(norms, np.float32).reshape(-1, H)
+    value = np.asarray(value, np.float32).reshape(-1, H, D)
+    meta_off = bs * H * dps
+    for t, s_ in enumerate(np.asarray(slot_mapping)):
+        if s_ < 0:
+            continue
+        blk, off = int(s_) // bs, int(s_) % bs
+        q, sc, zr = _quantise_value_np(value[t])
+        for h in range(H):
+            lo = np.zeros(D, np.int64)
+            hi = np.full(D, 7, np.int64)
+            for _ in range(3):
+                mid = (lo + hi) >> 1
+                right = y[t, h] >= mids[np.minimum(mid, 6)]
+                lo = np.where(right, mid + 1, lo)
+                hi = np.where(right, hi, mid)
+            idx = np.minimum(lo, 7)
+            stream = 0
+            for d in range(D):
+                stream |= int(idx[d]) << (3 * d)
+            base = off * H * dps + h * dps
+            flat[blk, base : base + kbytes] = np.frombuffer(stream.to_bytes(kbytes, "little"), np.uint8)
+            flat[blk, base + kbytes : base + dps] = q[h, 0::2] | (q[h, 1::2] << 4)
+            cv = c[idx]
+            nsq = np.float32((cv * cv).astype(np.float32).sum(dtype=np.float32)) + np.float32(1e-16)
+            vn = np.float32(norms[t, h] * (np.float32(1.0) / np.sqrt(nsq, dtype=np.float32)))
+            m = meta_off + h * 3 * bs * 2
+            for f, val in enumerate((np.float16(vn), sc[h], zr[h])):
+                flat[blk, m + f * 2 * bs + 2 * off : m + f * 2 * bs + 2 * off + 2] = np.frombuffer(
+                    np.float16(val).tobytes(), np.uint8)
+
+
 def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
     """Dequantise tokens (block_ids[i], offs[i]) of KV head ``kvh``.
     Returns ``K [n, D]`` (centroid*norm, norm correction applied for AoS) and
@@ -259,6 +307,20 @@ def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
         vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
         return E4M3[kb], vidx * vsc[:, None] + vz[:, None]
     c = np.asarray(centroids, np.float64)
+    if layout == LAYOUT_SOA_K3:
+        kbytes, dps = D * 3 // 8, D * 3 // 8 + D // 2  # 48 packed key bytes + 64 V bytes
+        base = offs * Hk * dps + kvh * dps
+        kb = flat[block_ids[:, None], base[:, None] + np.arange(kbytes)].astype(np.int64)
+        vb = flat[block_ids[:, None], base[:, None] + kbytes + np.arange(D // 2)]
+        meta = flat[:, bs * Hk * dps :].copy().view(np.float16).reshape(nb, Hk, 3, bs)
+        knorm = meta[block_ids, kvh, 0, offs].astype(np.float64)
+        vsc = meta[block_ids, kvh, 1, offs].astype(np.float64)
+        vz = meta[block_ids, kvh, 2, offs].astype(np.float64)
+        bit = 3 * np.arange(D)
+        b0, b1 = kb[:, bit // 8], kb[:, np.minimum(bit // 8 + 1, kbytes - 1)]
+        kidx = ((b0 | (b1 << 8)) >> (bit % 8)) & 7
+        vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
+        return c[kidx] * knorm[:, None], vidx * vsc[:, None] + vz[:, None]
     if layout == LAYOUT_SOA:
         dps = D  # 64 K + 64 V bytes
         base = offs * Hk * dps + kvh * dps

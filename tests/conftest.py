@@ -54,6 +54,12 @@ def golden_k8():
 
 
 @pytest.fixture(scope="session")
+def golden_k3():
+    """turboquant_k3v4_nc (3-bit keys): the reference store and SoA Stage1."""
+    return load_golden("k3v4_ragged")
+
+
+@pytest.fixture(scope="session")
 def golden_sinks():
     """SoA Stage1 of the reference with and without attention sinks."""
     return load_golden("sinks_gqa4")

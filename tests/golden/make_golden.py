@@ -221,6 +221,70 @@ def build_k8_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
                     num_splits=np.int32(num_splits), mid_o=mid, out_stage2=o2, lse_stage2=l2))
 
 
+def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_blocks):
+    """turboquant_k3v4_nc: 3-bit Lloyd-Max keys (48 bytes, dim d at bit 3d),
+    4-bit values, norm correction; the reference SoA store with mse_bits=3
+    (``reference/soa_store.py:305-345``) and the reference SoA Stage1 with
+    MSE_BITS=3.  Also saves the store kernel's inputs as the reference
+    launcher computes them (``reference/soa_store.py:482-487``)."""
+    t0 = time.time()
+    bits, mse_bytes = 3, HEAD_DIM * 3 // 8
+    B = len(seq_lens)
+    g = torch.Generator().manual_seed(seed)
+    pages = [max(1, math.ceil(L / BLOCK_SIZE)) for L in seq_lens]
+    perm = torch.randperm(pool_blocks, generator=g)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]].to(torch.int32)
+        k += pages[b]
+    R = orthogonal(seed + 1)
+    cents = ref.centroids_mod.get_centroids(HEAD_DIM, bits).to(torch.float32)
+    mids = ((cents[:-1] + cents[1:]) * 0.5).contiguous()
+    slot = mse_bytes + VAL_BYTES + 6  # 118
+    kv = torch.randint(0, 256, (pool_blocks, BLOCK_SIZE, hk, slot), generator=g, dtype=torch.uint8)
+    ntok = sum(seq_lens)
+    key = torch.randn(ntok, hk, HEAD_DIM, generator=g, dtype=torch.float32)
+    val = torch.randn(ntok, hk, HEAD_DIM, generator=g, dtype=torch.float32)
+    slots = []
+    for b in range(B):
+        for t in range(seq_lens[b]):
+            slots.append(int(bt[b, t // BLOCK_SIZE]) * BLOCK_SIZE + t % BLOCK_SIZE)
+    slot_mapping = torch.tensor(slots, dtype=torch.int32)
+    before = kv.clone()
+    ref.soa_store.triton_turboquant_store(
+        key, val, kv, slot_mapping, R, mids, bits, mse_bytes + 2, VALUE_BITS,
+        key_fp8=False, centroids=cents, norm_correction=True)
+    k_flat = key.float().reshape(ntok * hk, HEAD_DIM)
+    norms = k_flat.norm(dim=1, keepdim=True)
+    y = (k_flat / (norms + 1e-8)) @ R
+    q = torch.randn(B, hq, HEAD_DIM, generator=g, dtype=torch.float32)
+    q_rot = (q @ R).contiguous()
+    sl = torch.tensor(seq_lens, dtype=torch.int32)
+    print(f"[{name}] store done {time.time() - t0:.1f}s", flush=True)
+    mid = torch.full((B, hq, num_splits, HEAD_DIM + 1), float("nan"), dtype=torch.float32)
+    ref.soa_dec._tq_decode_stage1[(B, hq, num_splits)](
+        q_rot, kv, kv.view(torch.uint16), bt, sl, cents, mid, None,
+        q_rot.stride(0), q_rot.stride(1), kv.stride(0), bt.stride(0),
+        mid.stride(0), mid.stride(1), mid.stride(2),
+        NUM_KV_HEADS=hk, HEAD_DIM=HEAD_DIM, BLOCK_SIZE=BLOCK_SIZE,
+        NUM_KV_SPLITS=num_splits, KV_GROUP_SIZE=hq // hk,
+        MSE_BITS=bits, MSE_BYTES=mse_bytes, VQB=VALUE_BITS,
+        VAL_DATA_BYTES=VAL_BYTES, KEY_DATA_BYTES=mse_bytes,
+        META_REGION_OFFSET=BLOCK_SIZE * hk * (mse_bytes + VAL_BYTES), NUM_SOA_FIELDS=3,
+        SOA_K_NORM=0, SOA_V_SCALE=1, SOA_V_ZERO=2,
+        ATTN_SCALE=1.0 / math.sqrt(HEAD_DIM), BLOCK_D=triton.next_power_of_2(HEAD_DIM),
+        BLOCK_KV=4, KEY_FP8=0, NORM_CORRECTION=1, FP8_E4B15=0, USE_SINKS=0,
+        num_warps=1, num_stages=1,
+    )
+    print(f"[{name}] SoA K3 Stage1 done {time.time() - t0:.1f}s", flush=True)
+    o2, l2 = run_stage2(ref, mid, sl)
+    save(name, dict(y=y, norms=norms.squeeze(1), value=val.reshape(ntok * hk, HEAD_DIM), rotation=R,
+                    slot_mapping=slot_mapping, cache_before=before, kv_cache=kv, centroids=cents,
+                    midpoints=mids, block_table=bt, seq_lens=sl, q_rot=q_rot,
+                    num_splits=np.int32(num_splits), mid_o=mid, out_stage2=o2, lse_stage2=l2))
+
+
 def run_aos_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits):
     B, Hq, D = q_rot.shape
     Hk = kv.shape[2]
@@ -439,10 +503,14 @@ CASES = {
 def main(argv):
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = Ref()
-    wanted = argv or list(CASES) + ["store", "k8v4_ragged"]
+    wanted = argv or list(CASES) + ["store", "k8v4_ragged", "k3v4_ragged"]
     for name in wanted:
         if name == "store":
             build_store_case(ref, "store_small", seed=99, ntok=48, hk=4, pool_blocks=5)
+        elif name == "k3v4_ragged":
+            # 3-bit keys, 4-bit values: ragged lengths, GQA-4
+            build_k3_case(ref, name, seed=29, seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4,
+                          pool_blocks=16)
         elif name == "k8v4_ragged":
             # FP8-key preset: ragged lengths (an empty-split sequence, splits
             # starting mid-page), GQA-4

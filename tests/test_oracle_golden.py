@@ -173,3 +173,23 @@ def test_k8v4_stage1_numpy_matches_reference(golden_k8):
     assert (np.abs(mid - ref)[w] <= ORACLE_ATOL + 1e-6 * np.abs(ref)[w]).all()
     o2, l2 = O.stage2_np(ref, z["seq_lens"])
     assert_close(o2, z["out_stage2"], atol=1e-6, rtol=0, what="stage2_np out (k8v4)")
+
+
+def test_k3v4_oracle_against_reference(golden_k3):
+    """3-bit keys (turboquant_k3v4_nc): the oracle store is bit-identical to
+    the reference store (3-bit bucketize and little-endian packing, the
+    norm-corrected fp16 norm, 4-bit values), the Stage1 restatement matches
+    the reference SoA Stage1 with MSE_BITS=3, and the 3-bit codebook equals
+    the reference's."""
+    import tqb
+    z = golden_k3
+    assert np.array_equal(tqb.get_centroids(128, 3).numpy(), z["centroids"])
+    cache = z["cache_before"].copy()
+    O.store_k3_np(z["y"], z["norms"], z["value"], z["midpoints"], z["centroids"], z["slot_mapping"], cache)
+    assert np.array_equal(cache, z["kv_cache"]), f"{(cache != z['kv_cache']).sum()} bytes differ"
+    mid = O.stage1_np(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"],
+                      int(z["num_splits"]), layout=O.LAYOUT_SOA_K3)
+    ref = z["mid_o"]
+    w = _written(ref)
+    assert np.array_equal(~np.isnan(mid[..., 0]), w)
+    assert np.abs(mid - ref)[w].max() <= ORACLE_ATOL

@@ -17,6 +17,11 @@ constexpr int kSlotBytes = kDataBytes + 6; // + knorm, vscale, vzero (fp16)
 constexpr int kK8KeyBytes = kHeadDim;
 constexpr int kK8DataBytes = kK8KeyBytes + kVBytes;  // 192
 constexpr int kSlotBytesK8 = kK8DataBytes + 4;       // 196
+// 3-bit-key layout (TQB_LAYOUT_SOA_K3): 48 packed key bytes + 64 V bytes,
+// then knorm, vscale, vzero in the meta region; 8 centroids.
+constexpr int kK3KeyBytes = kHeadDim * 3 / 8;        // 48
+constexpr int kK3DataBytes = kK3KeyBytes + kVBytes;  // 112
+constexpr int kSlotBytesK3 = kK3DataBytes + 6;       // 118
 constexpr int kNumCentroids = 16;
 
 constexpr float kLog2e = 1.4426950408889634f;

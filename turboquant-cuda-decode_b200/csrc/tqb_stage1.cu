@@ -128,7 +128,14 @@ template <int LAYOUT>
 __device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int kvh, int lane) {
     const int g = lane >> 2, c = lane & 3;
     LaneOffsets o;
-    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+        const uint32_t tok = (uint32_t)P.Hk * kK3DataBytes;
+        const uint32_t head = (uint32_t)kvh * kK3DataBytes;
+        o.row = tok;
+        o.k0 = (2 * g) * tok + head + 12 * c;  // dims 32c .. 32c+31 = key bytes 12c .. 12c+11
+        o.v0 = (4 * c) * tok + head + kK3KeyBytes + 8 * g;
+        o.meta = kBlockSize * tok + (uint32_t)kvh * (3 * kBlockSize * 2) + 4 * g;
+    } else if (LAYOUT == TQB_LAYOUT_SOA_K8) {
         const uint32_t tok = (uint32_t)P.Hk * kK8DataBytes;
         const uint32_t head = (uint32_t)kvh * kK8DataBytes;
         o.row = tok;
@@ -158,6 +165,15 @@ __device__ __forceinline__ void prefetch_block(const uint8_t* block, uint32_t by
     if (leader) prefetch_l2_bulk(block, bytes);
 }
 
+// Bits [o, o + 6) of the little-endian 96-bit stream k.x | k.y | k.z (o a
+// compile-time constant after unrolling, o + 6 <= 96).
+__device__ __forceinline__ uint32_t bits6(const uint4& k, int o) {
+    const int i = o >> 5;
+    const uint32_t lo = i == 0 ? k.x : i == 1 ? k.y : k.z;
+    const uint32_t hi = i == 0 ? k.y : i == 1 ? k.z : 0u;
+    return __funnelshift_r(lo, hi, (uint32_t)(o & 31)) & 63u;
+}
+
 // Two e4m3 bytes (low byte first) to an exact f16x2 (low half first).
 __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
     const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
@@ -171,7 +187,18 @@ __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
 
 template <int LAYOUT>
 __device__ __forceinline__ void load_page(PageRegs& r, const uint8_t* base, const LaneOffsets& o) {
-    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+        const uint8_t* k = base + o.k0;
+        const uint8_t* v = base + o.v0;
+        const uint8_t* m = base + o.meta;
+        r.k0 = make_uint4(ld_stream_u32(k), ld_stream_u32(k + 4), ld_stream_u32(k + 8), 0u);
+        r.k1 = make_uint4(ld_stream_u32(k + o.row), ld_stream_u32(k + o.row + 4), ld_stream_u32(k + o.row + 8), 0u);
+#pragma unroll
+        for (int j = 0; j < 4; j++) r.v[j] = ld_stream_v2(v + j * o.row);
+        r.kn = ld_stream_u32(m);
+        r.vs = ld_stream_u32(m + 2 * kBlockSize);
+        r.vz = ld_stream_u32(m + 4 * kBlockSize);
+    } else if (LAYOUT == TQB_LAYOUT_SOA_K8) {
         const uint8_t* k = base + o.k0;
         const uint8_t* v = base + o.v0;
         const uint8_t* m = base + o.meta;
@@ -274,12 +301,23 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         const uint32_t w0 = word_of(cur.k0, ks >> 1), w1 = word_of(cur.k1, ks >> 1);
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // (byte << 8) | this lane's copy offset, in one PRMT
-        const uint32_t ia = prmt(w0, lut_sel_src, 0x5504u | (jA << 4));  // token 2g, dims k-lo
-        const uint32_t ib = prmt(w0, lut_sel_src, 0x5504u | (jB << 4));  // token 2g, dims k-hi
-        const uint32_t ic = prmt(w1, lut_sel_src, 0x5504u | (jA << 4));  // token 2g+1
-        const uint32_t id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
+        uint32_t ia, ib, ic, id;
+        if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+            // 3-bit keys: the dim pairs 32c + 4ks + {0,1} and {2,3} are the
+            // 6-bit fields at bits 12ks and 12ks + 6 of the lane's 96 bits;
+            // entry (pair << 8) + this lane's copy offset, as below.
+            ia = (bits6(cur.k0, 12 * ks) << 8) + lut_sel_src;
+            ib = (bits6(cur.k0, 12 * ks + 6) << 8) + lut_sel_src;
+            ic = (bits6(cur.k1, 12 * ks) << 8) + lut_sel_src;
+            id = (bits6(cur.k1, 12 * ks + 6) << 8) + lut_sel_src;
+        } else {
+            ia = prmt(w0, lut_sel_src, 0x5504u | (jA << 4));  // token 2g, dims k-lo
+            ib = prmt(w0, lut_sel_src, 0x5504u | (jB << 4));  // token 2g, dims k-hi
+            ic = prmt(w1, lut_sel_src, 0x5504u | (jA << 4));  // token 2g+1
+            id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
+        }
         uint2 e0, e1, e2, e3;
-        if (LAYOUT == TQB_LAYOUT_SOA) {
+        if (LAYOUT != TQB_LAYOUT_AOS) {
             e0 = lut_v2(lut, ia);
             e1 = lut_v2(lut, ib);
             e2 = lut_v2(lut, ic);
@@ -421,21 +459,25 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
 
     // ---- centroid table -------------------------------------------------
     // (FP8 keys need no table: their fp16 form is exact, scale exponent 0.)
+    // 3-bit keys: 8 centroids, table entries for the 64 6-bit dim pairs.
+    constexpr int kNc = LAYOUT == TQB_LAYOUT_SOA_K3 ? 8 : kNumCentroids;
+    constexpr int kPairs = LAYOUT == TQB_LAYOUT_SOA_K3 ? 64 : 256;
+    constexpr int kLowBits = LAYOUT == TQB_LAYOUT_SOA_K3 ? 3 : 4;
     float cmax = 0.0f;
     if (LAYOUT != TQB_LAYOUT_SOA_K8) {
 #pragma unroll
-        for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
+        for (int k = 0; k < kNc; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     }
     const int ec = LAYOUT == TQB_LAYOUT_SOA_K8 ? 0 : fp16_scale_exp(cmax);
     const float cscale = exp2i(ec);
-    for (int e = tid; LAYOUT != TQB_LAYOUT_SOA_K8 && e < 256 * kCopies; e += kThreads) {
+    for (int e = tid; LAYOUT != TQB_LAYOUT_SOA_K8 && e < kPairs * kCopies; e += kThreads) {
         const int byte = e / kCopies;
-        const float a = __ldg(P.cents + (byte & 15)), b = __ldg(P.cents + (byte >> 4));
+        const float a = __ldg(P.cents + (byte & (kNc - 1))), b = __ldg(P.cents + (byte >> kLowBits));
         const float clo = a * cscale, chi = b * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
         uint8_t* dst = smem + (size_t)e * kEntry;
-        if (LAYOUT == TQB_LAYOUT_SOA) {
+        if (LAYOUT != TQB_LAYOUT_AOS) {
             *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
         } else {
             *reinterpret_cast<uint4*>(dst) =
@@ -664,6 +706,9 @@ int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     if (P.layout == TQB_LAYOUT_SOA_K8)
         return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K8>(P, stream, num_sms)
                         : launch_t<2, TQB_LAYOUT_SOA_K8>(P, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K3)
+        return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K3>(P, stream, num_sms)
+                        : launch_t<2, TQB_LAYOUT_SOA_K3>(P, stream, num_sms);
     const bool soa = P.layout == TQB_LAYOUT_SOA;
     if (P.G <= 4) return soa ? launch_t<1, TQB_LAYOUT_SOA>(P, stream, num_sms)
                              : launch_t<1, TQB_LAYOUT_AOS>(P, stream, num_sms);

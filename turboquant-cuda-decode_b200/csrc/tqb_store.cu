@@ -51,21 +51,27 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     } else {
     // -- keys: bucketise + pack --
     const float ys[4] = {yv.x, yv.y, yv.z, yv.w};
+    // 3-bit keys: 8 centroids, 3 search steps (reference/soa_store.py:305-314
+    // with MSE_BITS = 3)
+    const bool k3 = P.layout == TQB_LAYOUT_SOA_K3;
+    const int nc = k3 ? 8 : kNumCentroids, steps = k3 ? 3 : 4;
     int idx[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        int lo = 0, hi = kNumCentroids - 1;
+        int lo = 0, hi = nc - 1;
 #pragma unroll
         for (int it = 0; it < 4; it++) {
+            if (it >= steps) break;
             const int mid = (lo + hi) >> 1;
-            const int safe = mid < kNumCentroids - 2 ? mid : kNumCentroids - 2;
+            const int safe = mid < nc - 2 ? mid : nc - 2;
             const bool right = ys[j] >= __ldg(P.mids + safe);
             lo = right ? mid + 1 : lo;
             hi = right ? hi : mid;
         }
-        idx[j] = lo < kNumCentroids - 1 ? lo : kNumCentroids - 1;
+        idx[j] = lo < nc - 1 ? lo : nc - 1;
     }
-    kpack = (uint32_t)(idx[0] | (idx[1] << 4) | (idx[2] << 8) | (idx[3] << 12));
+    kpack = k3 ? (uint32_t)(idx[0] | (idx[1] << 3) | (idx[2] << 6) | (idx[3] << 9))  // 12 bits, dim 4 lane at bit 0
+               : (uint32_t)(idx[0] | (idx[1] << 4) | (idx[2] << 8) | (idx[3] << 12));
 
     vn = __ldg(P.norms + pid);
     if (P.norm_correction) {
@@ -128,6 +134,26 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
                 base + (int64_t)kBlockSize * P.H * kK8DataBytes) + (int64_t)h * 2 * kBlockSize;
             meta[off] = sc_h;
             meta[kBlockSize + off] = zr_h;
+        }
+    } else if (P.layout == TQB_LAYOUT_SOA_K3) {
+        uint8_t* dp = base + off * ((int64_t)P.H * kK3DataBytes) + (int64_t)h * kK3DataBytes;
+        // Lanes 2m and 2m+1 hold dims 8m .. 8m+7 = bits 24m .. 24m+23 of the
+        // little-endian 3-bit stream, i.e. bytes 3m .. 3m+2.
+        const uint32_t up = __shfl_down_sync(0xffffffffu, kpack, 1);
+        if ((lane & 1) == 0) {
+            const uint32_t p24 = kpack | (up << 12);
+            uint8_t* kb = dp + 3 * (lane >> 1);
+            kb[0] = (uint8_t)p24;
+            kb[1] = (uint8_t)(p24 >> 8);
+            kb[2] = (uint8_t)(p24 >> 16);
+        }
+        reinterpret_cast<unsigned short*>(dp + kK3KeyBytes)[lane] = (unsigned short)vpack;
+        if (lane == 0) {
+            unsigned short* meta = reinterpret_cast<unsigned short*>(
+                base + (int64_t)kBlockSize * P.H * kK3DataBytes) + (int64_t)h * 3 * kBlockSize;
+            meta[off] = vn_h;
+            meta[kBlockSize + off] = sc_h;
+            meta[2 * kBlockSize + off] = zr_h;
         }
     } else if (P.layout == TQB_LAYOUT_SOA) {
         uint8_t* dp = base + off * ((int64_t)P.H * kDataBytes) + (int64_t)h * kDataBytes;

@@ -25,6 +25,7 @@ TQB_ERR_CUDA = -5
 TQB_LAYOUT_SOA = 0
 TQB_LAYOUT_AOS = 1
 TQB_LAYOUT_SOA_K8 = 2
+TQB_LAYOUT_SOA_K3 = 3
 
 TQB_P2P_MAX_RANKS = 8
 TQB_IPC_HANDLE_BYTES = 64

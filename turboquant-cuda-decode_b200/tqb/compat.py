@@ -132,12 +132,14 @@ def triton_turboquant_decode_attention(
     (reference/soa_decode_v1.py:134-145, 565-605).  FP8 keys and 3-bit codes
     are other presets of the reference and raise ``NotImplementedError``.
     ``key_fp8=True`` is the ``turboquant_k8v4`` preset: e4m3 keys, 4-bit
-    values, the query used unrotated (reference/soa_decode_v1.py:532-533)."""
-    if value_quant_bits != 4 or (not key_fp8 and mse_bits != 4):
-        raise NotImplementedError("supported presets: turboquant_4bit_nc (4-bit K and V) and "
-                                  "turboquant_k8v4 (FP8 keys, 4-bit V)")
+    values, the query used unrotated (reference/soa_decode_v1.py:532-533);
+    ``mse_bits=3`` the ``turboquant_k3v4_nc`` preset (3-bit keys, 8
+    centroids)."""
+    if value_quant_bits != 4 or (not key_fp8 and mse_bits not in (3, 4)):
+        raise NotImplementedError("supported presets: turboquant_4bit_nc, turboquant_k3v4_nc (3-bit K, "
+                                  "4-bit V) and turboquant_k8v4 (FP8 keys, 4-bit V)")
     return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale,
-                            "soa_k8" if key_fp8 else "soa", PiT=PiT,
+                            "soa_k8" if key_fp8 else ("soa_k3" if mse_bits == 3 else "soa"), PiT=PiT,
                             mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
                             max_num_kv_splits=max_num_kv_splits, sinks=sinks)
 
@@ -219,9 +221,11 @@ def triton_turboquant_store(
     ``key_fp8=True`` (``turboquant_k8v4``) casts the raw key to e4m3 in the
     kernel, SoA layout with 196 bytes per token-head
     (reference/soa_store.py:446-479)."""
-    if value_quant_bits != 4 or (not key_fp8 and mse_bits != 4):
-        raise NotImplementedError("supported presets: turboquant_4bit_nc (4-bit K and V) and "
-                                  "turboquant_k8v4 (FP8 keys, 4-bit V)")
+    if value_quant_bits != 4 or (not key_fp8 and mse_bits not in (3, 4)):
+        raise NotImplementedError("supported presets: turboquant_4bit_nc, turboquant_k3v4_nc (3-bit K, "
+                                  "4-bit V) and turboquant_k8v4 (FP8 keys, 4-bit V)")
+    if mse_bits == 3 and not key_fp8:
+        layout = "soa_k3"  # the 3-bit preset's SoA cache (118 bytes per token-head)
     N, H, D = key.shape
     if key_fp8:
         ops.store(key.float().reshape(N * H, D).contiguous(), None, value.float().reshape(N * H, D).contiguous(),

@@ -42,6 +42,11 @@ LAYOUT_AOS = 1
 LAYOUT_SOA_K8 = 2
 K8_KEY_BYTES = HEAD_DIM
 K8_SLOT_SIZE = HEAD_DIM + VAL_DATA_BYTES + 4  # 196
+# turboquant_k3v4_nc: 3-bit keys (48 B, dim d at bit 3d) + 4-bit values,
+# meta region [Hk][3][16] fp16 (knorm, vscale, vzero): 118 bytes per token-head
+LAYOUT_SOA_K3 = 3
+K3_KEY_BYTES = HEAD_DIM * 3 // 8
+K3_SLOT_SIZE = K3_KEY_BYTES + VAL_DATA_BYTES + 6  # 118
 
 
 def layout_id(layout) -> int:
@@ -51,7 +56,9 @@ def layout_id(layout) -> int:
         return LAYOUT_AOS
     if layout in (LAYOUT_SOA_K8, "soa_k8", "k8v4"):
         return LAYOUT_SOA_K8
-    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos' or 'soa_k8')")
+    if layout in (LAYOUT_SOA_K3, "soa_k3", "k3v4"):
+        return LAYOUT_SOA_K3
+    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos', 'soa_k8' or 'soa_k3')")
 
 
 def block_bytes(num_kv_heads: int, block_size: int = BLOCK_SIZE) -> int:
