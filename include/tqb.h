@@ -74,7 +74,12 @@ typedef enum tqb_layout {
      * [16 tok][Hk][K48 | V64] + [Hk][3][16] fp16 meta (knorm, vscale, vzero),
      * 118 bytes per token-head; key dim d at bits 3d..3d+2 of its 48 bytes
      * (little-endian, reference/soa_store.py:330-340); 8 centroids. */
-    TQB_LAYOUT_SOA_K3 = 3
+    TQB_LAYOUT_SOA_K3 = 3,
+    /* turboquant_3bit_nc (reference/config.py:36-40): as TQB_LAYOUT_SOA_K3
+     * with 3-bit values too: [16 tok][Hk][K48 | V48] + [Hk][3][16] fp16 meta,
+     * 102 bytes per token-head; value dim d at bits 3d..3d+2 of its 48 bytes,
+     * v = code * vscale + vzero with codes 0..7. */
+    TQB_LAYOUT_SOA_K3V3 = 4
 } tqb_layout;
 
 /*

@@ -33,6 +33,7 @@ LAYOUT_SOA = 0
 LAYOUT_AOS = 1
 LAYOUT_SOA_K8 = 2  # turboquant_k8v4: [16][Hk][K128 e4m3 | V64] + [Hk][2][16] fp16 meta
 LAYOUT_SOA_K3 = 3  # turboquant_k3v4_nc: [16][Hk][K48 3-bit | V64] + [Hk][3][16] fp16 meta
+LAYOUT_SOA_K3V3 = 4  # turboquant_3bit_nc: [16][Hk][K48 3-bit | V48 3-bit] + [Hk][3][16] fp16 meta
 HEAD_DIM = 128
 BLOCK_SIZE = 16
 SLOT_BYTES = 134  # 64 K + 64 V + 3 fp16 metadata
@@ -205,15 +206,17 @@ def e4m3_encode(x) -> np.ndarray:
     return np.where(np.isnan(x), np.uint8(0x7F), out).astype(np.uint8)
 
 
-def _quantise_value_np(v):
-    """4-bit value quantiser of the reference store in fp32
-    (reference/soa_store.py:85-116): returns codes and the fp16 scale/zero."""
+def _quantise_value_np(v, bits=4):
+    """Value quantiser of the reference store in fp32 (4-bit:
+    reference/soa_store.py:85-116; 3-bit: :49-60): returns codes and the
+    fp16 scale/zero."""
     v = np.asarray(v, np.float32)
+    top = (1 << bits) - 1
     vmin, vmax = v.min(-1, keepdims=True), v.max(-1, keepdims=True)
-    scale = (vmax - vmin) / np.float32(15.0)
+    scale = (vmax - vmin) / np.float32(top)
     scale = np.where(scale > np.float32(1e-8), scale, np.float32(1e-8)).astype(np.float32)
     t = ((v - vmin) / scale + np.float32(0.5)).astype(np.float32)
-    q = np.clip(np.trunc(t), 0, 15).astype(np.uint8)
+    q = np.clip(np.trunc(t), 0, top).astype(np.uint8)
     return q, scale[..., 0].astype(np.float16), vmin[..., 0].astype(np.float16)
 
 
@@ -242,18 +245,27 @@ def store_k8_np(key, value, slot_mapping, cache):
             flat[blk, m + 2 * bs + 2 * off : m + 2 * bs + 2 * off + 2] = np.frombuffer(zr[h].tobytes(), np.uint8)
 
 
-def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache):
+def _pack3(codes) -> np.ndarray:
+    """128 3-bit codes -> 48 bytes, code d at bits 3d..3d+2 (little-endian)."""
+    stream = 0
+    for d, x in enumerate(np.asarray(codes)):
+        stream |= int(x) << (3 * d)
+    return np.frombuffer(stream.to_bytes(len(codes) * 3 // 8, "little"), np.uint8)
+
+
+def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache, vbits=4):
     """3-bit-key store (turboquant_k3v4_nc; reference/soa_store.py:223-373
     with MSE_BITS = 3) into ``cache [nb, 16, H, 118]`` in place, from the
     kernel inputs (rotated unit keys ``y [N*H, D]``, key norms, values):
     3-step binary search over the 7 midpoints with ``y >= mid`` going right,
     codes packed little-endian at bit 3d, stored norm = fp16(|k| /
     sqrt(sum c^2 + 1e-16)) in fp32 (the sum in numpy's float32 order, as the
-    interpreted reference computes it), 4-bit values as the 4-bit store."""
+    interpreted reference computes it), values as the 4-bit store, or with
+    ``vbits=3`` (turboquant_3bit_nc) 7 levels packed like the keys."""
     nb, bs, H, slot = cache.shape
     flat = cache.reshape(nb, bs * H * slot)
     D = HEAD_DIM
-    kbytes, dps = D * 3 // 8, D * 3 // 8 + D // 2
+    kbytes, dps = D * 3 // 8, D * 3 // 8 + D * vbits // 8
     mids = np.asarray(midpoints, np.float32)
     c = np.asarray(centroids, np.float32)
     y = np.asarray(y, np.float32).reshape(-1, H, D)
@@ -264,7 +276,7 @@ def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache):
         if s_ < 0:
             continue
         blk, off = int(s_) // bs, int(s_) % bs
-        q, sc, zr = _quantise_value_np(value[t])
+        q, sc, zr = _quantise_value_np(value[t], vbits)
         for h in range(H):
             lo = np.zeros(D, np.int64)
             hi = np.full(D, 7, np.int64)
@@ -274,12 +286,9 @@ def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache):
                 lo = np.where(right, mid + 1, lo)
                 hi = np.where(right, hi, mid)
             idx = np.minimum(lo, 7)
-            stream = 0
-            for d in range(D):
-                stream |= int(idx[d]) << (3 * d)
             base = off * H * dps + h * dps
-            flat[blk, base : base + kbytes] = np.frombuffer(stream.to_bytes(kbytes, "little"), np.uint8)
-            flat[blk, base + kbytes : base + dps] = q[h, 0::2] | (q[h, 1::2] << 4)
+            flat[blk, base : base + kbytes] = _pack3(idx)
+            flat[blk, base + kbytes : base + dps] = _pack3(q[h]) if vbits == 3 else q[h, 0::2] | (q[h, 1::2] << 4)
             cv = c[idx]
             nsq = np.float32((cv * cv).astype(np.float32).sum(dtype=np.float32)) + np.float32(1e-16)
             vn = np.float32(norms[t, h] * (np.float32(1.0) / np.sqrt(nsq, dtype=np.float32)))
@@ -307,11 +316,13 @@ def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
         vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
         return E4M3[kb], vidx * vsc[:, None] + vz[:, None]
     c = np.asarray(centroids, np.float64)
-    if layout == LAYOUT_SOA_K3:
-        kbytes, dps = D * 3 // 8, D * 3 // 8 + D // 2  # 48 packed key bytes + 64 V bytes
+    if layout in (LAYOUT_SOA_K3, LAYOUT_SOA_K3V3):
+        v3 = layout == LAYOUT_SOA_K3V3
+        kbytes = D * 3 // 8                          # 48 packed key bytes
+        dps = kbytes + (D * 3 // 8 if v3 else D // 2)  # + 48 (3-bit) or 64 (4-bit) V bytes
         base = offs * Hk * dps + kvh * dps
         kb = flat[block_ids[:, None], base[:, None] + np.arange(kbytes)].astype(np.int64)
-        vb = flat[block_ids[:, None], base[:, None] + kbytes + np.arange(D // 2)]
+        vb = flat[block_ids[:, None], base[:, None] + kbytes + np.arange(dps - kbytes)].astype(np.int64)
         meta = flat[:, bs * Hk * dps :].copy().view(np.float16).reshape(nb, Hk, 3, bs)
         knorm = meta[block_ids, kvh, 0, offs].astype(np.float64)
         vsc = meta[block_ids, kvh, 1, offs].astype(np.float64)
@@ -319,7 +330,11 @@ def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
         bit = 3 * np.arange(D)
         b0, b1 = kb[:, bit // 8], kb[:, np.minimum(bit // 8 + 1, kbytes - 1)]
         kidx = ((b0 | (b1 << 8)) >> (bit % 8)) & 7
-        vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
+        if v3:
+            c0, c1 = vb[:, bit // 8], vb[:, np.minimum(bit // 8 + 1, kbytes - 1)]
+            vidx = (((c0 | (c1 << 8)) >> (bit % 8)) & 7).astype(np.float64)
+        else:
+            vidx = np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D).astype(np.float64)
         return c[kidx] * knorm[:, None], vidx * vsc[:, None] + vz[:, None]
     if layout == LAYOUT_SOA:
         dps = D  # 64 K + 64 V bytes

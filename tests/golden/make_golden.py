@@ -221,14 +221,16 @@ def build_k8_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
                     num_splits=np.int32(num_splits), mid_o=mid, out_stage2=o2, lse_stage2=l2))
 
 
-def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_blocks):
+def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_blocks, vbits=VALUE_BITS):
     """turboquant_k3v4_nc: 3-bit Lloyd-Max keys (48 bytes, dim d at bit 3d),
     4-bit values, norm correction; the reference SoA store with mse_bits=3
     (``reference/soa_store.py:305-345``) and the reference SoA Stage1 with
     MSE_BITS=3.  Also saves the store kernel's inputs as the reference
-    launcher computes them (``reference/soa_store.py:482-487``)."""
+    launcher computes them (``reference/soa_store.py:482-487``).  ``vbits=3``
+    is ``turboquant_3bit_nc``: 3-bit values too (48 bytes, same packing)."""
     t0 = time.time()
     bits, mse_bytes = 3, HEAD_DIM * 3 // 8
+    vbytes = HEAD_DIM * vbits // 8
     B = len(seq_lens)
     g = torch.Generator().manual_seed(seed)
     pages = [max(1, math.ceil(L / BLOCK_SIZE)) for L in seq_lens]
@@ -241,7 +243,7 @@ def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
     R = orthogonal(seed + 1)
     cents = ref.centroids_mod.get_centroids(HEAD_DIM, bits).to(torch.float32)
     mids = ((cents[:-1] + cents[1:]) * 0.5).contiguous()
-    slot = mse_bytes + VAL_BYTES + 6  # 118
+    slot = mse_bytes + vbytes + 6  # 118 (4-bit values) or 102 (3-bit)
     kv = torch.randint(0, 256, (pool_blocks, BLOCK_SIZE, hk, slot), generator=g, dtype=torch.uint8)
     ntok = sum(seq_lens)
     key = torch.randn(ntok, hk, HEAD_DIM, generator=g, dtype=torch.float32)
@@ -253,7 +255,7 @@ def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
     slot_mapping = torch.tensor(slots, dtype=torch.int32)
     before = kv.clone()
     ref.soa_store.triton_turboquant_store(
-        key, val, kv, slot_mapping, R, mids, bits, mse_bytes + 2, VALUE_BITS,
+        key, val, kv, slot_mapping, R, mids, bits, mse_bytes + 2, vbits,
         key_fp8=False, centroids=cents, norm_correction=True)
     k_flat = key.float().reshape(ntok * hk, HEAD_DIM)
     norms = k_flat.norm(dim=1, keepdim=True)
@@ -269,9 +271,9 @@ def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
         mid.stride(0), mid.stride(1), mid.stride(2),
         NUM_KV_HEADS=hk, HEAD_DIM=HEAD_DIM, BLOCK_SIZE=BLOCK_SIZE,
         NUM_KV_SPLITS=num_splits, KV_GROUP_SIZE=hq // hk,
-        MSE_BITS=bits, MSE_BYTES=mse_bytes, VQB=VALUE_BITS,
-        VAL_DATA_BYTES=VAL_BYTES, KEY_DATA_BYTES=mse_bytes,
-        META_REGION_OFFSET=BLOCK_SIZE * hk * (mse_bytes + VAL_BYTES), NUM_SOA_FIELDS=3,
+        MSE_BITS=bits, MSE_BYTES=mse_bytes, VQB=vbits,
+        VAL_DATA_BYTES=vbytes, KEY_DATA_BYTES=mse_bytes,
+        META_REGION_OFFSET=BLOCK_SIZE * hk * (mse_bytes + vbytes), NUM_SOA_FIELDS=3,
         SOA_K_NORM=0, SOA_V_SCALE=1, SOA_V_ZERO=2,
         ATTN_SCALE=1.0 / math.sqrt(HEAD_DIM), BLOCK_D=triton.next_power_of_2(HEAD_DIM),
         BLOCK_KV=4, KEY_FP8=0, NORM_CORRECTION=1, FP8_E4B15=0, USE_SINKS=0,
@@ -503,7 +505,7 @@ CASES = {
 def main(argv):
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = Ref()
-    wanted = argv or list(CASES) + ["store", "k8v4_ragged", "k3v4_ragged"]
+    wanted = argv or list(CASES) + ["store", "k8v4_ragged", "k3v4_ragged", "k3v3_ragged"]
     for name in wanted:
         if name == "store":
             build_store_case(ref, "store_small", seed=99, ntok=48, hk=4, pool_blocks=5)
@@ -511,6 +513,10 @@ def main(argv):
             # 3-bit keys, 4-bit values: ragged lengths, GQA-4
             build_k3_case(ref, name, seed=29, seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4,
                           pool_blocks=16)
+        elif name == "k3v3_ragged":
+            # 3-bit keys and 3-bit values (turboquant_3bit_nc), GQA-4
+            build_k3_case(ref, name, seed=37, seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4,
+                          pool_blocks=16, vbits=3)
         elif name == "k8v4_ragged":
             # FP8-key preset: ragged lengths (an empty-split sequence, splits
             # starting mid-page), GQA-4

@@ -193,3 +193,21 @@ def test_k3v4_oracle_against_reference(golden_k3):
     w = _written(ref)
     assert np.array_equal(~np.isnan(mid[..., 0]), w)
     assert np.abs(mid - ref)[w].max() <= ORACLE_ATOL
+
+
+def test_k3v3_oracle_against_reference():
+    """3-bit keys and values (turboquant_3bit_nc): the oracle store is
+    bit-identical to the reference store (values: 7 levels, packed like the
+    keys) and the Stage1 restatement matches the reference SoA Stage1 with
+    MSE_BITS=3 and VQB=3."""
+    from conftest import load_golden
+    z = load_golden("k3v3_ragged")
+    cache = z["cache_before"].copy()
+    O.store_k3_np(z["y"], z["norms"], z["value"], z["midpoints"], z["centroids"], z["slot_mapping"], cache, vbits=3)
+    assert np.array_equal(cache, z["kv_cache"]), f"{(cache != z['kv_cache']).sum()} bytes differ"
+    mid = O.stage1_np(z["q_rot"], z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"],
+                      int(z["num_splits"]), layout=O.LAYOUT_SOA_K3V3)
+    ref = z["mid_o"]
+    w = _written(ref)
+    assert np.array_equal(~np.isnan(mid[..., 0]), w)
+    assert np.abs(mid - ref)[w].max() <= ORACLE_ATOL

@@ -119,15 +119,16 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                 TQB_ERR_INVALID_ARG, "batch/heads/num_splits must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
-    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, k3 = a->layout == TQB_LAYOUT_SOA_K3;
+    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, v3 = a->layout == TQB_LAYOUT_SOA_K3V3;
+    const bool k3 = a->layout == TQB_LAYOUT_SOA_K3 || v3;
     TQB_REQUIRE(k8 || a->n_centroids == (k3 ? 8 : tqb::kNumCentroids), TQB_ERR_UNSUPPORTED,
-                "n_centroids must be 16 (4-bit keys) or 8 (TQB_LAYOUT_SOA_K3)");
+                "n_centroids must be 16 (4-bit keys) or 8 (3-bit keys)");
     TQB_REQUIRE(a->num_q_heads % a->num_kv_heads == 0, TQB_ERR_INVALID_ARG,
                 "num_q_heads must be a multiple of num_kv_heads");
     const int G = a->num_q_heads / a->num_kv_heads;
     TQB_REQUIRE(G <= 8, TQB_ERR_UNSUPPORTED, "GQA group size must be <= 8");
     TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8 || k3, TQB_ERR_INVALID_ARG,
-                "layout must be TQB_LAYOUT_SOA, TQB_LAYOUT_AOS, TQB_LAYOUT_SOA_K8 or TQB_LAYOUT_SOA_K3");
+                "layout must be a tqb_layout value");
     if (a->batch == 0) return TQB_OK;
     TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens && (a->centroids || k8) && a->mid_o,
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
@@ -146,9 +147,10 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                     TQB_ERR_ALIGNMENT, "FP8-key block stride must be >= 16*Hk*196 bytes and a multiple of 16");
     } else if (k3) {
         TQB_REQUIRE(aligned(a->kv_cache, 16), TQB_ERR_ALIGNMENT, "SoA kv_cache must be 16-byte aligned");
-        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytesK3 &&
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * (v3 ? tqb::kSlotBytesK3V3 : tqb::kSlotBytesK3) &&
                         a->cache_stride_block % 16 == 0,
-                    TQB_ERR_ALIGNMENT, "3-bit-key block stride must be >= 16*Hk*118 bytes and a multiple of 16");
+                    TQB_ERR_ALIGNMENT, "3-bit-key block stride must be >= 16*Hk*slot bytes (118, or 102 with "
+                                       "3-bit values) and a multiple of 16");
     } else if (a->layout == TQB_LAYOUT_SOA) {
         TQB_REQUIRE(aligned(a->kv_cache, 16), TQB_ERR_ALIGNMENT, "SoA kv_cache must be 16-byte aligned");
         TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes &&
@@ -476,11 +478,12 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
                 "num_tokens must be >= 0 and num_kv_heads > 0");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
-    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, k3 = a->layout == TQB_LAYOUT_SOA_K3;
+    const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, v3 = a->layout == TQB_LAYOUT_SOA_K3V3;
+    const bool k3 = a->layout == TQB_LAYOUT_SOA_K3 || v3;
     TQB_REQUIRE(k8 || a->n_centroids == (k3 ? 8 : tqb::kNumCentroids), TQB_ERR_UNSUPPORTED,
-                "n_centroids must be 16, or 8 for TQB_LAYOUT_SOA_K3");
+                "n_centroids must be 16, or 8 for 3-bit keys");
     TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8 || k3, TQB_ERR_INVALID_ARG,
-                "layout must be TQB_LAYOUT_SOA, TQB_LAYOUT_AOS, TQB_LAYOUT_SOA_K8 or TQB_LAYOUT_SOA_K3");
+                "layout must be a tqb_layout value");
     TQB_REQUIRE(!(k8 && a->norm_correction), TQB_ERR_INVALID_ARG,
                 "the FP8-key layout has no norm correction");
     if (a->num_tokens == 0) return TQB_OK;
@@ -499,8 +502,8 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
                     TQB_ERR_INVALID_ARG, "FP8-key block stride must be >= 16*Hk*196 bytes and a multiple of 4");
         TQB_REQUIRE(aligned(a->kv_cache, 4), TQB_ERR_ALIGNMENT, "FP8-key kv_cache must be 4-byte aligned");
     } else if (k3) {
-        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytesK3,
-                    TQB_ERR_INVALID_ARG, "3-bit-key block stride must be >= 16*Hk*118 bytes");
+        TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * (v3 ? tqb::kSlotBytesK3V3 : tqb::kSlotBytesK3),
+                    TQB_ERR_INVALID_ARG, "3-bit-key block stride must be >= 16*Hk*slot bytes (118, or 102 with 3-bit values)");
     } else if (a->layout == TQB_LAYOUT_SOA) {
         TQB_REQUIRE(a->cache_stride_block >= tqb::kBlockSize * hk * tqb::kSlotBytes,
                     TQB_ERR_INVALID_ARG, "SoA block stride must be >= 16*Hk*134 bytes");

@@ -22,6 +22,10 @@ constexpr int kSlotBytesK8 = kK8DataBytes + 4;       // 196
 constexpr int kK3KeyBytes = kHeadDim * 3 / 8;        // 48
 constexpr int kK3DataBytes = kK3KeyBytes + kVBytes;  // 112
 constexpr int kSlotBytesK3 = kK3DataBytes + 6;       // 118
+// 3-bit keys and values (TQB_LAYOUT_SOA_K3V3): 48 + 48 data bytes + meta.
+constexpr int kV3Bytes = kHeadDim * 3 / 8;           // 48
+constexpr int kK3V3DataBytes = kK3KeyBytes + kV3Bytes;  // 96
+constexpr int kSlotBytesK3V3 = kK3V3DataBytes + 6;   // 102
 constexpr int kNumCentroids = 16;
 
 constexpr float kLog2e = 1.4426950408889634f;

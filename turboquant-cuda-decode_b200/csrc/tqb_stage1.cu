@@ -128,7 +128,14 @@ template <int LAYOUT>
 __device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int kvh, int lane) {
     const int g = lane >> 2, c = lane & 3;
     LaneOffsets o;
-    if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K3V3) {
+        const uint32_t tok = (uint32_t)P.Hk * kK3V3DataBytes;
+        const uint32_t head = (uint32_t)kvh * kK3V3DataBytes;
+        o.row = tok;
+        o.k0 = (2 * g) * tok + head + 12 * c;
+        o.v0 = (4 * c) * tok + head + kK3KeyBytes + 6 * g;  // dims 16g .. 16g+15 = 6 value bytes
+        o.meta = kBlockSize * tok + (uint32_t)kvh * (3 * kBlockSize * 2) + 4 * g;
+    } else if (LAYOUT == TQB_LAYOUT_SOA_K3) {
         const uint32_t tok = (uint32_t)P.Hk * kK3DataBytes;
         const uint32_t head = (uint32_t)kvh * kK3DataBytes;
         o.row = tok;
@@ -165,6 +172,14 @@ __device__ __forceinline__ void prefetch_block(const uint8_t* block, uint32_t by
     if (leader) prefetch_l2_bulk(block, bytes);
 }
 
+// Eight 3-bit fields (bits 3i .. 3i+2 of h, 24 bits) to eight nibbles
+// (bits 4i .. 4i+2): halves, then quarters, then pairs move apart.
+__device__ __forceinline__ uint32_t spread3to4(uint32_t h) {
+    const uint32_t z = (h & 0xFFFu) | ((h & 0xFFF000u) << 4);
+    const uint32_t w = (z & 0x003F003Fu) | ((z & 0x0FC00FC0u) << 2);
+    return (w & 0x07070707u) | ((w & 0x38383838u) << 1);
+}
+
 // Bits [o, o + 6) of the little-endian 96-bit stream k.x | k.y | k.z (o a
 // compile-time constant after unrolling, o + 6 <= 96).
 __device__ __forceinline__ uint32_t bits6(const uint4& k, int o) {
@@ -187,7 +202,24 @@ __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {
 
 template <int LAYOUT>
 __device__ __forceinline__ void load_page(PageRegs& r, const uint8_t* base, const LaneOffsets& o) {
-    if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+    if (LAYOUT == TQB_LAYOUT_SOA_K3V3) {
+        const uint8_t* k = base + o.k0;
+        const uint8_t* v = base + o.v0;
+        const uint8_t* m = base + o.meta;
+        r.k0 = make_uint4(ld_stream_u32(k), ld_stream_u32(k + 4), ld_stream_u32(k + 8), 0u);
+        r.k1 = make_uint4(ld_stream_u32(k + o.row), ld_stream_u32(k + o.row + 4), ld_stream_u32(k + o.row + 8), 0u);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            // 16 3-bit codes (6 bytes, 2-byte aligned) spread to the nibble
+            // layout of the 4-bit values (low nibble = even dim)
+            const uint8_t* vj = v + j * o.row;
+            const uint32_t a = ld_stream_u16(vj), b = ld_stream_u16(vj + 2), cc = ld_stream_u16(vj + 4);
+            r.v[j] = make_uint2(spread3to4((a | (b << 16)) & 0xFFFFFFu), spread3to4((b >> 8) | (cc << 8)));
+        }
+        r.kn = ld_stream_u32(m);
+        r.vs = ld_stream_u32(m + 2 * kBlockSize);
+        r.vz = ld_stream_u32(m + 4 * kBlockSize);
+    } else if (LAYOUT == TQB_LAYOUT_SOA_K3) {
         const uint8_t* k = base + o.k0;
         const uint8_t* v = base + o.v0;
         const uint8_t* m = base + o.meta;
@@ -302,7 +334,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // (byte << 8) | this lane's copy offset, in one PRMT
         uint32_t ia, ib, ic, id;
-        if (LAYOUT == TQB_LAYOUT_SOA_K3) {
+        if (LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3) {
             // 3-bit keys: the dim pairs 32c + 4ks + {0,1} and {2,3} are the
             // 6-bit fields at bits 12ks and 12ks + 6 of the lane's 96 bits;
             // entry (pair << 8) + this lane's copy offset, as below.
@@ -460,9 +492,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     // ---- centroid table -------------------------------------------------
     // (FP8 keys need no table: their fp16 form is exact, scale exponent 0.)
     // 3-bit keys: 8 centroids, table entries for the 64 6-bit dim pairs.
-    constexpr int kNc = LAYOUT == TQB_LAYOUT_SOA_K3 ? 8 : kNumCentroids;
-    constexpr int kPairs = LAYOUT == TQB_LAYOUT_SOA_K3 ? 64 : 256;
-    constexpr int kLowBits = LAYOUT == TQB_LAYOUT_SOA_K3 ? 3 : 4;
+    constexpr bool kKey3 = LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3;
+    constexpr int kNc = kKey3 ? 8 : kNumCentroids;
+    constexpr int kPairs = kKey3 ? 64 : 256;
+    constexpr int kLowBits = kKey3 ? 3 : 4;
     float cmax = 0.0f;
     if (LAYOUT != TQB_LAYOUT_SOA_K8) {
 #pragma unroll
@@ -709,6 +742,9 @@ int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     if (P.layout == TQB_LAYOUT_SOA_K3)
         return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K3>(P, stream, num_sms)
                         : launch_t<2, TQB_LAYOUT_SOA_K3>(P, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K3V3)
+        return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K3V3>(P, stream, num_sms)
+                        : launch_t<2, TQB_LAYOUT_SOA_K3V3>(P, stream, num_sms);
     const bool soa = P.layout == TQB_LAYOUT_SOA;
     if (P.G <= 4) return soa ? launch_t<1, TQB_LAYOUT_SOA>(P, stream, num_sms)
                              : launch_t<1, TQB_LAYOUT_AOS>(P, stream, num_sms);

@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     const float ys[4] = {yv.x, yv.y, yv.z, yv.w};
     // 3-bit keys: 8 centroids, 3 search steps (reference/soa_store.py:305-314
     // with MSE_BITS = 3)
-    const bool k3 = P.layout == TQB_LAYOUT_SOA_K3;
+    const bool k3 = P.layout == TQB_LAYOUT_SOA_K3 || P.layout == TQB_LAYOUT_SOA_K3V3;
     const int nc = k3 ? 8 : kNumCentroids, steps = k3 ? 3 : 4;
     int idx[4];
 #pragma unroll
@@ -109,15 +109,19 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
         vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
         vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
     }
-    float scale = __fdiv_rn(__fsub_rn(vmax, vmin), 15.0f);
+    // 3-bit values (reference/soa_store.py:49-84): 7 levels, codes packed
+    // little-endian at bit 3d; 4-bit: 15 levels, two codes per byte.
+    const bool v3 = P.layout == TQB_LAYOUT_SOA_K3V3;
+    const int vtop = v3 ? 7 : 15;
+    float scale = __fdiv_rn(__fsub_rn(vmax, vmin), v3 ? 7.0f : 15.0f);
     scale = scale > 1e-8f ? scale : 1e-8f;
     uint32_t vpack = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const float t = __fadd_rn(__fdiv_rn(__fsub_rn(vs[j], vmin), scale), 0.5f);
         int q = __float2int_rz(t);
-        q = q < 0 ? 0 : (q > 15 ? 15 : q);
-        vpack |= (uint32_t)q << (4 * j);
+        q = q < 0 ? 0 : (q > vtop ? vtop : q);
+        vpack |= (uint32_t)q << ((v3 ? 3 : 4) * j);
     }
 
     // -- write --
@@ -134,6 +138,26 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
                 base + (int64_t)kBlockSize * P.H * kK8DataBytes) + (int64_t)h * 2 * kBlockSize;
             meta[off] = sc_h;
             meta[kBlockSize + off] = zr_h;
+        }
+    } else if (v3) {
+        uint8_t* dp = base + off * ((int64_t)P.H * kK3V3DataBytes) + (int64_t)h * kK3V3DataBytes;
+        // keys and values: lanes 2m and 2m+1 hold dims 8m .. 8m+7, bytes
+        // 3m .. 3m+2 of each 48-byte stream
+        const uint32_t kup = __shfl_down_sync(0xffffffffu, kpack, 1);
+        const uint32_t vup = __shfl_down_sync(0xffffffffu, vpack, 1);
+        if ((lane & 1) == 0) {
+            const uint32_t k24 = kpack | (kup << 12), v24 = vpack | (vup << 12);
+            uint8_t* kb = dp + 3 * (lane >> 1);
+            uint8_t* vb = dp + kK3KeyBytes + 3 * (lane >> 1);
+            kb[0] = (uint8_t)k24; kb[1] = (uint8_t)(k24 >> 8); kb[2] = (uint8_t)(k24 >> 16);
+            vb[0] = (uint8_t)v24; vb[1] = (uint8_t)(v24 >> 8); vb[2] = (uint8_t)(v24 >> 16);
+        }
+        if (lane == 0) {
+            unsigned short* meta = reinterpret_cast<unsigned short*>(
+                base + (int64_t)kBlockSize * P.H * kK3V3DataBytes) + (int64_t)h * 3 * kBlockSize;
+            meta[off] = vn_h;
+            meta[kBlockSize + off] = sc_h;
+            meta[2 * kBlockSize + off] = zr_h;
         }
     } else if (P.layout == TQB_LAYOUT_SOA_K3) {
         uint8_t* dp = base + off * ((int64_t)P.H * kK3DataBytes) + (int64_t)h * kK3DataBytes;

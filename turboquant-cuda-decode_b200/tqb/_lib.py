@@ -26,6 +26,7 @@ TQB_LAYOUT_SOA = 0
 TQB_LAYOUT_AOS = 1
 TQB_LAYOUT_SOA_K8 = 2
 TQB_LAYOUT_SOA_K3 = 3
+TQB_LAYOUT_SOA_K3V3 = 4
 
 TQB_P2P_MAX_RANKS = 8
 TQB_IPC_HANDLE_BYTES = 64

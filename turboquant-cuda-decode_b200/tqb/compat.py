@@ -134,14 +134,25 @@ def triton_turboquant_decode_attention(
     ``key_fp8=True`` is the ``turboquant_k8v4`` preset: e4m3 keys, 4-bit
     values, the query used unrotated (reference/soa_decode_v1.py:532-533);
     ``mse_bits=3`` the ``turboquant_k3v4_nc`` preset (3-bit keys, 8
-    centroids)."""
-    if value_quant_bits != 4 or (not key_fp8 and mse_bits not in (3, 4)):
-        raise NotImplementedError("supported presets: turboquant_4bit_nc, turboquant_k3v4_nc (3-bit K, "
-                                  "4-bit V) and turboquant_k8v4 (FP8 keys, 4-bit V)")
-    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale,
-                            "soa_k8" if key_fp8 else ("soa_k3" if mse_bits == 3 else "soa"), PiT=PiT,
+    centroids), with ``value_quant_bits=3`` too ``turboquant_3bit_nc``."""
+    layout = _preset_layout(key_fp8, mse_bits, value_quant_bits)
+    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, PiT=PiT,
                             mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
                             max_num_kv_splits=max_num_kv_splits, sinks=sinks)
+
+
+def _preset_layout(key_fp8: bool, mse_bits: int, value_quant_bits: int) -> str:
+    """Cache layout of a TurboQuant preset (reference/config.py:20-41)."""
+    if key_fp8 and value_quant_bits == 4:
+        return "soa_k8"        # turboquant_k8v4
+    if not key_fp8 and mse_bits == 4 and value_quant_bits == 4:
+        return "soa"           # turboquant_4bit_nc
+    if not key_fp8 and mse_bits == 3 and value_quant_bits == 4:
+        return "soa_k3"        # turboquant_k3v4_nc
+    if not key_fp8 and mse_bits == 3 and value_quant_bits == 3:
+        return "soa_k3v3"      # turboquant_3bit_nc
+    raise NotImplementedError(f"no TurboQuant preset with key_fp8={key_fp8}, mse_bits={mse_bits}, "
+                              f"value_quant_bits={value_quant_bits}")
 
 
 def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, *, PiT=None,
@@ -221,11 +232,9 @@ def triton_turboquant_store(
     ``key_fp8=True`` (``turboquant_k8v4``) casts the raw key to e4m3 in the
     kernel, SoA layout with 196 bytes per token-head
     (reference/soa_store.py:446-479)."""
-    if value_quant_bits != 4 or (not key_fp8 and mse_bits not in (3, 4)):
-        raise NotImplementedError("supported presets: turboquant_4bit_nc, turboquant_k3v4_nc (3-bit K, "
-                                  "4-bit V) and turboquant_k8v4 (FP8 keys, 4-bit V)")
-    if mse_bits == 3 and not key_fp8:
-        layout = "soa_k3"  # the 3-bit preset's SoA cache (118 bytes per token-head)
+    preset = _preset_layout(key_fp8, mse_bits, value_quant_bits)
+    if preset != "soa":
+        layout = preset  # the other presets' caches are SoA only
     N, H, D = key.shape
     if key_fp8:
         ops.store(key.float().reshape(N * H, D).contiguous(), None, value.float().reshape(N * H, D).contiguous(),

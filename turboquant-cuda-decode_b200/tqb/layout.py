@@ -47,6 +47,9 @@ K8_SLOT_SIZE = HEAD_DIM + VAL_DATA_BYTES + 4  # 196
 LAYOUT_SOA_K3 = 3
 K3_KEY_BYTES = HEAD_DIM * 3 // 8
 K3_SLOT_SIZE = K3_KEY_BYTES + VAL_DATA_BYTES + 6  # 118
+# turboquant_3bit_nc: 3-bit keys and 3-bit values (48 + 48 B), same meta
+LAYOUT_SOA_K3V3 = 4
+K3V3_SLOT_SIZE = K3_KEY_BYTES + HEAD_DIM * 3 // 8 + 6  # 102
 
 
 def layout_id(layout) -> int:
@@ -58,7 +61,9 @@ def layout_id(layout) -> int:
         return LAYOUT_SOA_K8
     if layout in (LAYOUT_SOA_K3, "soa_k3", "k3v4"):
         return LAYOUT_SOA_K3
-    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos', 'soa_k8' or 'soa_k3')")
+    if layout in (LAYOUT_SOA_K3V3, "soa_k3v3", "3bit"):
+        return LAYOUT_SOA_K3V3
+    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos', 'soa_k8', 'soa_k3' or 'soa_k3v3')")
 
 
 def block_bytes(num_kv_heads: int, block_size: int = BLOCK_SIZE) -> int:

@@ -17,7 +17,10 @@ import torch
 
 from . import _lib
 from ._lib import MergeArgs, RotateArgs, SinkArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
-from .layout import BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, LAYOUT_SOA_K3, LAYOUT_SOA_K8, layout_id
+from .layout import (BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3, LAYOUT_SOA_K8,
+                     layout_id)
+
+_SOA_FAMILY = (LAYOUT_SOA, LAYOUT_SOA_K8, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3)  # block-as-raw-bytes layouts
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -92,7 +95,7 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     _require(tuple(mid_o.shape[:2]) == (B, Hq) and mid_o.shape[3] == D + 1,
              f"mid_o shape {tuple(mid_o.shape)} does not match q_rot {tuple(q_rot.shape)}")
     _require(block_table.shape[0] == B and seq_lens.shape[0] == B, "batch mismatch")
-    if lay in (LAYOUT_SOA, LAYOUT_SOA_K8, LAYOUT_SOA_K3):
+    if lay in _SOA_FAMILY:
         _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
     devs = {t.device for t in (q_rot, kv_cache, block_table, seq_lens, centroids, mid_o) if t is not None}
     _require(len(devs) == 1, f"all tensors must be on one device, got {devs}")
@@ -275,7 +278,7 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
              "y/value must be [N*H, 128] and norms [N*H]")
     if k8:
         _require(not norm_correction, "FP8 keys have no norm correction")
-    if lay in (LAYOUT_SOA, LAYOUT_SOA_K8, LAYOUT_SOA_K3):
+    if lay in _SOA_FAMILY:
         _require(_block_dense(kv_cache), "SoA cache needs each block's bytes contiguous")
     if norm_correction:
         _require(centroids is not None, "norm_correction=True requires centroids")
@@ -293,7 +296,7 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
         kv_cache.stride(0), kv_cache.stride(1), kv_cache.stride(2))
     a.num_blocks = nb
     a.num_tokens, a.num_kv_heads, a.head_dim, a.block_size = N, H, HEAD_DIM, bs
-    a.n_centroids = 8 if lay == LAYOUT_SOA_K3 else 16
-    a.norm_correction = int(bool(norm_correction)) if lay in (LAYOUT_SOA, LAYOUT_SOA_K3) else 0
+    a.n_centroids = 8 if lay in (LAYOUT_SOA_K3, LAYOUT_SOA_K3V3) else 16
+    a.norm_correction = int(bool(norm_correction)) if lay in (LAYOUT_SOA, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3) else 0
     with torch.cuda.device(kv_cache.device):
         _lib.check(_lib.load().tqb_store(a, stream if stream is not None else _stream(kv_cache.device)))
