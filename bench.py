@@ -66,9 +66,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
-    ap.add_argument("--layout", choices=["soa", "aos", "soa_k8", "soa_k3"], default="soa",
+    ap.add_argument("--layout", choices=["soa", "aos", "soa_k8", "soa_k3", "soa_k3v3"], default="soa",
                     help="cache layout; soa_k8 = the turboquant_k8v4 preset (FP8 keys, 4-bit values), "
-                         "soa_k3 = turboquant_k3v4_nc (3-bit keys, 4-bit values); both c1 only")
+                         "soa_k3 = turboquant_k3v4_nc (3-bit keys, 4-bit values), soa_k3v3 = "
+                         "turboquant_3bit_nc (3-bit keys and values); these three c1 only")
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
@@ -142,11 +143,11 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
     R = orthogonal(seed + 1).to(dev)
     perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
     bt = perm.reshape(B, pages).to(dev)
-    k8, k3 = layout == "soa_k8", layout == "soa_k3"
+    k8, k3, v3 = layout == "soa_k8", layout in ("soa_k3", "soa_k3v3"), layout == "soa_k3v3"
     if k3:  # 3-bit keys: 8 centroids
         cents = tqb.get_centroids(128, 3).to(dev)
         mids = tqb.get_midpoints(cents)
-    slot = L.K8_SLOT_SIZE if k8 else (L.K3_SLOT_SIZE if k3 else L.SLOT_SIZE)
+    slot = L.K8_SLOT_SIZE if k8 else (L.K3V3_SLOT_SIZE if v3 else L.K3_SLOT_SIZE if k3 else L.SLOT_SIZE)
     kv = torch.zeros(nblk, L.BLOCK_SIZE, Hk, slot, dtype=torch.uint8, device=dev)
     chunk = 8192
     tok_b = torch.arange(Lc, device=dev)
@@ -161,8 +162,8 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
                                             key_fp8=True)
             else:
                 tqb.triton_turboquant_store(key, val, kv, slots_b[s0:s0 + n], R, mids, 3 if k3 else 4,
-                                            50 if k3 else 66, 4, centroids=cents,
-                                            norm_correction=(layout in ("soa", "soa_k3")), layout=layout)
+                                            50 if k3 else 66, 3 if v3 else 4, centroids=cents,
+                                            norm_correction=(layout != "aos"), layout=layout)
     query = torch.randn(B, Hq, 128, generator=gen, device=dev).to(torch.bfloat16)
     # FP8 keys score against the unrotated query
     q_rot = query.float().contiguous() if k8 else (query.float() @ R).contiguous()
@@ -177,7 +178,7 @@ def algorithmic_bytes(w) -> int:
     196 B with FP8 keys), the fp32 query, the block-table entries used,
     seq_lens, the centroid table, and the fp32 mid_o write."""
     B, Hq, Hk, S, Lc = w["B"], w["Hq"], w["Hk"], w["S"], w["L"]
-    cache = B * Lc * Hk * {"soa_k8": 196, "soa_k3": 118}.get(w["layout"], 134)
+    cache = B * Lc * Hk * {"soa_k8": 196, "soa_k3": 118, "soa_k3v3": 102}.get(w["layout"], 134)
     q = B * Hq * 128 * 4
     bt = B * math.ceil(Lc / 16) * 4
     mid = B * Hq * S * 129 * 4
@@ -358,7 +359,7 @@ def run_reference(args, world, rank):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm runs the c1 headline config only"}),
               flush=True)
         return
-    if args.layout in ("soa_k8", "soa_k3"):
+    if args.layout in ("soa_k8", "soa_k3", "soa_k3v3"):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm restates the 4-bit key presets only"}),
               flush=True)
         return
@@ -554,8 +555,8 @@ def main():
     args = parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
-    if args.layout in ("soa_k8", "soa_k3") and args.config != "c1":
-        raise SystemExit("--layout soa_k8 / soa_k3 run the single-GPU c1 workload only")
+    if args.layout in ("soa_k8", "soa_k3", "soa_k3v3") and args.config != "c1":
+        raise SystemExit("--layout soa_k8 / soa_k3 / soa_k3v3 run the single-GPU c1 workload only")
     if args.impl == "ours" and args.config != "c1":
         run_sharded(args, world, rank, local)
         if world > 1:
@@ -667,7 +668,9 @@ def main():
             dbuf.copy_(hbuf, non_blocking=True)
             o = tqb.triton_turboquant_decode_attention(
                 dq, w["kv"], dbt, dsl, w["R"].T, w["cents"], 1.0 / math.sqrt(128),
-                {"soa_k8": 8, "soa_k3": 3}.get(args.layout, 4), {"soa_k8": 128, "soa_k3": 50}.get(args.layout, 66), 4,
+                {"soa_k8": 8, "soa_k3": 3, "soa_k3v3": 3}.get(args.layout, 4),
+                {"soa_k8": 128, "soa_k3": 50, "soa_k3v3": 50}.get(args.layout, 66),
+                3 if args.layout == "soa_k3v3" else 4,
                 key_fp8=args.layout == "soa_k8", norm_correction=args.layout != "soa_k8", PiT=w["R"],
                 mid_o_buf=mbuf, output_buf=obuf, lse_buf=lbuf, max_num_kv_splits=S)
             hout.copy_(o, non_blocking=True)
@@ -716,7 +719,8 @@ def main():
         "vs_baseline": None,
         "dtype": ("f32 (e4m3 K, 4-bit V codes, fp16 tensor-core MMA, fp32 accumulate)" if args.layout == "soa_k8"
                   else "f32 (3-bit K / 4-bit V codes, fp16-split tensor-core MMA, fp32 accumulate)"
-                  if args.layout == "soa_k3"
+                  if args.layout == "soa_k3" else "f32 (3-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"
+                  if args.layout == "soa_k3v3"
                   else "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"),
         "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
         "config": {"workload": cfg["workload"], "layout": args.layout,
@@ -735,12 +739,13 @@ def main():
                      "kernel": ("tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)" if args.layout == "soa"
                                 else "tqb stage1_kernel (register page ring, FP8 keys)" if args.layout == "soa_k8"
                                 else "tqb stage1_kernel (register page ring, 3-bit keys)" if args.layout == "soa_k3"
+                                else "tqb stage1_kernel (register page ring, 3-bit keys and values)" if args.layout == "soa_k3v3"
                                 else "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)")},
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
-    if not args.no_cpu_baseline and world == 1 and args.layout not in ("soa_k8", "soa_k3"):
+    if not args.no_cpu_baseline and world == 1 and args.layout not in ("soa_k8", "soa_k3", "soa_k3v3"):
         # the C restatement covers the 4-bit keys only
         line["cpu_baseline"] = cpu_baseline(w)
     print(json.dumps(line), flush=True)
