@@ -289,6 +289,41 @@ def ncu_traffic(config: str, layout: str):
 # ---------------------------------------------------------------------------
 
 
+def measure_store(w, dev, peak: float, reps: int = 20) -> dict:
+    """The sm_100a store (4-bit SoA, norm correction) on a prefill-sized
+    batch: 32768 tokens x Hk heads of rotated unit keys, norms and values,
+    scattered into a shuffled block pool; 305 MB of fp32 inputs at Hk = 8,
+    larger than the 126 MB L2.  CUDA events around `reps` launches after 3
+    warm-up launches; bytes = the fp32 y / value / norm reads, the slot
+    index, and the 134-byte slot written per token-head."""
+    import tqb
+
+    N, H = 32768, w["Hk"]
+    gen = torch.Generator(device=dev).manual_seed(7)
+    y = torch.nn.functional.normalize(torch.randn(N * H, 128, device=dev, generator=gen), dim=1)
+    norms = torch.rand(N * H, device=dev, generator=gen) * 10 + 1
+    val = torch.randn(N * H, 128, device=dev, generator=gen)
+    cache = torch.zeros(N // 16, 16, H, 134, dtype=torch.uint8, device=dev)
+    slots = torch.randperm(N, device=dev, generator=gen).to(torch.int32)
+    mids = tqb.get_midpoints(w["cents"])
+    for _ in range(3):
+        tqb.store(y, norms, val, cache, slots, mids, w["cents"])
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(reps):
+        tqb.store(y, norms, val, cache, slots, mids, w["cents"])
+    b.record()
+    torch.cuda.synchronize(dev)
+    us = a.elapsed_time(b) / reps * 1e3
+    per_th = 128 * 4 * 2 + 4 + 134
+    alg = N * H * per_th + N * 4
+    return {"token_heads": N * H, "us_per_launch": us, "token_heads_per_s": N * H / (us * 1e-6),
+            "algorithmic_bytes_per_launch": alg, "bytes_per_token_head": per_th,
+            "achieved_gbs": alg / (us * 1e-6) / 1e9, "frac_of_peak": alg / (us * 1e-6) / 1e9 / peak,
+            "kernel": "tqb store_kernel (warp per token-head, 4-bit SoA with norm correction)"}
+
+
 def cpu_baseline(w, min_seconds=10.0):
     from oracle import oracle as O
 
@@ -745,6 +780,8 @@ def main():
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
+    if args.layout == "soa":
+        line["store"] = measure_store(w, dev, peak)
     if not args.no_cpu_baseline and world == 1 and args.layout not in ("soa_k8", "soa_k3", "soa_k3v3"):
         # the C restatement covers the 4-bit keys only
         line["cpu_baseline"] = cpu_baseline(w)
