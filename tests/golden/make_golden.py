@@ -17,6 +17,16 @@ Reference kernels exercised (paths relative to the reference checkout):
 * V2-fixed       ``baseline/triton_v2.py:58-561`` (fp16 tensor-core baseline)
 * Stage2 merge   ``baseline/stage2.py:8-55``
 * Codebook       ``reference/centroids.py:31-86``
+* Other presets  FP8 keys (``_tq_fused_store_fp8``, ``reference/soa_store.py:
+  125-221``; SoA Stage1 with ``KEY_FP8=1``), 3-bit keys with 4-bit or 3-bit
+  values (the MSE store with ``MSE_BITS=3`` / ``VQB=3``, ``:223-373``, and
+  the SoA Stage1 with those constexprs), attention sinks (SoA Stage1 with
+  ``USE_SINKS=1``, ``reference/soa_decode_v1.py:134-145``)
+
+Note on FP8: the interpreter's float -> e4m3 cast rounds ties up, flushes
+subnormals and wraps on overflow, unlike the hardware cast the compiled
+reference uses on sm_90+, so the FP8 fixture's key bytes pin nothing; its
+value bytes, meta and Stage1 output (decoding is exact) are used.
 
 The kernels are launched through the raw ``kernel[grid](...)`` form with each
 fixture's constexprs, because the harness launchers assert the fixed
