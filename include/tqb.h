@@ -211,6 +211,11 @@ int tqb_merge_partials(const tqb_merge_args* args, cudaStream_t stream);
  * fp32 [N*H, D].  Bucketising, packing, norm folding (SoA,
  * norm_correction=1) and value quantisation are bit-exact with the
  * reference arithmetic.  Negative slot_mapping entries are skipped.
+ * Other presets: TQB_LAYOUT_SOA_K3 / _K3V3 take the same inputs with 8
+ * centroids and 7 midpoints (3-bit keys; _K3V3 also quantises values to 7
+ * levels); TQB_LAYOUT_SOA_K8 takes the raw keys in y, cast to e4m3 (round to
+ * nearest even, saturating at +-448, reference/soa_store.py:125-221), with
+ * norms, midpoints and centroids unused (may be NULL) and no norm correction.
  */
 typedef struct tqb_store_args {
     const float* y;              /* [N*H, D] */
@@ -227,7 +232,7 @@ typedef struct tqb_store_args {
     int32_t num_kv_heads;        /* H */
     int32_t head_dim;            /* 128 */
     int32_t block_size;          /* 16 */
-    int32_t n_centroids;         /* 16 */
+    int32_t n_centroids;         /* 16 (8 for the 3-bit-key layouts; ignored for K8) */
     int32_t norm_correction;     /* SoA: fold 1/|c| into the stored norm */
 } tqb_store_args;
 

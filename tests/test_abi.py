@@ -97,6 +97,25 @@ def test_argument_validation_without_launch(lib):
     s = _lib.StoreArgs()
     s.num_tokens, s.num_kv_heads, s.head_dim, s.block_size, s.n_centroids = 1, 8, 128, 16, 8
     assert lib.tqb_store(ctypes.byref(s), None) == _lib.TQB_ERR_UNSUPPORTED
+    # The preset layouts: 3-bit keys need 8 centroids; FP8 keys none; an
+    # unknown layout is rejected; the FP8-key store has no norm correction.
+    a = _lib.Stage1Args()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.num_splits = 1, 32, 8, 4
+    a.head_dim, a.block_size, a.n_centroids = 128, 16, 16
+    for lay in (_lib.TQB_LAYOUT_SOA_K3, _lib.TQB_LAYOUT_SOA_K3V3):
+        a.layout = lay
+        assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_UNSUPPORTED
+        assert b"n_centroids" in lib.tqb_last_error_detail()
+    a.layout, a.n_centroids = _lib.TQB_LAYOUT_SOA_K8, 0
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG  # NULL pointers, not centroids
+    assert b"NULL" in lib.tqb_last_error_detail()
+    a.layout, a.n_centroids = 9, 16
+    assert lib.tqb_stage1(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    s = _lib.StoreArgs()
+    s.num_tokens, s.num_kv_heads, s.head_dim, s.block_size, s.n_centroids = 1, 8, 128, 16, 16
+    s.layout, s.norm_correction = _lib.TQB_LAYOUT_SOA_K8, 1
+    assert lib.tqb_store(ctypes.byref(s), None) == _lib.TQB_ERR_INVALID_ARG
+    assert b"norm correction" in lib.tqb_last_error_detail()
     # Empty batches are valid no-ops.
     a = _lib.Stage1Args()
     a.batch, a.num_q_heads, a.num_kv_heads, a.num_splits = 0, 32, 8, 32
