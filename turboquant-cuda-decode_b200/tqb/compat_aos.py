@@ -44,7 +44,8 @@ def triton_turboquant_decode_attention(
     """Decode over an AoS cache ``[num_blocks, 16, Hk, 134]``; returns
     ``[B, Hq, D]`` in the query's dtype."""
     if key_fp8 or mse_bits != 4 or value_quant_bits != 4:
-        raise NotImplementedError("only the turboquant_4bit_nc preset (4-bit K and V) is supported")
+        raise NotImplementedError("the AoS cache serves the turboquant_4bit_nc preset; the FP8-key and 3-bit "
+                                  "presets use the SoA cache (tqb.compat.triton_turboquant_decode_attention)")
     if not norm_correction:
         raise NotImplementedError("the AoS kernels implement the norm-corrected decode (norm_correction=True) "
                                   "of the turboquant_4bit_nc preset")
