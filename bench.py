@@ -16,6 +16,22 @@ the data path).
 
 ``--impl reference`` times the reference algorithm on the host CPU (the
 fp32 C restatement in ``oracle/``, all host threads) on the same workload.
+
+At N=1 the c1 line also carries, from the same process:
+
+* ``parity``: this library's Stage1 partials and Stage2 output/LSE of the
+  timed workload against the CPU oracle (the same inputs, the full c1
+  workload), with the decode bar |got - ref| <= 1e-4 + 2e-3 |ref|;
+* ``reference_gpu``: the reference's own Stage1 kernels (Triton AoS V1, SoA
+  V1 and V2-fixed, CUDA V9 and V7 built for sm_100a) on the same B200 and
+  the same inputs, loaded from the reference checkout that
+  ``baseline/install_ref.py`` places under ``baseline/_ref/``, timed with the
+  reference's protocol (``benchmarks/stage1.py:32-43,508-527``: 20 warm-up
+  launches, 100 timed, 5 rounds in rotated order, median) beside this
+  library's Stage1, and checked against the reference SoA V1 output;
+* ``reference_interpreter``: the reference SoA V1 and V2-fixed Stage1 under
+  ``TRITON_INTERPRET=1`` on the host CPU, a bounded subset of the c1 grid,
+  with the per-program rate and the full-grid time extrapolated from it.
 """
 
 from __future__ import annotations
@@ -75,6 +91,11 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--splits", type=int, default=None,
                     help="override the config's (local) KV split count")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own kernels on the GPU")
+    ap.add_argument("--no-interpreter", action="store_true",
+                    help="skip the reference-under-TRITON_INTERPRET CPU sample")
+    ap.add_argument("--interp-child", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.splits is not None:
         CONFIGS[args.config] = dict(CONFIGS[args.config], S=args.splits)
@@ -171,6 +192,14 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
     torch.cuda.synchronize(dev)
     return dict(kv=kv, bt=bt, seq_lens=seq_lens, cents=cents, R=R, query=query, q_rot=q_rot,
                 B=B, Hq=Hq, Hk=Hk, S=S, L=Lc, layout=layout)
+
+
+def c1_config(cfg: dict, layout: str, B: int, L: int, S: int, world: int, cache_mb: float) -> dict:
+    """The `config` object of the c1 line; the reference arm prints the same."""
+    return {"workload": cfg["workload"], "layout": layout,
+            "per_gpu_batch": B, "global_batch": world * B, "seq_len": L,
+            "num_splits": S, "parallelism": f"dp{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (cache %.0f MB per GPU vs 126 MB L2); no flush" % cache_mb}
 
 
 def algorithmic_bytes(w) -> int:
@@ -325,6 +354,10 @@ def measure_store(w, dev, peak: float, reps: int = 20) -> dict:
 
 
 def cpu_baseline(w, min_seconds=10.0):
+    """The C restatement of the reference Stage1 + Stage2 on the host cores,
+    repeated over the full workload for about ``min_seconds``.  Returns the
+    baseline record and the last repetition's (mid_o, output, lse), which
+    the parity check compares with the GPU results."""
     from oracle import oracle as O
 
     cores = O.default_threads()
@@ -338,15 +371,239 @@ def cpu_baseline(w, min_seconds=10.0):
     t0 = time.perf_counter()
     while True:
         mid = O.stage1(q, kv, bt, sl, cents, w["S"], layout=lay, nthreads=cores)
-        O.stage2(mid, sl, nthreads=cores)
+        out, lse = O.stage2(mid, sl, nthreads=cores)
         reps += 1
         if time.perf_counter() - t0 >= min_seconds:
             break
     dt = (time.perf_counter() - t0) / reps
-    return {"value": w["B"] / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"full B{w['B']} x {w['L']} workload, Stage1+Stage2, fp32 C restatement "
-                      f"of reference/soa_decode_v1.py + baseline/stage2.py, {reps} rep(s), "
-                      f"{dt * 1e3:.1f} ms each"}
+    rec = {"value": w["B"] / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+           "sample": f"full B{w['B']} x {w['L']} workload, Stage1+Stage2, fp32 C restatement "
+                     f"of reference/soa_decode_v1.py + baseline/stage2.py, {reps} rep(s), "
+                     f"{dt * 1e3:.1f} ms each"}
+    return rec, (mid, out, lse)
+
+
+PARITY_ATOL, PARITY_RTOL = 1e-4, 2e-3  # the decode bar: |got - ref| <= 1e-4 + 2e-3 |ref|
+
+
+def _compare(got: np.ndarray, ref: np.ndarray) -> dict:
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    both_nan = np.isnan(got) & np.isnan(ref)
+    err = np.where(both_nan, 0.0, np.abs(got - ref))
+    bad = ~(err <= PARITY_ATOL + PARITY_RTOL * np.abs(ref))
+    return {"max_abs": float(np.nanmax(err)) if err.size else 0.0, "n_bad": int(bad.sum()), "n": int(got.size)}
+
+
+def parity_vs_oracle(mid, out, lse, oracle_res) -> dict:
+    """This library's results of the timed workload against the oracle's,
+    element by element, with the decode bar."""
+    rmid, rout, rlse = oracle_res
+    gmid = mid.cpu().numpy()
+    res = {"bar": f"|got - ref| <= {PARITY_ATOL} + {PARITY_RTOL}|ref|",
+           "against": "CPU oracle (C restatement of the reference Stage1/Stage2), same inputs, full workload",
+           "stage1_o": _compare(gmid[..., :128], rmid[..., :128]),
+           "stage1_lse": _compare(gmid[..., 128], rmid[..., 128]),
+           "stage2_output": _compare(out.cpu().numpy(), rout),
+           "stage2_lse": _compare(lse.cpu().numpy(), rlse)}
+    res["n_bad"] = sum(v["n_bad"] for v in res.values() if isinstance(v, dict))
+    res["max_abs"] = max(v["max_abs"] for v in res.values() if isinstance(v, dict))
+    return res
+
+
+# ---------------------------------------------------------------------------
+# The reference's own kernels on the same GPU (from baseline/_ref)
+# ---------------------------------------------------------------------------
+
+REF_CHECKOUT = ROOT / "baseline" / "_ref" / "turboquant-cuda-decode"
+REF_NATIVE = {"CUDA V9": ("tq4_cuda_v9_ext", ROOT / "baseline" / "_ref" / "build_v9", "tq4_cuda_v9"),
+              "CUDA V7": ("tq4_cuda_v7_ext", ROOT / "baseline" / "_ref" / "build_v7", "tq4_cuda_v7_stage1")}
+
+
+def _reference_harness():
+    """The reference's harness modules (baseline/triton_v1.py, triton_v2.py,
+    common.py), imported from the checkout copy under baseline/_ref with the
+    harness's own vLLM import stubs.  Raises FileNotFoundError without it."""
+    import importlib
+
+    if not (REF_CHECKOUT / "baseline" / "triton_v1.py").is_file():
+        raise FileNotFoundError("no reference checkout under baseline/_ref (baseline/install_ref.py places it)")
+    if str(REF_CHECKOUT) not in sys.path:
+        sys.path.insert(0, str(REF_CHECKOUT))
+    tv1 = importlib.import_module("baseline.triton_v1")
+    tv2 = importlib.import_module("baseline.triton_v2")
+    common = importlib.import_module("baseline.common")
+    return tv1, tv2, common
+
+
+def _reference_native(label: str):
+    import importlib.machinery
+    import importlib.util
+
+    mod, folder, fn = REF_NATIVE[label]
+    so = sorted(folder.glob(f"{mod}*.so"))
+    if not so:
+        raise FileNotFoundError(f"{label}: no {mod}*.so under baseline/_ref (baseline/install_ref.py builds it)")
+    loader = importlib.machinery.ExtensionFileLoader(mod, str(so[0]))
+    spec = importlib.util.spec_from_file_location(mod, str(so[0]), loader=loader)
+    m = importlib.util.module_from_spec(spec)
+    loader.exec_module(m)
+    return getattr(m, fn)
+
+
+def _event_time_ms(fn, warmup: int, iters: int) -> float:
+    """benchmarks/stage1.py:32-43: warm-up launches, then `iters` launches
+    between two events, mean per launch."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def reference_gpu(w, dev, ours: dict, warmup=20, iters=100, rounds=5) -> dict:
+    """Time the reference's Stage1 kernels and this library's Stage1 on the
+    same inputs with the reference's protocol (benchmarks/stage1.py:508-527:
+    every round times each runner in a rotated order; the median over
+    rounds is reported), and check each against the reference SoA V1.
+    ``ours`` maps a label to (launch function, the mid_o it writes)."""
+    tv1, tv2, common = _reference_harness()
+    q, kv, bt, sl, cents = w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"]
+    B, Hq, S = w["B"], w["Hq"], w["S"]
+    pair_lut = common.build_pair_lut(cents)
+    aos = common.convert_soa_to_aos_kv_cache(kv, cents)
+    outs = {}
+
+    def buf():
+        return torch.full((B, Hq, S, 129), float("nan"), device=dev)
+
+    runners = []
+
+    def add(label, fn):
+        outs[label] = buf()
+        runners.append((label, fn))
+
+    add("AoS Triton V1", lambda: tv1.launch_aos_v1_stage1(q, aos, bt, sl, cents, outs["AoS Triton V1"]))
+    add("SoA Triton V1", lambda: tv1.launch_soa_v1_stage1(q, kv, bt, sl, cents, outs["SoA Triton V1"]))
+    add("SoA Triton V2-fixed",
+        lambda: tv2.launch_tq4_v2_stage1(q, kv, bt, sl, cents, pair_lut, outs["SoA Triton V2-fixed"]))
+    unavailable = {}
+    for label in REF_NATIVE:
+        try:
+            fn = _reference_native(label)
+        except Exception as e:  # recorded, not fatal: the Triton kernels still run
+            unavailable[label] = str(e).splitlines()[0][:300]
+            continue
+        add(label, (lambda f, lab: (lambda: f(q, kv, bt, sl, cents, outs[lab])))(fn, label))
+    for label, (fn, out) in ours.items():  # this library: a launcher and the buffer it writes
+        outs[label] = out
+        runners.append((label, fn))
+    for _, fn in runners:  # compile / load and produce the outputs
+        fn()
+    torch.cuda.synchronize(dev)
+    ref = outs["SoA Triton V1"]
+    parity = {}
+    for label, o in outs.items():
+        if label == "SoA Triton V1":
+            continue
+        d_o = (o[..., :128] - ref[..., :128]).abs()
+        d_l = (o[..., 128] - ref[..., 128]).abs()
+        within = (o - ref).abs() <= PARITY_ATOL + PARITY_RTOL * ref.abs()
+        parity[label] = {"output_max_abs": float(d_o.max()), "output_mean_abs": float(d_o.mean()),
+                         "lse_max_abs": float(d_l.max()), "lse_mean_abs": float(d_l.mean()),
+                         "n_bad": int((~within).sum()), "finite": bool(torch.isfinite(o).all())}
+    samples = {label: [] for label, _ in runners}
+    for r in range(rounds):
+        k = r % len(runners)
+        for label, fn in runners[k:] + runners[:k]:
+            samples[label].append(_event_time_ms(fn, warmup, iters))
+    med = {label: statistics.median(v) * 1e3 for label, v in samples.items()}
+    v2 = med["SoA Triton V2-fixed"]
+    res = {"protocol": f"benchmarks/stage1.py: {warmup} warm-up + {iters} timed launches per runner, "
+                       f"{rounds} rounds in rotated order, median; no L2 flush (cache 281 MB > 126 MB L2)",
+           "source": "unmodified reference checkout under baseline/_ref (Triton kernels through the "
+                     "reference harness launchers; CUDA V9/V7 built from cuda/*.cu for sm_100a)",
+           "median_us": med, "rounds_us": {k: [x * 1e3 for x in v] for k, v in samples.items()},
+           "speedup_vs_v2_fixed": {label: v2 / t for label, t in med.items()},
+           "parity_vs_soa_v1": parity}
+    if unavailable:
+        res["unavailable"] = unavailable
+    del aos
+    return res
+
+
+def interpreter_sample(w, timeout_s: int = 240) -> dict:
+    """Run the reference SoA V1 and V2-fixed Stage1 under TRITON_INTERPRET=1
+    on the host CPU, in a child process (the interpreter is chosen when the
+    kernels are defined), over a bounded subset of the c1 grid."""
+    import subprocess
+    import tempfile
+
+    try:
+        _reference_harness_path_ok = (REF_CHECKOUT / "baseline" / "triton_v1.py").is_file()
+        if not _reference_harness_path_ok:
+            return {"unavailable": "no reference checkout under baseline/_ref"}
+        with tempfile.TemporaryDirectory() as td:
+            np.savez(Path(td) / "w.npz", q=w["q_rot"].cpu().numpy(), kv=w["kv"].cpu().numpy(),
+                     bt=w["bt"].cpu().numpy(), sl=w["seq_lens"].cpu().numpy(), cents=w["cents"].cpu().numpy())
+            env = dict(os.environ, TRITON_INTERPRET="1", CUDA_VISIBLE_DEVICES="")
+            res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--interp-child", td], env=env,
+                                 capture_output=True, text=True, timeout=timeout_s)
+            lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+            if res.returncode != 0 or not lines:
+                return {"unavailable": f"interpreter child rc={res.returncode}: "
+                                       f"{(res.stderr or res.stdout).strip().splitlines()[-1:]}"}
+            return json.loads(lines[-1])
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def _interp_child(folder: str) -> None:
+    """Child of interpreter_sample: the reference launchers with the grid cut
+    to a prefix of batch row 0 (the same programs the full launch runs for
+    that row; every c1 program covers 128 tokens of one sequence)."""
+    tv1, tv2, common = _reference_harness()
+    with np.load(Path(folder) / "w.npz") as z:
+        q, kv, bt, sl, cents = (torch.from_numpy(z[k]) for k in ("q", "kv", "bt", "sl", "cents"))
+    B, Hq, _ = q.shape
+    Hk, S = kv.shape[2], 32
+    pair_lut = common.build_pair_lut(cents)
+    mid = torch.full((B, Hq, S, 129), float("nan"))
+
+    class Prefix:  # kernel[grid] with the grid replaced by a prefix of it
+        def __init__(self, kern, grid):
+            self.kern, self.grid = kern, grid
+
+        def __getitem__(self, grid):
+            return self.kern[self.grid]
+
+    out = {"cores": os.cpu_count(), "threads_used": 1,
+           "note": "Triton interpreter (numpy, one thread); full-grid times are EXTRAPOLATED from the subset's "
+                   "per-program rate; c1 Stage1 programs all cover 128 tokens"}
+    for label, mod, attr, sub, full, call in (
+        ("SoA Triton V1", tv1, "_soa_stage1", (1, 1, S), B * Hq * S,
+         lambda: tv1.launch_soa_v1_stage1(q, kv, bt, sl, cents, mid)),
+        ("SoA Triton V2-fixed", tv2, "tq4_decode_stage1_v2", (1, 2, S), B * Hk * S,
+         lambda: tv2.launch_tq4_v2_stage1(q, kv, bt, sl, cents, pair_lut, mid)),
+    ):
+        real = getattr(mod, attr)
+        setattr(mod, attr, Prefix(real, (1, 1, 1)))
+        call()  # first call: interpreter set-up, not timed
+        setattr(mod, attr, Prefix(real, sub))
+        t0 = time.perf_counter()
+        call()
+        dt = time.perf_counter() - t0
+        setattr(mod, attr, real)
+        n = sub[0] * sub[1] * sub[2]
+        out[label] = {"grid_subset": list(sub), "programs": n, "seconds": dt, "s_per_program": dt / n,
+                      "full_grid_programs": full, "extrapolated_stage1_s": dt / n * full,
+                      "extrapolated_tok_per_s": B / (dt / n * full)}
+    print(json.dumps(out), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -410,25 +667,31 @@ def run_reference(args, world, rank):
                        nthreads=cores)
         O.stage2(mid, w["seq_lens"], nthreads=cores)
 
-    step()  # one warm-up pass (a CPU has no JIT or clock ramp to hide)
-    steps = max(1, min(args.steps, 10))
+    for _ in range(args.warmup):  # the same untimed warm-up count as the GPU arm
+        step()
+    steps = args.steps
     t0 = time.perf_counter()
     for _ in range(steps):
         step()
     dt = (time.perf_counter() - t0) / steps
+    # One host runs this arm whatever N is: its rate is per host, and the
+    # whole-job value at N GPUs is that same host's rate.
     value = w["B"] / dt
     line = {
         "impl": "reference", "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s",
-        "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": dt * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg["workload"], "layout": args.layout, "per_gpu_batch": w["B"],
-                   "seq_len": w["L"], "num_splits": w["S"]},
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) K/V written by the oracle store, seeded rotation)",
+        "config": c1_config(cfg, args.layout, w["B"], w["L"], w["S"], world, w["kv"].nbytes / 1e6),
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"the full B{w['B']} x {w['L']} workload per step, {steps} step(s) "
-                                   f"(capped at 10), fp32 C restatement of the reference Stage1+Stage2, "
+                         "sample": f"the full B{w['B']} x {w['L']} workload per step, {steps} step(s) after "
+                                   f"{args.warmup} warm-up, fp32 C restatement of the reference Stage1+Stage2, "
                                    f"{cores} threads"},
     }
+    if world > 1:
+        line["note"] = (f"CPU arm: rank 0's host alone runs it (one host, {cores} threads); its value is the "
+                        "per-host rate, not scaled by the {world} GPUs of the job").replace("{world}", str(world))
     print(json.dumps(line), flush=True)
 
 
@@ -588,6 +851,9 @@ def run_sharded(args, world, rank, local):
 
 def main():
     args = parse_args()
+    if args.interp_child:
+        _interp_child(args.interp_child)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
     if args.layout in ("soa_k8", "soa_k3", "soa_k3v3") and args.config != "c1":
@@ -671,7 +937,28 @@ def main():
     s1_avg_ms = max_over_ranks(a1.elapsed_time(b1) / K, world)
     ms_per_step = total_ms / K
     value = world * B / (ms_per_step * 1e-3)
-    del g_step, g_s1
+    del g_step
+
+    # -- the reference's own kernels on this GPU, same inputs, its protocol --
+    ref_gpu = None
+    single_c1 = world == 1 and args.config == "c1"
+    if single_c1 and args.layout == "soa" and not args.no_reference_gpu:
+        mid_eager = torch.empty_like(mid)
+        ours = {"tqb (graph replay)": (g_s1.replay, mid),
+                "tqb (compat.launch_soa_v1_stage1)":
+                    ((lambda: tqb.compat.launch_soa_v1_stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"],
+                                                              w["cents"], mid_eager)), mid_eager)}
+        try:
+            ref_gpu = reference_gpu(w, dev, ours)
+        except Exception as e:  # the reference not placed, or its kernels refused: say so in the line
+            ref_gpu = {"unavailable": f"{type(e).__name__}: {e}"[:400]}
+        del mid_eager
+        torch.cuda.synchronize(dev)
+    del g_s1
+    # the timed step's results, for the parity check against the oracle
+    tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, layout=args.layout)
+    tqb.stage2(mid, w["seq_lens"], out, lse)
+    torch.cuda.synchronize(dev)
 
     # -- end to end through the production entry point, host buffers ------
     e2e = None
@@ -758,14 +1045,13 @@ def main():
                   if args.layout == "soa_k3v3"
                   else "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"),
         "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
-        "config": {"workload": cfg["workload"], "layout": args.layout,
-                   "per_gpu_batch": B, "global_batch": world * B, "seq_len": w["L"],
-                   "num_splits": S, "parallelism": f"dp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (cache %.0f MB per GPU vs 126 MB L2); no flush"
-                         % (w["kv"].numel() / 1e6)},
+        "config": c1_config(cfg, args.layout, B, w["L"], S, world, w["kv"].numel() / 1e6),
         "stage1_us": s1_avg_ms * 1e3,
         "stage2_us": (ms_per_step - s1_avg_ms) * 1e3,
-        "timing": "CUDA-graph replay of the decode step (Stage1 + Stage2), CUDA events; stage1_us from Stage1-only replays",
+        "timing": ("value: exactly `steps` CUDA-graph replays of the decode step (Stage1 + Stage2) after "
+                   "`warmup`, CUDA events; stage1_us: `steps` Stage1-only replays (the roofline's duration); "
+                   "stage1_us_reference_protocol: the reference's protocol (benchmarks/stage1.py, 20 warm-up + "
+                   "100 timed, 5 rotated rounds, median) in reference_gpu"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -780,11 +1066,21 @@ def main():
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
+        med = ref_gpu.get("median_us", {})
+        if "tqb (graph replay)" in med:
+            line["stage1_us_reference_protocol"] = med["tqb (graph replay)"]
+            line["speedup_vs_v2_fixed"] = ref_gpu["speedup_vs_v2_fixed"]["tqb (graph replay)"]
     if args.layout == "soa":
         line["store"] = measure_store(w, dev, peak)
     if not args.no_cpu_baseline and world == 1 and args.layout not in ("soa_k8", "soa_k3", "soa_k3v3"):
         # the C restatement covers the 4-bit keys only
-        line["cpu_baseline"] = cpu_baseline(w)
+        line["cpu_baseline"], oracle_res = cpu_baseline(w)
+        line["parity"] = parity_vs_oracle(mid, out, lse, oracle_res)
+        del oracle_res
+    if single_c1 and args.layout == "soa" and not args.no_interpreter:
+        line["reference_interpreter"] = interpreter_sample(w)
     print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -7,12 +7,21 @@
  * store.  Every entry point:
  *   - takes plain device pointers, sizes and byte/element strides (no torch
  *     types), and the CUDA stream to launch on;
- *   - launches asynchronously and allocates nothing;
+ *   - launches asynchronously;
  *   - returns TQB_OK (0) or a negative tqb_status; tqb_strerror() names it
  *     and tqb_last_error_detail() says which argument was rejected (per
  *     calling thread).
- * Thread safety: stateless apart from a per-device attribute cache; calls on
- * different streams may run concurrently.
+ * Memory: the decode, store and merge entry points allocate no device
+ * memory; the caller owns every buffer.  Two exceptions are named here:
+ * tqb_p2p_alloc allocates the sequence-parallel exchange buffer (that is its
+ * purpose), and tqb_decode_static uses a static partial buffer that the
+ * library holds on every device it runs on (4,227,072 bytes, a module-scope
+ * __device__ array, not an allocation per call).
+ * Library state: a per-device cache of device attributes and tensor-map
+ * support, the per-device address of tqb_decode_static's buffer, and device
+ * counters of bounded waits that gave up (tqb_wait_timeouts).  Calls on
+ * different streams may run concurrently, except tqb_decode_static calls on
+ * one device (they share its buffer).
  *
  * Reference interfaces replaced (paths inside zben777/turboquant-cuda-decode):
  *   tqb_stage1   <- launch_soa_v1_stage1 / launch_aos_v1_stage1
@@ -249,11 +258,11 @@ int tqb_version(void);
  * For callers that cannot allocate per call: a C or C++ host without a
  * caching allocator (cudaMalloc/cudaFree synchronise the device on every
  * step) and serving loops whose device memory is planned up front.
- * Limit: batch * num_q_heads * num_splits <= 8192 (a 4 MiB buffer per
- * device); larger calls return TQB_ERR_UNSUPPORTED.  The buffer address is
- * looked up on the first call on each device; make that first call before
- * any stream capture.  Calls that overlap on one device share the buffer
- * and race: serialise them.
+ * Limit: batch * num_q_heads * num_splits <= 8192 (8192 rows of 129 floats,
+ * 4,227,072 bytes per device); larger calls return TQB_ERR_UNSUPPORTED.  The
+ * buffer address is looked up on the first call on each device; make that
+ * first call before any stream capture.  Calls that overlap on one device
+ * share the buffer and race: serialise them.
  */
 typedef struct tqb_decode_static_args {
     tqb_stage1_args stage1;      /* as for tqb_stage1; mid_o fields ignored */

@@ -2,9 +2,9 @@
 
 This script runs the reference's own Triton kernels on the host CPU under
 ``TRITON_INTERPRET=1`` and saves their inputs and outputs as small ``.npz``
-fixtures next to this file.  It needs the reference checkout (default
-``/root/reference``, override with ``TQ_REFERENCE_DIR``) and is only run in the
-build container; the fixtures it writes are what travels and what the tests
+fixtures next to this file.  It needs a reference checkout, named by the
+``TQ_REFERENCE_DIR`` environment variable (required), and is only run where
+that checkout exists; the fixtures it writes are what travels and what the tests
 read.  Nothing here is imported by the product.
 
 Reference kernels exercised (paths relative to the reference checkout):
@@ -55,7 +55,9 @@ import torch  # noqa: E402
 import triton  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TQ_REFERENCE_DIR", "/root/reference"))
+if not os.environ.get("TQ_REFERENCE_DIR"):
+    raise SystemExit("set TQ_REFERENCE_DIR to a zben777/turboquant-cuda-decode checkout")
+REF = Path(os.environ["TQ_REFERENCE_DIR"])
 
 HEAD_DIM = 128
 BLOCK_SIZE = 16

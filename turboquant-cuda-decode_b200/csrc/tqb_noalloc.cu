@@ -9,8 +9,15 @@
 // with TQB_ERR_UNSUPPORTED.  Nothing in the buffer must start at zero: Stage2
 // reads exactly the rows Stage1 wrote in the same call.  Calls that overlap
 // on a device (different streams, or host threads) share the buffer and race.
+//
+// The per-device address slots are atomics: two host threads that make their
+// first call on one device at the same time both look the address up and
+// both store it; the lookups return the same address, so either store wins
+// with the same value.
 #include <cuda_runtime.h>
 #include <stdio.h>
+
+#include <atomic>
 
 #include "tqb_common.cuh"
 #include "tqb_internal.h"
@@ -22,7 +29,7 @@ constexpr int kMaxStaticDevices = 64;
 
 __device__ __align__(256) float g_static_partials[kStaticPartialRows * (tqb::kHeadDim + 1)];
 
-float* g_static_ptr[kMaxStaticDevices] = {nullptr};
+std::atomic<float*> g_static_ptr[kMaxStaticDevices] = {};
 
 int fail(int code, const char* msg) {
     tqb::set_error_detail(msg);
@@ -57,7 +64,8 @@ extern "C" int tqb_decode_static(const tqb_decode_static_args* a, cudaStream_t s
     }
     dev = attr.device;
     if (dev < 0 || dev >= kMaxStaticDevices) return fail(TQB_ERR_UNSUPPORTED, "device ordinal out of range");
-    if (g_static_ptr[dev] == nullptr) {
+    float* mid = g_static_ptr[dev].load(std::memory_order_acquire);
+    if (mid == nullptr) {
         if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
             cudaGetLastError();
             return fail(TQB_ERR_CUDA, "cannot select the device owning output");
@@ -69,9 +77,9 @@ extern "C" int tqb_decode_static(const tqb_decode_static_args* a, cudaStream_t s
             cudaGetLastError();
             return fail(TQB_ERR_CUDA, "cudaGetSymbolAddress of the static partial buffer failed");
         }
-        g_static_ptr[dev] = static_cast<float*>(p);
+        mid = static_cast<float*>(p);
+        g_static_ptr[dev].store(mid, std::memory_order_release);
     }
-    float* mid = g_static_ptr[dev];
 
     tqb_stage1_args s1 = s;
     s1.mid_o = mid;

@@ -107,10 +107,15 @@ __global__ void __launch_bounds__(kHeadDim) sp_merge_kernel(const SpMergeParams 
         int ok = 1;
         for (int r = 0; r < P.world && ok; r++) {
             const unsigned long long* f = flag_slot(P.buffer, L, parity, r, P.world);
-            if (ld_acquire_sys_u64(f) >= P.epoch) continue;
+            // A flag of this parity holds epoch - 2 (not yet sent) or epoch
+            // (sent).  Anything else (epoch + 2: the peer already overwrote
+            // these rows with a later step) is not ready either, so it ends
+            // in the timeout path (NaN and a counted timeout) rather than a
+            // merge of overwritten rows.
+            if (ld_acquire_sys_u64(f) == P.epoch) continue;
             const long long t0 = clock64();
             for (;;) {
-                if (ld_acquire_sys_u64(f) >= P.epoch) break;
+                if (ld_acquire_sys_u64(f) == P.epoch) break;
                 if (clock64() - t0 > kP2PWaitCycles) {
                     atomicAdd(&g_p2p_timeouts, 1u);
                     ok = 0;
