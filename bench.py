@@ -778,12 +778,15 @@ def run_sharded(args, world, rank, local):
     # SP: the local Stage2, the exchange of the merged rows and the
     # cross-range merge are the peer-memory exchange (tqb_sp_exchange +
     # tqb_sp_merge: rows stored straight into every rank's buffer over
-    # NVLink), not Stage2 + NCCL all-gather + merge kernel.
-    ex = sharding.P2PExchange(B, Hq, dev) if sp else None
+    # NVLink), not Stage2 + NCCL all-gather + merge kernel.  Its epochs are
+    # kept on the device, so the whole step is one CUDA graph.
+    ex = sharding.P2PExchange(B, Hq, dev, device_epochs=True) if sp else None
 
     def local_step():
         tqb.stage1(w["q_rot"], w["kv"], w["bt"], w["seq_lens"], w["cents"], mid, num_splits_per_seq=w["nsplits"])
-        if not sp:
+        if sp:
+            ex.step(mid, w["seq_lens"], fout, flse, num_splits_per_seq=w["nsplits"])
+        else:
             tqb.stage2(mid, w["seq_lens"], out, lse, num_splits_per_seq=w["nsplits"])
 
     cap = torch.cuda.Stream(dev)
@@ -797,8 +800,6 @@ def run_sharded(args, world, rank, local):
 
     def step():
         g.replay()
-        if sp:
-            ex.step(mid, w["seq_lens"], fout, flse, num_splits_per_seq=w["nsplits"])
 
     for _ in range(args.warmup):
         step()
@@ -839,7 +840,7 @@ def run_sharded(args, world, rank, local):
             "rank0_stage1_frac_of_peak": cache_bytes / (s1_ms * 1e-3) / 1e9 / peak,
             "peak_source": peak_kind,
             "timing": ("step = CUDA-graph replay of the local Stage1 + the peer-memory exchange "
-                       "(Stage2 rows to every rank over NVLink, then the merge)" if sp else
+                       "(Stage2 rows to every rank over NVLink, then the merge; device epochs)" if sp else
                        "step = CUDA-graph replay of the local Stage1+Stage2") + ", CUDA events, max over ranks",
             "e2e": None, "e2e_note": "the end-to-end leg is measured on the c1 headline config",
         }

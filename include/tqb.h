@@ -289,8 +289,13 @@ int tqb_decode_static(const tqb_decode_static_args* args, cudaStream_t stream);
  *     of tqb_merge_partials).
  * epoch is 1 on the first step and grows by one per step, identically on all
  * ranks; consecutive steps alternate between two row sets, so a rank may run
- * one step ahead of another.  A merge whose wait gives up writes NaN and
- * counts in tqb_wait_timeouts.  Every rank must call both, in the same order.
+ * one step ahead of another.  epoch 0 keeps the epoch on the device instead
+ * (a counter in the rank's buffer that the exchange advances and the merge
+ * reads): no per-step host value, so Stage1 + exchange + merge can be
+ * captured in one CUDA graph and replayed.  A buffer uses host epochs or
+ * device epochs from its first step on, never both.  A merge whose wait gives
+ * up writes NaN and counts in tqb_wait_timeouts.  Every rank must call both,
+ * in the same order.
  */
 #define TQB_P2P_MAX_RANKS 8
 #define TQB_IPC_HANDLE_BYTES 64
@@ -307,7 +312,7 @@ typedef struct tqb_sp_exchange_args {
     int32_t rank, world;               /* world <= TQB_P2P_MAX_RANKS */
     int64_t cap_rows;                  /* rows per slot, >= batch * num_q_heads, same on all ranks */
     void* buffers[TQB_P2P_MAX_RANKS];  /* every rank's buffer as mapped in this process */
-    uint64_t epoch;
+    uint64_t epoch;                    /* >= 1: host epoch; 0: device epoch */
 } tqb_sp_exchange_args;
 
 int tqb_sp_exchange(const tqb_sp_exchange_args* args, cudaStream_t stream);
@@ -316,7 +321,7 @@ typedef struct tqb_sp_merge_args {
     void* buffer;                      /* this rank's exchange buffer */
     int32_t world, batch, num_q_heads, head_dim;
     int64_t cap_rows;
-    uint64_t epoch;
+    uint64_t epoch;                    /* the exchange's epoch, or 0 with device epochs */
     float* output;                     /* [B, Hq, D] */
     int64_t out_stride_b, out_stride_h;
     float* lse;                        /* [B, Hq], may be NULL */

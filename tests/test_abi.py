@@ -145,10 +145,10 @@ int main(void) {
 
 
 def test_p2p_entry_points_reject_on_the_host(lib):
-    """The SP exchange validates rank, world, epoch and capacity before any
-    device call, and sizes its buffer as rows + flags + counter."""
+    """The SP exchange validates rank, world and capacity before any device
+    call, and sizes its buffer as rows + flags + CTA counter + step counter."""
     row = 129 * 4
-    assert lib.tqb_p2p_buffer_bytes(2, 128) == 2 * 2 * 128 * row + 2 * 2 * 8 + 8
+    assert lib.tqb_p2p_buffer_bytes(2, 128) == 2 * 2 * 128 * row + 2 * 2 * 8 + 8 + 8
     assert lib.tqb_p2p_buffer_bytes(0, 128) == -1
     assert lib.tqb_p2p_buffer_bytes(_lib.TQB_P2P_MAX_RANKS + 1, 128) == -1
     a = _lib.SpExchangeArgs()
@@ -156,9 +156,7 @@ def test_p2p_entry_points_reject_on_the_host(lib):
     a.rank, a.world, a.cap_rows, a.epoch = 0, 2, 64, 1
     a.rank = 2  # not below world
     assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
-    a.rank, a.epoch = 0, 0  # epochs start at 1
-    assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
-    a.epoch, a.cap_rows = 1, 63  # batch * heads = 64 rows do not fit
+    a.rank, a.epoch, a.cap_rows = 0, 0, 63  # device epochs; batch * heads = 64 rows do not fit
     assert lib.tqb_sp_exchange(ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
     assert b"cap_rows" in lib.tqb_last_error_detail()
     a.cap_rows = 64  # rows fit, but no mid_o / buffers given

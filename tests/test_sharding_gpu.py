@@ -83,15 +83,17 @@ def test_dp_ranks_reassembled(cuda_device):
     assert_close(got[..., 128], ref_lse, what="DP lse")
 
 
+@pytest.mark.parametrize("device_epochs", [False, True])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_sp_p2p_exchange_emulated(cuda_device, world):
+def test_sp_p2p_exchange_emulated(cuda_device, world, device_epochs):
     """The peer-memory SP exchange with every rank of one process on one GPU
     (local buffers, no IPC): all ranks send, then all merge; three steps, so
-    both row sets and growing epochs are used."""
+    both row sets and growing epochs are used (host epochs, or the epochs the
+    device keeps in each buffer)."""
     lens = [1000, 17, 4100, 1, 0]
     c = random_case(200 + world, len(lens), 32, 8, lens)
     dev = cuda_device
-    ranks = sharding.P2PExchange.emulated(world, len(lens), 32, dev)
+    ranks = sharding.P2PExchange.emulated(world, len(lens), 32, dev, device_epochs=device_epochs)
     ref_out, ref_lse = _full_ref(c)
     live = np.asarray(lens) > 0
     try:
@@ -118,6 +120,48 @@ def test_sp_p2p_exchange_emulated(cuda_device, world):
                 assert_close(got[live], ref_out[live], what=f"P2P SP{world} step {step} rank {r} output")
                 assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"P2P SP{world} rank {r} lse")
                 assert np.all(np.isnan(got[~live])), "a sequence without tokens merges to NaN"
+    finally:
+        ranks[0].close()
+
+
+def test_sp_p2p_device_epochs_graph_replay(cuda_device):
+    """Device epochs make the exchange graph-capturable: one CUDA graph holds
+    every emulated rank's exchange and then every rank's merge; three
+    replays, each checked against the single-range oracle."""
+    world, lens = 4, [900, 33, 2500]
+    c = random_case(210, len(lens), 32, 8, lens)
+    dev = cuda_device
+    ranks = sharding.P2PExchange.emulated(world, len(lens), 32, dev, device_epochs=True)
+    ref_out, ref_lse = _full_ref(c)
+    try:
+        mids = []
+        for r in range(world):
+            bt, sl, _ = sharding.sp_shard(_dev(c, "block_table", dev), lens, world, r)
+            mid = torch.empty(len(lens), 32, 8, 129, device=dev)
+            tqb.stage1(_dev(c, "q_rot", dev), _dev(c, "kv_cache", dev), bt, sl, _dev(c, "centroids", dev), mid)
+            mids.append((mid, sl))
+        outs = [(torch.empty(len(lens), 32, 128, device=dev), torch.empty(len(lens), 32, device=dev))
+                for _ in range(world)]
+        torch.cuda.synchronize()
+        tqb.wait_timeouts(reset=True)
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for r in range(world):
+                    ranks[r].send(*mids[r])
+                for r in range(world):
+                    ranks[r].recv(*outs[r])
+        for step in range(3):
+            for o, l in outs:
+                o.fill_(-1.0)
+            g.replay()
+            torch.cuda.synchronize()
+            assert tqb.wait_timeouts(reset=True) == 0
+            for r, (o, l) in enumerate(outs):
+                assert_close(o.cpu().numpy(), ref_out, what=f"graph step {step} rank {r} output")
+                assert_close(l.cpu().numpy(), ref_lse, what=f"graph step {step} rank {r} lse")
+        del g
     finally:
         ranks[0].close()
 

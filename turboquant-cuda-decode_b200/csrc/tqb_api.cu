@@ -356,7 +356,6 @@ int tqb_sp_exchange(const tqb_sp_exchange_args* a, cudaStream_t stream) {
     const tqb_stage2_args* s = &a->stage2;
     TQB_REQUIRE(a->world >= 1 && a->world <= TQB_P2P_MAX_RANKS && a->rank >= 0 && a->rank < a->world,
                 TQB_ERR_INVALID_ARG, "rank/world out of range");
-    TQB_REQUIRE(a->epoch >= 1, TQB_ERR_INVALID_ARG, "epoch must start at 1");
     TQB_REQUIRE(s->batch >= 0 && s->num_q_heads > 0 && s->num_splits > 0, TQB_ERR_INVALID_ARG,
                 "batch/heads/num_splits must be positive");
     TQB_REQUIRE(s->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
@@ -391,7 +390,6 @@ int tqb_sp_merge(const tqb_sp_merge_args* a, cudaStream_t stream) {
     g_detail[0] = '\0';
     TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
     TQB_REQUIRE(a->world >= 1 && a->world <= TQB_P2P_MAX_RANKS, TQB_ERR_INVALID_ARG, "world out of range");
-    TQB_REQUIRE(a->epoch >= 1, TQB_ERR_INVALID_ARG, "epoch must start at 1");
     TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0, TQB_ERR_INVALID_ARG, "batch/heads must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE((int64_t)a->batch * a->num_q_heads <= a->cap_rows && a->cap_rows < (int64_t(1) << 31),

@@ -7,7 +7,14 @@
 //     recv  [2 parities][G ranks][cap_rows][D+1] fp32   (O, LSE) rows
 //     flags [2 parities][G ranks] uint64               epoch received
 //     done  uint32                                     CTAs finished (local)
-// Call k of a rank (epoch k + 1) uses parity k & 1.
+//     step  uint64                                     last epoch sent (local)
+// Call k of a rank (epoch k + 1) uses parity k & 1.  The epoch is either
+// given by the host (1, 2, ... on every rank) or, with epoch 0 in the call,
+// kept on the device in `step`: the exchange reads step + 1 and its last CTA
+// stores it back, the merge reads step.  Device epochs need no host value
+// per step, so a whole decode step (Stage1, exchange, merge) can be
+// captured once in a CUDA graph and replayed.  One buffer uses one of the
+// two forms from the start (a zero-filled buffer); they are not mixed.
 //  * tqb_sp_exchange: one CTA per (b, h) merges the rank's own splits (the
 //    Stage2 algebra) and stores the row straight into slot [rank] of every
 //    rank's recv buffer; every thread then fences at system scope, and the
@@ -48,14 +55,23 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 
 // Exchange-buffer layout (bytes).
 struct P2PLayout {
-    int64_t recv_bytes, flags_off, done_off, total;
+    int64_t recv_bytes, flags_off, done_off, step_off, total;
     __host__ __device__ P2PLayout(int world, int64_t cap_rows) {
         recv_bytes = 2 * (int64_t)world * cap_rows * kRow * 4;
         flags_off = (recv_bytes + 7) / 8 * 8;
         done_off = flags_off + 2 * (int64_t)world * 8;
-        total = done_off + 8;
+        step_off = done_off + 8;
+        total = step_off + 8;
     }
 };
+__device__ __forceinline__ unsigned long long* step_slot(void* buf, const P2PLayout& L) {
+    return reinterpret_cast<unsigned long long*>(static_cast<char*>(buf) + L.step_off);
+}
+// The step counter is written by an earlier kernel on this GPU (stream
+// order): read it from L2, not from a line an earlier launch left in L1.
+__device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
+    return __ldcg(p);
+}
 __device__ __forceinline__ float* recv_slot(void* buf, int parity, int src, int world, int64_t cap_rows) {
     return static_cast<float*>(buf) + ((int64_t)parity * world + src) * cap_rows * kRow;
 }
@@ -72,7 +88,11 @@ __global__ void __launch_bounds__(kHeadDim) sp_exchange_kernel(const SpExchangeP
     const int b = (int)(item / P.s2.Hq), h = (int)(item % P.s2.Hq);
     float o, lse;
     merge_row(P.s2, b, h, &o, &lse);
-    const int parity = (int)((P.epoch - 1) & 1);
+    const P2PLayout L(P.world, P.cap_rows);
+    // Device epochs: every CTA reads step before the last CTA advances it
+    // (the last CTA is the one that finds all others counted in `done`).
+    const unsigned long long epoch = P.epoch ? P.epoch : ld_cg_u64(step_slot(P.buffers[P.rank], L)) + 1ull;
+    const int parity = (int)((epoch - 1) & 1);
     const int d = threadIdx.x;
     for (int r = 0; r < P.world; r++) {
         float* row = recv_slot(P.buffers[r], parity, P.rank, P.world, P.cap_rows) + item * kRow;
@@ -83,14 +103,14 @@ __global__ void __launch_bounds__(kHeadDim) sp_exchange_kernel(const SpExchangeP
     __threadfence_system();
     __syncthreads();
     if (d == 0) {
-        const P2PLayout L(P.world, P.cap_rows);
         unsigned int* done = reinterpret_cast<unsigned int*>(static_cast<char*>(P.buffers[P.rank]) + L.done_off);
         if (atomicAdd(done, 1u) == gridDim.x - 1) {
             // the last CTA: all rows of this rank are visible; publish the epoch
             __threadfence_system();
             *done = 0u;  // ready for the next call (a later launch on this stream)
+            if (!P.epoch) *step_slot(P.buffers[P.rank], L) = epoch;
             for (int r = 0; r < P.world; r++)
-                st_release_sys_u64(flag_slot(P.buffers[r], L, parity, P.rank, P.world), P.epoch);
+                st_release_sys_u64(flag_slot(P.buffers[r], L, parity, P.rank, P.world), epoch);
         }
     }
 }
@@ -101,8 +121,10 @@ __global__ void __launch_bounds__(kHeadDim) sp_merge_kernel(const SpMergeParams 
     __shared__ int s_ok;
     const int64_t item = blockIdx.x;
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
-    const int parity = (int)((P.epoch - 1) & 1);
     const P2PLayout L(P.world, P.cap_rows);
+    // device epochs: this rank's exchange, earlier on this stream, stored it
+    const unsigned long long epoch = P.epoch ? P.epoch : ld_cg_u64(step_slot(P.buffer, L));
+    const int parity = (int)((epoch - 1) & 1);
     if (threadIdx.x == 0) {
         int ok = 1;
         for (int r = 0; r < P.world && ok; r++) {
@@ -112,10 +134,10 @@ __global__ void __launch_bounds__(kHeadDim) sp_merge_kernel(const SpMergeParams 
             // these rows with a later step) is not ready either, so it ends
             // in the timeout path (NaN and a counted timeout) rather than a
             // merge of overwritten rows.
-            if (ld_acquire_sys_u64(f) == P.epoch) continue;
+            if (ld_acquire_sys_u64(f) == epoch) continue;
             const long long t0 = clock64();
             for (;;) {
-                if (ld_acquire_sys_u64(f) == P.epoch) break;
+                if (ld_acquire_sys_u64(f) == epoch) break;
                 if (clock64() - t0 > kP2PWaitCycles) {
                     atomicAdd(&g_p2p_timeouts, 1u);
                     ok = 0;

@@ -224,15 +224,20 @@ class P2PExchange:
 
     ``emulated(world, ...)`` builds the ``world`` ranks of one process on one
     GPU (the buffers are local; ranks are stepped one after another), for
-    testing the data path without IPC."""
+    testing the data path without IPC.
+
+    ``device_epochs=True`` keeps the step epoch in the exchange buffer on the
+    device (epoch 0 in the C calls): ``step`` then passes no per-step value,
+    so it can be recorded into a CUDA graph with Stage1 and replayed."""
 
     def __init__(self, batch: int, num_q_heads: int, device: torch.device, group=None, *,
-                 _local: Optional[dict] = None):
+                 device_epochs: bool = False, _local: Optional[dict] = None):
         from . import _lib
 
         self._lib = _lib.load()
         self.device = torch.device(device)
         self.cap_rows = batch * num_q_heads
+        self.device_epochs = device_epochs
         self.epoch = 0
         self._imported = []
         self._owned = None
@@ -268,7 +273,8 @@ class P2PExchange:
         self.buffers = buffers
 
     @classmethod
-    def emulated(cls, world: int, batch: int, num_q_heads: int, device: torch.device) -> list["P2PExchange"]:
+    def emulated(cls, world: int, batch: int, num_q_heads: int, device: torch.device, *,
+                 device_epochs: bool = False) -> list["P2PExchange"]:
         from . import _lib
 
         lib = _lib.load()
@@ -279,8 +285,8 @@ class P2PExchange:
                 p = ctypes.c_void_p()
                 _lib.check(lib.tqb_p2p_alloc(nbytes, ctypes.byref(p)))
                 bufs.append(p.value)
-        ranks = [cls(batch, num_q_heads, device, _local={"world": world, "rank": r, "buffers": bufs})
-                 for r in range(world)]
+        ranks = [cls(batch, num_q_heads, device, device_epochs=device_epochs,
+                     _local={"world": world, "rank": r, "buffers": bufs}) for r in range(world)]
         ranks[0]._owned_list = bufs  # freed by ranks[0].close()
         return ranks
 
@@ -314,7 +320,8 @@ class P2PExchange:
         if num_splits_per_seq is not None:
             s2.num_splits_per_seq = num_splits_per_seq.data_ptr()
         s2.batch, s2.num_q_heads, s2.head_dim, s2.num_splits = B, Hq, D1 - 1, S
-        a.rank, a.world, a.cap_rows, a.epoch = self.rank, self.world, self.cap_rows, self.epoch
+        a.rank, a.world, a.cap_rows = self.rank, self.world, self.cap_rows
+        a.epoch = 0 if self.device_epochs else self.epoch
         for r, p in enumerate(self.buffers):
             a.buffers[r] = p
         with torch.cuda.device(self.device):
@@ -328,7 +335,8 @@ class P2PExchange:
         B, Hq, D = self._shape
         m = _lib.SpMergeArgs()
         m.buffer, m.world, m.batch, m.num_q_heads, m.head_dim = self.buffers[self.rank], self.world, B, Hq, D
-        m.cap_rows, m.epoch = self.cap_rows, self.epoch
+        m.cap_rows = self.cap_rows
+        m.epoch = 0 if self.device_epochs else self.epoch
         m.output, m.out_stride_b, m.out_stride_h = output.data_ptr(), output.stride(0), output.stride(1)
         if lse is not None:
             m.lse, m.lse_stride_b = lse.data_ptr(), lse.stride(0)
