@@ -81,7 +81,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--config", default="c1",
+                    help="one of " + ", ".join(sorted(CONFIGS)) + "; a comma-separated list of the sharded "
+                         "configs (c2,c3,c4) runs them one after another in one process, one line each")
     ap.add_argument("--layout", choices=["soa", "aos", "soa_k8", "soa_k3", "soa_k3v3"], default="soa",
                     help="cache layout; soa_k8 = the turboquant_k8v4 preset (FP8 keys, 4-bit values), "
                          "soa_k3 = turboquant_k3v4_nc (3-bit keys, 4-bit values), soa_k3v3 = "
@@ -97,7 +99,13 @@ def parse_args():
                     help="skip the reference-under-TRITON_INTERPRET CPU sample")
     ap.add_argument("--interp-child", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
-    if args.splits is not None:
+    cfgs = args.config.split(",")
+    for c in cfgs:
+        if c not in CONFIGS:
+            ap.error(f"unknown config {c!r}")
+    if len(cfgs) > 1 and "c1" in cfgs:
+        ap.error("c1 runs alone; lists are for the sharded configs c2, c3, c4")
+    if args.splits is not None and len(cfgs) == 1:
         CONFIGS[args.config] = dict(CONFIGS[args.config], S=args.splits)
     return args
 
@@ -835,7 +843,9 @@ def run_sharded(args, world, rank, local):
             "config": {"workload": cfg["workload"], "layout": "soa", "global_batch": w["total_seqs"],
                        "parallelism": f"{cfg['parallel']}{world}", "rank0_batch": B, "rank0_heads": Hq,
                        "rank0_cache_bytes": cache_bytes},
+            "gpus_active": world, "nccl_ranks": world,
             "stage1_us_max_over_ranks": s1_ms * 1e3,
+            "rest_of_step_us": (ms - s1_ms) * 1e3,
             "rank0_stage1_hbm_gbs": cache_bytes / (s1_ms * 1e-3) / 1e9,
             "rank0_stage1_frac_of_peak": cache_bytes / (s1_ms * 1e-3) / 1e9 / peak,
             "peak_source": peak_kind,
@@ -850,6 +860,132 @@ def run_sharded(args, world, rank, local):
         ex.close()
 
 
+def measure_e2e(args, w, dev, world: int, B: int, Hq: int, S: int) -> dict:
+    """End to end through tqb.triton_turboquant_decode_attention with host
+    buffers.  A step copies its inputs (query, block table, seq_lens: packed
+    in one pinned host buffer, one copy) to the device, calls the API
+    (fused query cast + rotation, Stage1, Stage2 writing bf16) on typed views
+    of the device copy, and copies the bf16 output back to pinned host
+    memory.  Every step does both copies.
+
+    Three forms, same work per step:
+      * ``value``: each of two buffer sets records its step (the two copies
+        and the API call) once as a CUDA graph, and the graphs are replayed
+        on two streams, so one step's copies overlap the other step's
+        kernels, as a serving loop with two batches in flight;
+      * ``serial_graph``: one buffer set, its graph replayed back to back;
+      * ``serial_eager``: the Python call every step, one stream.
+    Device time by CUDA events over `e2e_steps` steps, max over ranks."""
+    import tqb
+
+    srcs = [w["query"], w["bt"], w["seq_lens"]]
+    offs, n = [], 0
+    for t in srcs:
+        offs.append(n)
+        n += (t.numel() * t.element_size() + 255) // 256 * 256
+
+    def views(buf):
+        return [buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for o, t in zip(offs, srcs)]
+
+    def make_set():
+        hbuf = torch.empty(n, dtype=torch.uint8).pin_memory()
+        for h, t in zip(views(hbuf), srcs):
+            h.copy_(t.cpu())
+        st = {"hbuf": hbuf, "dbuf": torch.empty(n, dtype=torch.uint8, device=dev),
+              "hout": torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory(),
+              "mbuf": torch.empty(B, Hq, S, 129, device=dev),
+              "obuf": torch.empty(B, Hq, 128, dtype=w["query"].dtype, device=dev),  # vLLM's workspace: query dtype
+              "lbuf": torch.empty(B, Hq, device=dev)}
+        st["dq"], st["dbt"], st["dsl"] = views(st["dbuf"])
+        return st
+
+    def e2e_step(st):
+        st["dbuf"].copy_(st["hbuf"], non_blocking=True)
+        o = tqb.triton_turboquant_decode_attention(
+            st["dq"], w["kv"], st["dbt"], st["dsl"], w["R"].T, w["cents"], 1.0 / math.sqrt(128),
+            {"soa_k8": 8, "soa_k3": 3, "soa_k3v3": 3}.get(args.layout, 4),
+            {"soa_k8": 128, "soa_k3": 50, "soa_k3v3": 50}.get(args.layout, 66),
+            3 if args.layout == "soa_k3v3" else 4,
+            key_fp8=args.layout == "soa_k8", norm_correction=args.layout != "soa_k8", PiT=w["R"],
+            mid_o_buf=st["mbuf"], output_buf=st["obuf"], lse_buf=st["lbuf"], max_num_kv_splits=S)
+        st["hout"].copy_(o, non_blocking=True)
+
+    K = args.e2e_steps
+    sets = [make_set(), make_set()]
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+
+    def timed(run) -> float:
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        a.record(cur)
+        for sm in streams:
+            sm.wait_event(a)
+        run()
+        for sm in streams:
+            cur.wait_stream(sm)
+        b_.record(cur)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        return max_over_ranks(a.elapsed_time(b_), world) / K
+
+    # eager, one stream (the launches from Python every step)
+    for _ in range(3):
+        with torch.cuda.stream(streams[0]):
+            e2e_step(sets[0])
+
+    def run_eager():
+        with torch.cuda.stream(streams[0]):
+            for _ in range(K):
+                e2e_step(sets[0])
+
+    eager_ms = timed(run_eager)
+    # each buffer set's step recorded once as a graph on its own stream
+    graphs = []
+    for st, sm in zip(sets, streams):
+        with torch.cuda.stream(sm):
+            e2e_step(st)
+            sm.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=sm):
+                e2e_step(st)
+        graphs.append(g)
+    torch.cuda.synchronize(dev)
+    for _ in range(3):
+        for g, sm in zip(graphs, streams):
+            with torch.cuda.stream(sm):
+                g.replay()
+
+    def run_serial():
+        with torch.cuda.stream(streams[0]):
+            for _ in range(K):
+                graphs[0].replay()
+
+    def run_pipelined():
+        for i in range(K):
+            with torch.cuda.stream(streams[i % 2]):
+                graphs[i % 2].replay()
+
+    serial_ms = timed(run_serial)
+    piped_ms = timed(run_pipelined)
+    del graphs
+    st = sets[0]
+    h2d = st["hbuf"].numel()  # the packed buffer, padding included
+    d2h = st["hout"].numel() * st["hout"].element_size()
+    return {"value": world * B / (piped_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": piped_ms, "steps": K,
+            "serial_graph": {"value": world * B / (serial_ms * 1e-3), "ms_per_step": serial_ms},
+            "serial_eager": {"value": world * B / (eager_ms * 1e-3), "ms_per_step": eager_ms},
+            "path": "tqb.triton_turboquant_decode_attention (fused query cast + rotation, Stage1, Stage2 "
+                    "writing bf16); per step one H2D copy of query/block_table/seq_lens from one pinned "
+                    "host buffer and one D2H copy of the bf16 output to pinned memory; value: each of two "
+                    "buffer sets' steps (copies + API call) recorded once as a CUDA graph, replayed "
+                    "alternately on two streams (two steps in flight); serial_graph: one graph, one "
+                    "stream; serial_eager: the Python call every step"}
+
+
 def main():
     args = parse_args()
     if args.interp_child:
@@ -860,7 +996,10 @@ def main():
     if args.layout in ("soa_k8", "soa_k3", "soa_k3v3") and args.config != "c1":
         raise SystemExit("--layout soa_k8 / soa_k3 / soa_k3v3 run the single-GPU c1 workload only")
     if args.impl == "ours" and args.config != "c1":
-        run_sharded(args, world, rank, local)
+        for c in args.config.split(","):
+            args.config = c
+            run_sharded(args, world, rank, local)
+            barrier(world)
         if world > 1:
             import torch.distributed as dist
 
@@ -964,59 +1103,7 @@ def main():
     # -- end to end through the production entry point, host buffers ------
     e2e = None
     if args.e2e_steps > 0:
-        # The step's inputs (query, block table, seq_lens) sit packed in one
-        # pinned host buffer and go over in one copy, as a serving loop would
-        # stage them; the API is called on typed views of the device copy.
-        srcs = [w["query"], w["bt"], w["seq_lens"]]
-        offs, n = [], 0
-        for t in srcs:
-            offs.append(n)
-            n += (t.numel() * t.element_size() + 255) // 256 * 256
-        hbuf = torch.empty(n, dtype=torch.uint8).pin_memory()
-        dbuf = torch.empty(n, dtype=torch.uint8, device=dev)
-
-        def views(buf):
-            return [buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for o, t in zip(offs, srcs)]
-
-        hq, hbt, hsl = views(hbuf)
-        for h, t in zip((hq, hbt, hsl), srcs):
-            h.copy_(t.cpu())
-        dq, dbt, dsl = views(dbuf)
-        hout = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
-        mbuf = torch.empty(B, Hq, S, 129, device=dev)
-        obuf = torch.empty(B, Hq, 128, dtype=w["query"].dtype, device=dev)  # vLLM's workspace: query dtype
-        lbuf = torch.empty(B, Hq, device=dev)
-
-        def e2e_step():
-            dbuf.copy_(hbuf, non_blocking=True)
-            o = tqb.triton_turboquant_decode_attention(
-                dq, w["kv"], dbt, dsl, w["R"].T, w["cents"], 1.0 / math.sqrt(128),
-                {"soa_k8": 8, "soa_k3": 3, "soa_k3v3": 3}.get(args.layout, 4),
-                {"soa_k8": 128, "soa_k3": 50, "soa_k3v3": 50}.get(args.layout, 66),
-                3 if args.layout == "soa_k3v3" else 4,
-                key_fp8=args.layout == "soa_k8", norm_correction=args.layout != "soa_k8", PiT=w["R"],
-                mid_o_buf=mbuf, output_buf=obuf, lse_buf=lbuf, max_num_kv_splits=S)
-            hout.copy_(o, non_blocking=True)
-
-        for _ in range(3):
-            e2e_step()
-        torch.cuda.synchronize(dev)
-        barrier(world)
-        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        b_.record()
-        torch.cuda.synchronize(dev)
-        barrier(world)
-        e2e_ms = max_over_ranks(a.elapsed_time(b_), world) / args.e2e_steps
-        h2d = hbuf.numel()  # the packed buffer, padding included
-        d2h = hout.numel() * hout.element_size()
-        e2e = {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-               "path": "tqb.triton_turboquant_decode_attention (fused query cast + rotation, Stage1, Stage2 "
-                       "writing bf16), query/block_table/seq_lens in one pinned host buffer (one copy), "
-                       "bf16 output out"}
+        e2e = measure_e2e(args, w, dev, world, B, Hq, S)
 
     if rank != 0:
         if world > 1:

@@ -146,9 +146,10 @@ int main(void) {
 
 def test_p2p_entry_points_reject_on_the_host(lib):
     """The SP exchange validates rank, world and capacity before any device
-    call, and sizes its buffer as rows + flags + CTA counter + step counter."""
+    call, and sizes its buffer as rows of tagged elements (value + epoch, 8
+    bytes each) + CTA counter + step counter."""
     row = 129 * 4
-    assert lib.tqb_p2p_buffer_bytes(2, 128) == 2 * 2 * 128 * row + 2 * 2 * 8 + 8 + 8
+    assert lib.tqb_p2p_buffer_bytes(2, 128) == 2 * 2 * 128 * 2 * row + 8 + 8
     assert lib.tqb_p2p_buffer_bytes(0, 128) == -1
     assert lib.tqb_p2p_buffer_bytes(_lib.TQB_P2P_MAX_RANKS + 1, 128) == -1
     a = _lib.SpExchangeArgs()

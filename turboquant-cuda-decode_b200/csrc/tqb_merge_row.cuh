@@ -5,11 +5,13 @@
 // (baseline/stage2.py:8-55): out = sum_s w_s O_s / sum_s w_s with
 // w_s = exp(lse_s - max), lse = max + ln(sum_s w_s); the exponentials and the
 // logarithm run on the hardware base-2 units (as Triton's tl.exp / tl.log in
-// the reference's Stage2 do).  Called by all 128
-// threads of a CTA (4 warps; warp w merges splits w, w + 4, ... with the loads
-// of kSplitsPerPass splits in flight, lane l owning dims l, l+32, l+64, l+96;
-// the four partial states combine through shared memory).  Thread d returns
-// output dim d in *o and every thread the row's LSE in *lse_out.
+// the reference's Stage2 do).  Called by all threads of a CTA of kWarps
+// warps (warp w merges splits w, w + kWarps, ... with the loads of
+// kSplitsPerPass splits in flight, lane l owning dims l, l+32, l+64, l+96;
+// the kWarps partial states combine through shared memory).  Thread d < 128
+// returns output dim d in *o, and every thread the row's LSE in *lse_out.
+// Stage2 uses 4 warps per row (many rows, few splits each); the
+// sequence-parallel exchange 16 (few rows, many splits each).
 #pragma once
 
 #include "tqb_common.cuh"
@@ -19,8 +21,9 @@ namespace tqb {
 
 constexpr int kSplitsPerPass = 4;  // splits whose loads a warp keeps in flight at once
 
+template <int kParts = kHeadDim / 32>
 __device__ __forceinline__ void merge_row(const Stage2Params& P, int b, int h, float* o, float* lse_out) {
-    constexpr int kParts = kHeadDim / 32;  // warps per CTA
+    static_assert(kParts * 32 >= kHeadDim, "one thread per output dim");
     __shared__ float s_acc[kParts][kHeadDim];
     __shared__ float s_max[kParts], s_sum[kParts];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -65,7 +68,7 @@ __device__ __forceinline__ void merge_row(const Stage2Params& P, int b, int h, f
         s_sum[warp] = sum;
     }
     __syncthreads();
-    const int d = threadIdx.x;
+    const int d = threadIdx.x < kHeadDim ? threadIdx.x : kHeadDim - 1;
     float gmax = -INFINITY;
 #pragma unroll
     for (int p = 0; p < kParts; p++) gmax = fmaxf(gmax, s_max[p]);
