@@ -287,13 +287,17 @@ __device__ __forceinline__ int tile_items(const Stage1Params& P, uint32_t t, int
 }
 
 // ---------------------------------------------------------------------------
-// Balanced tile ranges.  The items (b, s, KV head) in order are weighted by
-// their split's token count plus kSplitCost (empty splits weigh nothing) and
+// Balanced tile ranges.  The items (b, s, KV head) in order are weighted and
 // cut into gridDim.x * kGroups ranges of equal weight; group g takes the
-// tiles whose first item starts inside its range: a contiguous run of tiles
-// of about equal work, whatever the spread of sequence lengths.  Every CTA
-// derives the same cut from seq_lens (and nsplits), so no state is shared
-// between CTAs or launches.
+// tiles whose first item starts inside its range: a contiguous run of tiles.
+// Weights: with many tiles per group, each item weighs its split's token
+// count plus kSplitCost, so ranges carry about equal work whatever the
+// spread of sequence lengths; with at most two non-empty tiles per group
+// (a small batch, e.g. one rank's share of a data-parallel batch), each
+// non-empty item weighs 1, so every group takes one or two tiles: equal
+// token weights would let a range catch a short tile and a long one.  Empty
+// splits weigh nothing either way.  Every CTA derives the same cut from
+// seq_lens (and nsplits), so no state is shared between CTAs or launches.
 // ---------------------------------------------------------------------------
 struct SeqSplit {
     int L, sl, ne;  // clamped length, split length, non-empty splits
@@ -311,8 +315,8 @@ __device__ __forceinline__ SeqSplit seq_split_of(const Stage1Params& P, int len,
 __device__ __forceinline__ SeqSplit seq_split(const Stage1Params& P, int b) {
     return seq_split_of(P, __ldg(P.seq_lens + b), P.nsplits ? __ldg(P.nsplits + b) : P.S);
 }
-__device__ __forceinline__ long long seq_weight(const Stage1Params& P, const SeqSplit& q) {
-    return (long long)P.Hk * ((long long)q.L + (long long)kSplitCost * q.ne);
+__device__ __forceinline__ long long seq_weight(const Stage1Params& P, const SeqSplit& q, bool by_count) {
+    return by_count ? (long long)P.Hk * q.ne : (long long)P.Hk * ((long long)q.L + (long long)kSplitCost * q.ne);
 }
 __device__ __forceinline__ long long warp_sum_ll(long long v) {
 #pragma unroll
@@ -323,11 +327,12 @@ __device__ __forceinline__ long long warp_sum_ll(long long v) {
 // at most the sequence's weight): split s* = the last split starting below
 // r, then the KV head in it.
 __device__ __forceinline__ uint32_t cut_tile(const Stage1Params& P, const SeqSplit& q, int b, long long r,
-                                             uint32_t num_tiles) {
-    const long long unit = (long long)P.Hk * (q.sl + kSplitCost);
+                                             uint32_t num_tiles, bool by_count) {
+    const long long unit = by_count ? (long long)P.Hk : (long long)P.Hk * (q.sl + kSplitCost);
     const long long ss = min((long long)(q.ne - 1), (r - 1) / unit);
     const long long a = unit * ss;
-    const long long per = (long long)(min((int)(ss + 1) * q.sl, q.L) - (int)ss * q.sl) + kSplitCost;
+    const long long per =
+        by_count ? 1 : (long long)(min((int)(ss + 1) * q.sl, q.L) - (int)ss * q.sl) + kSplitCost;
     const long long kv = (r - a + per - 1) / per;  // in [1, Hk]
     const long long item = ((long long)b * P.S + ss) * P.Hk + kv;
     return (uint32_t)min((long long)num_tiles, (item + kGroupWarps - 1) / kGroupWarps);
@@ -341,14 +346,16 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
                           int lane) {
     const uint32_t cuts = gridDim.x * (uint32_t)groups_per_cta;
     const uint32_t g = blockIdx.x * (uint32_t)groups_per_cta + (uint32_t)gi;
-    long long tot = 0;
+    long long tot = 0, cnt = 0;
     int lmin = 0x7fffffff, lmax = -0x7fffffff, nmin = 0x7fffffff, nmax = -0x7fffffff;
 #pragma unroll 1
     for (int b0 = 0; b0 < P.B; b0 += 32) {
         const int b = b0 + lane;
         if (b < P.B) {
             const int len = __ldg(P.seq_lens + b), nsp = P.nsplits ? __ldg(P.nsplits + b) : P.S;
-            tot += seq_weight(P, seq_split_of(P, len, nsp));
+            const SeqSplit q = seq_split_of(P, len, nsp);
+            tot += seq_weight(P, q, false);
+            cnt += seq_weight(P, q, true);
             lmin = min(lmin, len);
             lmax = max(lmax, len);
             nmin = min(nmin, nsp);
@@ -356,6 +363,7 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
         }
     }
     tot = warp_sum_ll(tot);
+    cnt = warp_sum_ll(cnt);
     if (__reduce_min_sync(0xffffffffu, lmin) == __reduce_max_sync(0xffffffffu, lmax) &&
         __reduce_min_sync(0xffffffffu, nmin) == __reduce_max_sync(0xffffffffu, nmax)) {
         res[0] = g;
@@ -364,6 +372,8 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
         return;
     }
     res[2] = 1u;
+    const bool by_count = cnt <= 2LL * kGroupWarps * (long long)cuts;  // <= 2 non-empty tiles per group
+    if (by_count) tot = cnt;
     const long long qt = tot / (long long)cuts, rt = tot % (long long)cuts;
 #pragma unroll 1
     for (int k = 0; k < 2; k++) {
@@ -381,7 +391,7 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
                 const int b = b0 + lane;
                 SeqSplit q{0, 1, 0};
                 if (b < P.B) q = seq_split(P, b);
-                const long long w = seq_weight(P, q);
+                const long long w = seq_weight(P, q, by_count);
                 long long incl = w;
 #pragma unroll 1
                 for (int o = 1; o < 32; o <<= 1) {
@@ -392,7 +402,7 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
                 const bool here = w > 0 && excl < tgt && tgt <= base + incl;
                 const uint32_t m = __ballot_sync(0xffffffffu, here);
                 if (m) {
-                    const uint32_t tl = here ? cut_tile(P, q, b, tgt - excl, num_tiles) : 0u;
+                    const uint32_t tl = here ? cut_tile(P, q, b, tgt - excl, num_tiles, by_count) : 0u;
                     t = __shfl_sync(0xffffffffu, tl, __ffs(m) - 1);
                     break;
                 }
