@@ -88,7 +88,19 @@ typedef enum tqb_layout {
      * with 3-bit values too: [16 tok][Hk][K48 | V48] + [Hk][3][16] fp16 meta,
      * 102 bytes per token-head; value dim d at bits 3d..3d+2 of its 48 bytes,
      * v = code * vscale + vzero with codes 0..7. */
-    TQB_LAYOUT_SOA_K3V3 = 4
+    TQB_LAYOUT_SOA_K3V3 = 4,
+    /* AoS forms of the three presets above (reference/aos_store.py:26-340,
+     * reference/aos_decode.py:43-313): one slot per (token, KV head),
+     * [key codes | fp16 key norm | value codes | fp16 vscale | fp16 vzero],
+     * addressed like TQB_LAYOUT_AOS through the position and head strides.
+     * TQB_LAYOUT_AOS_K8: 128 e4m3 key bytes, no norm, 64 value bytes: 196
+     * bytes.  TQB_LAYOUT_AOS_K3: 48 bytes of 3-bit keys, the raw norm, 64
+     * value bytes: 118 bytes.  TQB_LAYOUT_AOS_K3V3: as AOS_K3 with 48 bytes of
+     * 3-bit values: 102 bytes.  Like TQB_LAYOUT_AOS, the Lloyd-Max forms store
+     * the raw |k| and Stage1 applies the norm correction c / |c|. */
+    TQB_LAYOUT_AOS_K8 = 5,
+    TQB_LAYOUT_AOS_K3 = 6,
+    TQB_LAYOUT_AOS_K3V3 = 7
 } tqb_layout;
 
 /*
@@ -115,7 +127,7 @@ typedef struct tqb_stage1_args {
     int32_t max_blocks_per_seq;
     const int32_t* seq_lens;     /* [B] */
     const float* centroids;      /* [n_centroids] fp32 Lloyd-Max codebook */
-    int32_t n_centroids;         /* must be 16 */
+    int32_t n_centroids;         /* 16 (4-bit keys) or 8 (3-bit keys); unused for e4m3 keys */
     const float* pair_lut;       /* optional [256, 2]; accepted, not needed */
     const int32_t* num_splits_per_seq; /* optional [B] */
     float* mid_o;                /* [B, Hq, S, D+1] fp32, unit inner stride */

@@ -34,6 +34,12 @@ LAYOUT_AOS = 1
 LAYOUT_SOA_K8 = 2  # turboquant_k8v4: [16][Hk][K128 e4m3 | V64] + [Hk][2][16] fp16 meta
 LAYOUT_SOA_K3 = 3  # turboquant_k3v4_nc: [16][Hk][K48 3-bit | V64] + [Hk][3][16] fp16 meta
 LAYOUT_SOA_K3V3 = 4  # turboquant_3bit_nc: [16][Hk][K48 3-bit | V48 3-bit] + [Hk][3][16] fp16 meta
+# AoS forms of the presets: one slot per (token, KV head), [key codes | fp16
+# raw norm (Lloyd-Max keys only) | value codes | fp16 vscale | fp16 vzero]
+LAYOUT_AOS_K8 = 5    # [K128 e4m3 | V64 | sc | zr] = 196 bytes
+LAYOUT_AOS_K3 = 6    # [K48 | norm | V64 | sc | zr] = 118 bytes
+LAYOUT_AOS_K3V3 = 7  # [K48 | norm | V48 | sc | zr] = 102 bytes
+AOS_PRESETS = (LAYOUT_AOS_K8, LAYOUT_AOS_K3, LAYOUT_AOS_K3V3)
 HEAD_DIM = 128
 BLOCK_SIZE = 16
 SLOT_BYTES = 134  # 64 K + 64 V + 3 fp16 metadata
@@ -298,12 +304,96 @@ def store_k3_np(y, norms, value, midpoints, centroids, slot_mapping, cache, vbit
                     np.float16(val).tobytes(), np.uint8)
 
 
+def _aos_geometry(layout):
+    """(key bytes, has norm, value bits) of an AoS preset slot."""
+    return {LAYOUT_AOS_K8: (128, False, 4), LAYOUT_AOS_K3: (48, True, 4), LAYOUT_AOS_K3V3: (48, True, 3)}[layout]
+
+
+def aos_slot_bytes(layout) -> int:
+    kb, has_norm, vbits = _aos_geometry(layout)
+    return kb + (2 if has_norm else 0) + HEAD_DIM * vbits // 8 + 4
+
+
+def _bucketize(y, mids, nc, steps):
+    """The reference store's binary search over the sorted midpoints,
+    ``y >= mid`` going right (reference/aos_store.py:280-295)."""
+    lo = np.zeros(y.shape, np.int64)
+    hi = np.full(y.shape, nc - 1, np.int64)
+    for _ in range(steps):
+        mid = (lo + hi) >> 1
+        right = y >= mids[np.minimum(mid, nc - 2)]
+        lo = np.where(right, mid + 1, lo)
+        hi = np.where(right, hi, mid)
+    return np.minimum(lo, nc - 1)
+
+
+def store_aos_np(layout, y, norms, value, midpoints, slot_mapping, cache):
+    """AoS store of the FP8-key and 3-bit presets (reference/aos_store.py:
+    145-219 FP8, :221-340 MSE with MSE_BITS = 3, values :26-116) into
+    ``cache [nb, 16, H, slot]`` in place.  ``y`` is the raw key for
+    ``LAYOUT_AOS_K8`` (cast to e4m3, nearest even, saturating) and the
+    rotated unit key for the 3-bit forms, whose slot stores the raw norm
+    fp16(|k|) (the decoder applies the norm correction)."""
+    kb, has_norm, vbits = _aos_geometry(layout)
+    D = HEAD_DIM
+    nb, bs, H, slot = cache.shape
+    y = np.asarray(y, np.float32).reshape(-1, H, D)
+    value = np.asarray(value, np.float32).reshape(-1, H, D)
+    if has_norm:
+        norms = np.asarray(norms, np.float32).reshape(-1, H)
+        mids = np.asarray(midpoints, np.float32)
+    voff = kb + (2 if has_norm else 0)
+    vbytes = D * vbits // 8
+    for t, s_ in enumerate(np.asarray(slot_mapping)):
+        if s_ < 0:
+            continue
+        blk, off = int(s_) // bs, int(s_) % bs
+        q, sc, zr = _quantise_value_np(value[t], vbits)
+        for h in range(H):
+            dst = cache[blk, off, h]
+            if layout == LAYOUT_AOS_K8:
+                dst[:kb] = e4m3_encode(y[t, h])
+            else:
+                dst[:kb] = _pack3(_bucketize(y[t, h], mids, 8, 3))
+                dst[kb:kb + 2] = np.frombuffer(np.float16(norms[t, h]).tobytes(), np.uint8)
+            dst[voff:voff + vbytes] = _pack3(q[h]) if vbits == 3 else q[h, 0::2] | (q[h, 1::2] << 4)
+            dst[voff + vbytes:voff + vbytes + 2] = np.frombuffer(sc[h].tobytes(), np.uint8)
+            dst[voff + vbytes + 2:voff + vbytes + 4] = np.frombuffer(zr[h].tobytes(), np.uint8)
+
+
+def _unpack3(b, n=HEAD_DIM):
+    """Little-endian 3-bit codes of the byte rows ``b [m, 3n/8]``."""
+    b = np.asarray(b, np.int64)
+    bit = 3 * np.arange(n)
+    b0, b1 = b[:, bit // 8], b[:, np.minimum(bit // 8 + 1, b.shape[1] - 1)]
+    return ((b0 | (b1 << 8)) >> (bit % 8)) & 7
+
+
 def decode_kv_np(cache, block_ids, offs, kvh, centroids, layout=LAYOUT_SOA):
     """Dequantise tokens (block_ids[i], offs[i]) of KV head ``kvh``.
     Returns ``K [n, D]`` (centroid*norm, norm correction applied for AoS) and
     ``V [n, D]`` in float64."""
     nb, bs, Hk, slot = cache.shape
     D = HEAD_DIM
+    if layout in AOS_PRESETS:
+        # reference/aos_decode.py:153-299: e4m3 keys as they are; 3-bit keys
+        # c[idx] / |c| * norm (NORM_CORRECTION); values code * scale + zero
+        kb, has_norm, vbits = _aos_geometry(layout)
+        slots = cache[block_ids, offs, kvh].astype(np.uint8)  # [n, slot]
+        voff = kb + (2 if has_norm else 0)
+        vbytes = D * vbits // 8
+        sc = slots[:, voff + vbytes:voff + vbytes + 2].copy().view(np.float16)[:, 0].astype(np.float64)
+        zr = slots[:, voff + vbytes + 2:voff + vbytes + 4].copy().view(np.float16)[:, 0].astype(np.float64)
+        vb = slots[:, voff:voff + vbytes]
+        vidx = (_unpack3(vb) if vbits == 3 else np.stack([vb & 0xF, vb >> 4], -1).reshape(-1, D)).astype(np.float64)
+        V = vidx * sc[:, None] + zr[:, None]
+        if layout == LAYOUT_AOS_K8:
+            return E4M3[slots[:, :kb]], V
+        c = np.asarray(centroids, np.float64)
+        kc = c[_unpack3(slots[:, :kb])]
+        kc = kc / np.sqrt((kc * kc).sum(-1, keepdims=True) + 1e-16)
+        knorm = slots[:, kb:kb + 2].copy().view(np.float16)[:, 0].astype(np.float64)
+        return kc * knorm[:, None], V
     flat = cache.reshape(nb, bs * Hk * slot)
     if layout == LAYOUT_SOA_K8:
         dps = D + D // 2  # 128 e4m3 key bytes + 64 V bytes

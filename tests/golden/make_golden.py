@@ -21,7 +21,9 @@ Reference kernels exercised (paths relative to the reference checkout):
   125-221``; SoA Stage1 with ``KEY_FP8=1``), 3-bit keys with 4-bit or 3-bit
   values (the MSE store with ``MSE_BITS=3`` / ``VQB=3``, ``:223-373``, and
   the SoA Stage1 with those constexprs), attention sinks (SoA Stage1 with
-  ``USE_SINKS=1``, ``reference/soa_decode_v1.py:134-145``)
+  ``USE_SINKS=1``, ``reference/soa_decode_v1.py:134-145``), and the AoS
+  forms of the three presets (``reference/aos_store.py:145-340``,
+  ``reference/aos_decode.py:43-313``)
 
 Note on FP8: the interpreter's float -> e4m3 cast rounds ties up, flushes
 subnormals and wraps on overflow, unlike the hardware cast the compiled
@@ -299,6 +301,82 @@ def build_k3_case(ref: Ref, name, *, seed, seq_lens, hq, hk, num_splits, pool_bl
                     num_splits=np.int32(num_splits), mid_o=mid, out_stage2=o2, lse_stage2=l2))
 
 
+def build_aos_preset_case(ref: Ref, name, *, preset, seed, seq_lens, hq, hk, num_splits, pool_blocks):
+    """AoS forms of the FP8-key and 3-bit presets: the reference AoS store
+    (``reference/aos_store.py:145-219`` FP8, ``:221-340`` MSE with
+    MSE_BITS=3, values ``:26-116``; slot = [key codes | raw fp16 norm (MSE
+    keys) | value codes | vscale | vzero]) and the reference AoS V1 Stage1
+    (``reference/aos_decode.py:43-313``) with KEY_FP8=1 (``preset="k8"``, the
+    fp16 query unrotated) or MSE_BITS=3 and VQB=4 / 3 (``"k3"`` / ``"k3v3"``,
+    NORM_CORRECTION=1), then Stage2.  The 3-bit cases also save the store
+    kernel's inputs as the reference launcher computes them
+    (``reference/aos_store.py:425-429``)."""
+    t0 = time.time()
+    fp8 = preset == "k8"
+    bits = 4 if fp8 else 3
+    vbits = 3 if preset == "k3v3" else 4
+    kbytes = HEAD_DIM if fp8 else HEAD_DIM * 3 // 8
+    kps = kbytes if fp8 else kbytes + 2
+    vbytes = HEAD_DIM * vbits // 8
+    slot = kps + vbytes + 4  # 196, 118 or 102
+    B = len(seq_lens)
+    g = torch.Generator().manual_seed(seed)
+    pages = [max(1, math.ceil(L / BLOCK_SIZE)) for L in seq_lens]
+    perm = torch.randperm(pool_blocks, generator=g)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]].to(torch.int32)
+        k += pages[b]
+    kv = torch.randint(0, 256, (pool_blocks, BLOCK_SIZE, hk, slot), generator=g, dtype=torch.uint8)
+    ntok = sum(seq_lens)
+    slots = []
+    for b in range(B):
+        for t in range(seq_lens[b]):
+            slots.append(int(bt[b, t // BLOCK_SIZE]) * BLOCK_SIZE + t % BLOCK_SIZE)
+    slot_mapping = torch.tensor(slots, dtype=torch.int32)
+    before = kv.clone()
+    cents = ref.centroids_mod.get_centroids(HEAD_DIM, bits).to(torch.float32)
+    mids = ((cents[:-1] + cents[1:]) * 0.5).contiguous()
+    sl = torch.tensor(seq_lens, dtype=torch.int32)
+    extra = {}
+    if fp8:
+        key = (torch.randn(ntok, hk, HEAD_DIM, generator=g) * 3.0).to(torch.float16)
+        val = torch.randn(ntok, hk, HEAD_DIM, generator=g).to(torch.float16)
+        ref.aos_store.triton_turboquant_store(key, val, kv, slot_mapping, torch.eye(HEAD_DIM), mids, bits, kps,
+                                              vbits, key_fp8=True)
+        q = (torch.randn(B, hq, HEAD_DIM, generator=g) * 0.5).to(torch.float16).float()
+        extra.update(key=key.float(), value=val.float(), query=q)
+    else:
+        R = orthogonal(seed + 1)
+        key = torch.randn(ntok, hk, HEAD_DIM, generator=g, dtype=torch.float32)
+        val = torch.randn(ntok, hk, HEAD_DIM, generator=g, dtype=torch.float32)
+        ref.aos_store.triton_turboquant_store(key, val, kv, slot_mapping, R, mids, bits, kps, vbits)
+        k_flat = key.reshape(ntok * hk, HEAD_DIM)
+        norms = k_flat.norm(dim=1, keepdim=True)
+        y = (k_flat / (norms + 1e-8)) @ R
+        q = (torch.randn(B, hq, HEAD_DIM, generator=g, dtype=torch.float32) @ R).contiguous()
+        extra.update(y=y, norms=norms.squeeze(1), value=val.reshape(ntok * hk, HEAD_DIM), rotation=R, q_rot=q)
+    print(f"[{name}] AoS store done {time.time() - t0:.1f}s", flush=True)
+    mid = torch.full((B, hq, num_splits, HEAD_DIM + 1), float("nan"), dtype=torch.float32)
+    ref.aos_dec._tq_decode_stage1[(B, hq, num_splits)](
+        q, kv, bt, sl, cents, mid,
+        q.stride(0), q.stride(1), kv.stride(0), kv.stride(1), kv.stride(2),
+        bt.stride(0), mid.stride(0), mid.stride(1), mid.stride(2),
+        NUM_KV_HEADS=hk, HEAD_DIM=HEAD_DIM, BLOCK_SIZE=BLOCK_SIZE,
+        NUM_KV_SPLITS=num_splits, KV_GROUP_SIZE=hq // hk,
+        MSE_BITS=bits, MSE_BYTES=HEAD_DIM * bits // 8, KPS=kps, VQB=vbits,
+        VAL_DATA_BYTES=vbytes, ATTN_SCALE=1.0 / math.sqrt(HEAD_DIM),
+        BLOCK_D=triton.next_power_of_2(HEAD_DIM), BLOCK_KV=4, KEY_FP8=1 if fp8 else 0,
+        NORM_CORRECTION=0 if fp8 else 1, FP8_E4B15=0, num_warps=1, num_stages=1,
+    )
+    print(f"[{name}] AoS V1 Stage1 done {time.time() - t0:.1f}s", flush=True)
+    o2, l2 = run_stage2(ref, mid, sl)
+    save(name, dict(slot_mapping=slot_mapping, cache_before=before, kv_cache=kv, centroids=cents,
+                    midpoints=mids, block_table=bt, seq_lens=sl, num_splits=np.int32(num_splits),
+                    mid_o=mid, out_stage2=o2, lse_stage2=l2, **extra))
+
+
 def run_aos_v1(ref: Ref, q_rot, kv, bt, seq_lens, cents, num_splits):
     B, Hq, D = q_rot.shape
     Hk = kv.shape[2]
@@ -517,9 +595,15 @@ CASES = {
 def main(argv):
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = Ref()
-    wanted = argv or list(CASES) + ["store", "k8v4_ragged", "k3v4_ragged", "k3v3_ragged"]
+    aos_presets = {"aos_k8v4_ragged": ("k8", 41), "aos_k3v4_ragged": ("k3", 43), "aos_k3v3_ragged": ("k3v3", 47)}
+    wanted = argv or list(CASES) + ["store", "k8v4_ragged", "k3v4_ragged", "k3v3_ragged"] + list(aos_presets)
     for name in wanted:
-        if name == "store":
+        if name in aos_presets:
+            # AoS forms of the presets: ragged lengths (an empty-split
+            # sequence, splits starting mid-page), GQA-4
+            build_aos_preset_case(ref, name, preset=aos_presets[name][0], seed=aos_presets[name][1],
+                                  seq_lens=[1, 45, 130], hq=16, hk=4, num_splits=4, pool_blocks=16)
+        elif name == "store":
             build_store_case(ref, "store_small", seed=99, ntok=48, hk=4, pool_blocks=5)
         elif name == "k3v4_ragged":
             # 3-bit keys, 4-bit values: ragged lengths, GQA-4

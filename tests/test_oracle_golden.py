@@ -211,3 +211,42 @@ def test_k3v3_oracle_against_reference():
     w = _written(ref)
     assert np.array_equal(~np.isnan(mid[..., 0]), w)
     assert np.abs(mid - ref)[w].max() <= ORACLE_ATOL
+
+
+@pytest.mark.parametrize("name,layout", [("aos_k8v4_ragged", O.LAYOUT_AOS_K8), ("aos_k3v4_ragged", O.LAYOUT_AOS_K3),
+                                         ("aos_k3v3_ragged", O.LAYOUT_AOS_K3V3)])
+def test_aos_presets_oracle_against_reference(name, layout):
+    """AoS forms of the FP8-key and 3-bit presets (reference/aos_store.py,
+    reference/aos_decode.py): the oracle's AoS store reproduces the
+    reference store's bytes (for FP8 keys: the value codes, scale and zero;
+    the key bytes are the hardware e4m3 cast, as for the SoA form, because
+    the interpreter's FP8 cast differs), and the Stage1 restatement matches
+    the reference AoS V1 Stage1 (KEY_FP8=1, or MSE_BITS=3 with VQB 4 / 3 and
+    the in-kernel norm correction)."""
+    import torch
+    from conftest import load_golden
+    z = load_golden(name)
+    cache = z["cache_before"].copy()
+    if layout == O.LAYOUT_AOS_K8:
+        O.store_aos_np(layout, z["key"], None, z["value"], None, z["slot_mapping"], cache)
+        got, ref = cache.copy(), z["kv_cache"]
+        assert np.array_equal(got[..., 128:], ref[..., 128:]), "value bytes / scale / zero differ"
+        sm = z["slot_mapping"]
+        for t in range(len(sm)):
+            blk, off = int(sm[t]) // 16, int(sm[t]) % 16
+            for h in range(cache.shape[2]):
+                k = torch.from_numpy(np.clip(z["key"][t, h], -448, 448)).to(torch.float8_e4m3fn)
+                assert np.array_equal(got[blk, off, h, :128], k.view(torch.uint8).numpy())
+        q = z["query"]
+    else:
+        O.store_aos_np(layout, z["y"], z["norms"], z["value"], z["midpoints"], z["slot_mapping"], cache)
+        assert np.array_equal(cache, z["kv_cache"]), f"{(cache != z['kv_cache']).sum()} bytes differ"
+        q = z["q_rot"]
+    mid = O.stage1_np(q, z["kv_cache"], z["block_table"], z["seq_lens"], z["centroids"], int(z["num_splits"]),
+                      layout=layout)
+    ref = z["mid_o"]
+    w = _written(ref)
+    assert np.array_equal(~np.isnan(mid[..., 0]), w)
+    assert (np.abs(mid - ref)[w] <= ORACLE_ATOL + 1e-6 * np.abs(ref)[w]).all(), np.abs(mid - ref)[w].max()
+    o2, l2 = O.stage2_np(ref, z["seq_lens"])
+    assert_close(o2, z["out_stage2"], atol=1e-6, rtol=0, what=f"stage2_np out ({name})")

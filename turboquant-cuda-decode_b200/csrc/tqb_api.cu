@@ -76,11 +76,11 @@ int report_launch(cudaError_t e) {
 // AoS slot strides (bytes): token-major ([16][Hk][slot], the reference's own
 // cache) or head-major ([Hk][16][slot]: vLLM's (blocks, H, N, C) storage seen
 // through kv_cache.transpose(1, 2), reference/turboquant_attn.py:565), with
-// every slot of a block inside the block stride.
-static bool aos_strides_ok(int64_t block, int64_t ps, int64_t hs, int64_t hk) {
-    const bool token_major = hs >= tqb::kSlotBytes && ps >= hk * hs;
-    const bool head_major = ps >= tqb::kSlotBytes && hs >= tqb::kBlockSize * ps;
-    const int64_t extent = (tqb::kBlockSize - 1) * ps + (hk - 1) * hs + tqb::kSlotBytes;
+// every slot (of `slot` bytes) of a block inside the block stride.
+static bool aos_strides_ok(int64_t block, int64_t ps, int64_t hs, int64_t hk, int64_t slot) {
+    const bool token_major = hs >= slot && ps >= hk * hs;
+    const bool head_major = ps >= slot && hs >= tqb::kBlockSize * ps;
+    const int64_t extent = (tqb::kBlockSize - 1) * ps + (hk - 1) * hs + slot;
     return (token_major || head_major) && block >= extent && extent < (int64_t(1) << 31);
 }
 
@@ -119,18 +119,19 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                 TQB_ERR_INVALID_ARG, "batch/heads/num_splits must be positive");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
+    TQB_REQUIRE(tqb::layout_valid(a->layout), TQB_ERR_INVALID_ARG, "layout must be a tqb_layout value");
     const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, v3 = a->layout == TQB_LAYOUT_SOA_K3V3;
     const bool k3 = a->layout == TQB_LAYOUT_SOA_K3 || v3;
-    TQB_REQUIRE(k8 || a->n_centroids == (k3 ? 8 : tqb::kNumCentroids), TQB_ERR_UNSUPPORTED,
-                "n_centroids must be 16 (4-bit keys) or 8 (3-bit keys)");
+    TQB_REQUIRE(tqb::layout_fp8_keys(a->layout) ||
+                    a->n_centroids == (tqb::layout_3bit_keys(a->layout) ? 8 : tqb::kNumCentroids),
+                TQB_ERR_UNSUPPORTED, "n_centroids must be 16 (4-bit keys) or 8 (3-bit keys)");
     TQB_REQUIRE(a->num_q_heads % a->num_kv_heads == 0, TQB_ERR_INVALID_ARG,
                 "num_q_heads must be a multiple of num_kv_heads");
     const int G = a->num_q_heads / a->num_kv_heads;
     TQB_REQUIRE(G <= 8, TQB_ERR_UNSUPPORTED, "GQA group size must be <= 8");
-    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8 || k3, TQB_ERR_INVALID_ARG,
-                "layout must be a tqb_layout value");
     if (a->batch == 0) return TQB_OK;
-    TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens && (a->centroids || k8) && a->mid_o,
+    TQB_REQUIRE(a->q_rot && a->kv_cache && a->block_table && a->seq_lens &&
+                    (a->centroids || tqb::layout_fp8_keys(a->layout)) && a->mid_o,
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
     TQB_REQUIRE(aligned(a->q_rot, 16) && a->q_stride_b % 4 == 0 && a->q_stride_h % 4 == 0,
                 TQB_ERR_ALIGNMENT, "q_rot must be 16-byte aligned with strides multiple of 4");
@@ -160,8 +161,11 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
         TQB_REQUIRE(aligned(a->kv_cache, 2) && a->cache_stride_block % 2 == 0 &&
                         a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0,
                     TQB_ERR_ALIGNMENT, "AoS cache pointer and strides must be even");
-        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk),
-                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134] slots, token- or head-major");
+        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk,
+                                   tqb::aos_slot_bytes(a->layout)),
+                    TQB_ERR_INVALID_ARG,
+                    "AoS strides must describe [blocks, 16, Hk, >= slot] slots (slot 134, 196, 118 or 102 bytes "
+                    "by layout), token- or head-major");
     }
     DeviceGuard guard(a->mid_o);
     TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
@@ -476,16 +480,16 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
                 "num_tokens must be >= 0 and num_kv_heads > 0");
     TQB_REQUIRE(a->head_dim == tqb::kHeadDim, TQB_ERR_UNSUPPORTED, "head_dim must be 128");
     TQB_REQUIRE(a->block_size == tqb::kBlockSize, TQB_ERR_UNSUPPORTED, "block_size must be 16");
+    TQB_REQUIRE(tqb::layout_valid(a->layout), TQB_ERR_INVALID_ARG, "layout must be a tqb_layout value");
     const bool k8 = a->layout == TQB_LAYOUT_SOA_K8, v3 = a->layout == TQB_LAYOUT_SOA_K3V3;
     const bool k3 = a->layout == TQB_LAYOUT_SOA_K3 || v3;
-    TQB_REQUIRE(k8 || a->n_centroids == (k3 ? 8 : tqb::kNumCentroids), TQB_ERR_UNSUPPORTED,
-                "n_centroids must be 16, or 8 for 3-bit keys");
-    TQB_REQUIRE(a->layout == TQB_LAYOUT_SOA || a->layout == TQB_LAYOUT_AOS || k8 || k3, TQB_ERR_INVALID_ARG,
-                "layout must be a tqb_layout value");
-    TQB_REQUIRE(!(k8 && a->norm_correction), TQB_ERR_INVALID_ARG,
-                "the FP8-key layout has no norm correction");
+    const bool fp8 = tqb::layout_fp8_keys(a->layout);
+    TQB_REQUIRE(fp8 || a->n_centroids == (tqb::layout_3bit_keys(a->layout) ? 8 : tqb::kNumCentroids),
+                TQB_ERR_UNSUPPORTED, "n_centroids must be 16, or 8 for 3-bit keys");
+    TQB_REQUIRE(!(fp8 && a->norm_correction), TQB_ERR_INVALID_ARG,
+                "the FP8-key layouts have no norm correction");
     if (a->num_tokens == 0) return TQB_OK;
-    TQB_REQUIRE(a->y && a->value && a->slot_mapping && a->kv_cache && (k8 || (a->norms && a->midpoints)),
+    TQB_REQUIRE(a->y && a->value && a->slot_mapping && a->kv_cache && (fp8 || (a->norms && a->midpoints)),
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
     TQB_REQUIRE(!a->norm_correction || a->centroids, TQB_ERR_INVALID_ARG,
                 "norm_correction requires centroids");
@@ -508,8 +512,11 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
     } else {
         TQB_REQUIRE(a->cache_stride_pos % 2 == 0 && a->cache_stride_head % 2 == 0, TQB_ERR_ALIGNMENT,
                     "AoS strides must be even");
-        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk),
-                    TQB_ERR_INVALID_ARG, "AoS strides must describe [blocks, 16, Hk, >=134] slots, token- or head-major");
+        TQB_REQUIRE(aos_strides_ok(a->cache_stride_block, a->cache_stride_pos, a->cache_stride_head, hk,
+                                   tqb::aos_slot_bytes(a->layout)),
+                    TQB_ERR_INVALID_ARG,
+                    "AoS strides must describe [blocks, 16, Hk, >= slot] slots (slot 134, 196, 118 or 102 bytes "
+                    "by layout), token- or head-major");
     }
     DeviceGuard guard(a->kv_cache);
     TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning kv_cache");

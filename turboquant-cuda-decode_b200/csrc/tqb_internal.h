@@ -9,6 +9,38 @@
 
 namespace tqb {
 
+// ---- cache layout traits (tqb_layout values) ------------------------------
+// Key codes: 4-bit Lloyd-Max (SOA, AOS), 3-bit Lloyd-Max (*_K3, *_K3V3) or
+// e4m3 bytes (*_K8); value codes 4-bit, or 3-bit for *_K3V3.
+__host__ __device__ constexpr bool layout_is_aos(int l) {
+    return l == TQB_LAYOUT_AOS || l == TQB_LAYOUT_AOS_K8 || l == TQB_LAYOUT_AOS_K3 || l == TQB_LAYOUT_AOS_K3V3;
+}
+__host__ __device__ constexpr bool layout_fp8_keys(int l) {
+    return l == TQB_LAYOUT_SOA_K8 || l == TQB_LAYOUT_AOS_K8;
+}
+__host__ __device__ constexpr bool layout_3bit_keys(int l) {
+    return l == TQB_LAYOUT_SOA_K3 || l == TQB_LAYOUT_SOA_K3V3 || l == TQB_LAYOUT_AOS_K3 || l == TQB_LAYOUT_AOS_K3V3;
+}
+__host__ __device__ constexpr bool layout_3bit_values(int l) {
+    return l == TQB_LAYOUT_SOA_K3V3 || l == TQB_LAYOUT_AOS_K3V3;
+}
+__host__ __device__ constexpr bool layout_valid(int l) { return l >= TQB_LAYOUT_SOA && l <= TQB_LAYOUT_AOS_K3V3; }
+// AoS cache slot, one per (token, KV head) (reference/aos_store.py:26-116,
+// :145-340): [key codes | fp16 key norm (Lloyd-Max keys only) | value codes |
+// fp16 value scale | fp16 value zero].  The stored norm is the raw |k|; the
+// decoder applies the norm correction c / |c| itself.
+__host__ __device__ constexpr int aos_key_bytes(int l) {
+    return layout_fp8_keys(l) ? 128 : layout_3bit_keys(l) ? 48 : 64;
+}
+__host__ __device__ constexpr int aos_norm_off(int l) { return aos_key_bytes(l); }  // absent for e4m3 keys
+__host__ __device__ constexpr int aos_val_off(int l) { return aos_key_bytes(l) + (layout_fp8_keys(l) ? 0 : 2); }
+__host__ __device__ constexpr int val_code_bytes(int l) { return layout_3bit_values(l) ? 48 : 64; }
+__host__ __device__ constexpr int aos_scale_off(int l) { return aos_val_off(l) + val_code_bytes(l); }
+__host__ __device__ constexpr int aos_slot_bytes(int l) { return aos_scale_off(l) + 4; }
+static_assert(aos_slot_bytes(TQB_LAYOUT_AOS) == 134 && aos_slot_bytes(TQB_LAYOUT_AOS_K8) == 196 &&
+                  aos_slot_bytes(TQB_LAYOUT_AOS_K3) == 118 && aos_slot_bytes(TQB_LAYOUT_AOS_K3V3) == 102,
+              "AoS slot sizes of the reference presets");
+
 // Division of 32-bit unsigned n < 2^31 by a fixed divisor d >= 1 with a
 // multiply-high and a shift (Granlund & Montgomery, "Division by invariant
 // integers using multiplication", 1994): with l = ceil(log2 d) and

@@ -157,11 +157,17 @@ __device__ __forceinline__ LaneOffsets lane_offsets(const Stage1Params& P, int k
         o.v0 = (4 * c) * tok + head + kKBytes + 8 * g;
         o.meta = kBlockSize * tok + (uint32_t)kvh * (3 * kBlockSize * 2) + 4 * g;
     } else {
+        // AoS slot [key codes | fp16 norm | value codes | fp16 vscale | vzero]
+        // (layout_is_aos): keys of dims 32c .. 32c+31 are 16 bytes (4-bit), 12
+        // (3-bit) or 32 (e4m3) at that multiple of c; values of dims 16g ..
+        // 16g+15 are 8 bytes (4-bit) or 6 (3-bit).
         const uint32_t pos = (uint32_t)P.pos_stride, hs = (uint32_t)P.head_stride * kvh;
+        constexpr uint32_t kKeyLane = layout_fp8_keys(LAYOUT) ? 32 : layout_3bit_keys(LAYOUT) ? 12 : 16;
+        constexpr uint32_t kValLane = layout_3bit_values(LAYOUT) ? 6 : 8;
         o.row = pos;
-        o.k0 = (2 * g) * pos + hs + 16 * c;
-        o.v0 = (4 * c) * pos + hs + kKBytes + 2 + 8 * g;
-        o.meta = (2 * g) * pos + hs + kKBytes;
+        o.k0 = (2 * g) * pos + hs + kKeyLane * c;
+        o.v0 = (4 * c) * pos + hs + aos_val_off(LAYOUT) + kValLane * g;
+        o.meta = (2 * g) * pos + hs + aos_norm_off(LAYOUT);
     }
     return o;
 }
@@ -255,20 +261,40 @@ __device__ __forceinline__ void load_page(PageRegs& r, const uint8_t* base, cons
         r.vs = ld_stream_u32(m + 2 * kBlockSize);
         r.vz = ld_stream_u32(m + 4 * kBlockSize);
     } else {
+        // AoS slots are only 2-byte aligned: 16-bit gathers.
         const uint8_t* s0 = base + o.k0;
         const uint8_t* s1 = s0 + o.row;
-        r.k0 = make_uint4(ld2x16(s0), ld2x16(s0 + 4), ld2x16(s0 + 8), ld2x16(s0 + 12));
-        r.k1 = make_uint4(ld2x16(s1), ld2x16(s1 + 4), ld2x16(s1 + 8), ld2x16(s1 + 12));
+        if (layout_fp8_keys(LAYOUT)) {
+            r.k0 = make_uint4(ld2x16(s0), ld2x16(s0 + 4), ld2x16(s0 + 8), ld2x16(s0 + 12));
+            r.k0b = make_uint4(ld2x16(s0 + 16), ld2x16(s0 + 20), ld2x16(s0 + 24), ld2x16(s0 + 28));
+            r.k1 = make_uint4(ld2x16(s1), ld2x16(s1 + 4), ld2x16(s1 + 8), ld2x16(s1 + 12));
+            r.k1b = make_uint4(ld2x16(s1 + 16), ld2x16(s1 + 20), ld2x16(s1 + 24), ld2x16(s1 + 28));
+        } else if (layout_3bit_keys(LAYOUT)) {
+            r.k0 = make_uint4(ld2x16(s0), ld2x16(s0 + 4), ld2x16(s0 + 8), 0u);
+            r.k1 = make_uint4(ld2x16(s1), ld2x16(s1 + 4), ld2x16(s1 + 8), 0u);
+        } else {
+            r.k0 = make_uint4(ld2x16(s0), ld2x16(s0 + 4), ld2x16(s0 + 8), ld2x16(s0 + 12));
+            r.k1 = make_uint4(ld2x16(s1), ld2x16(s1 + 4), ld2x16(s1 + 8), ld2x16(s1 + 12));
+        }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const uint8_t* sv = base + o.v0 + j * o.row;
-            r.v[j] = make_uint2(ld2x16(sv), ld2x16(sv + 4));
+            if (layout_3bit_values(LAYOUT)) {
+                // 16 3-bit codes (6 bytes) spread to the nibble layout of the
+                // 4-bit values (low nibble = even dim)
+                const uint32_t a = ld_stream_u16(sv), b = ld_stream_u16(sv + 2), cc = ld_stream_u16(sv + 4);
+                r.v[j] = make_uint2(spread3to4((a | (b << 16)) & 0xFFFFFFu), spread3to4((b >> 8) | (cc << 8)));
+            } else {
+                r.v[j] = make_uint2(ld2x16(sv), ld2x16(sv + 4));
+            }
         }
         const uint8_t* m0 = base + o.meta;
         const uint8_t* m1 = m0 + o.row;
-        r.kn = ld_stream_u16(m0) | (ld_stream_u16(m1) << 16);
-        r.vs = ld_stream_u16(m0 + 2 + kVBytes) | (ld_stream_u16(m1 + 2 + kVBytes) << 16);
-        r.vz = ld_stream_u16(m0 + 4 + kVBytes) | (ld_stream_u16(m1 + 4 + kVBytes) << 16);
+        constexpr int kSc = aos_scale_off(LAYOUT) - aos_norm_off(LAYOUT);  // scale, relative to the norm
+        r.kn = layout_fp8_keys(LAYOUT) ? 0x3C003C00u  // no key norm: fp16 1.0 for both tokens
+                                       : (ld_stream_u16(m0) | (ld_stream_u16(m1) << 16));
+        r.vs = ld_stream_u16(m0 + kSc) | (ld_stream_u16(m1 + kSc) << 16);
+        r.vz = ld_stream_u16(m0 + kSc + 2) | (ld_stream_u16(m1 + kSc + 2) << 16);
     }
 }
 
@@ -312,7 +338,10 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
 #pragma unroll
             for (int k = 0; k < 4; k++) dq[nt][mt][k] = 0.0f;
     float csq0 = 0.0f, csq1 = 0.0f;  // AoS: partial sums of c^2
-    if (LAYOUT == TQB_LAYOUT_SOA_K8) {
+    // AoS Lloyd-Max keys: the table entries carry the squared centroid sums
+    // for the in-kernel norm correction.
+    constexpr bool kNormCorr = layout_is_aos(LAYOUT) && !layout_fp8_keys(LAYOUT);
+    if (layout_fp8_keys(LAYOUT)) {
         // FP8 keys convert exactly to fp16, so one M tile holds the whole
         // page: row g = token 2g, row g+8 = token 2g+1; k columns map to the
         // same dims 32c + 4ks + {0,1 | 2,3} as the query fragments.  Even and
@@ -334,7 +363,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
         // (byte << 8) | this lane's copy offset, in one PRMT
         uint32_t ia, ib, ic, id;
-        if (LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3) {
+        if (layout_3bit_keys(LAYOUT)) {
             // 3-bit keys: the dim pairs 32c + 4ks + {0,1} and {2,3} are the
             // 6-bit fields at bits 12ks and 12ks + 6 of the lane's 96 bits;
             // entry (pair << 8) + this lane's copy offset, as below.
@@ -349,7 +378,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
             id = prmt(w1, lut_sel_src, 0x5504u | (jB << 4));
         }
         uint2 e0, e1, e2, e3;
-        if (LAYOUT != TQB_LAYOUT_AOS) {
+        if (!kNormCorr) {
             e0 = lut_v2(lut, ia);
             e1 = lut_v2(lut, ib);
             e2 = lut_v2(lut, ic);
@@ -374,7 +403,7 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
     }
     }  // 4-bit keys
     float kn0 = half_bits_to_float(cur.kn), kn1 = half_bits_to_float(cur.kn >> 16);
-    if (LAYOUT == TQB_LAYOUT_AOS) {
+    if (kNormCorr) {
         // Norm correction c / |c| (reference/aos_decode.py:199-206).
         csq0 = warp_sum_xor(csq0, 1, 2);
         csq1 = warp_sum_xor(csq1, 1, 2);
@@ -396,10 +425,10 @@ __device__ __forceinline__ void process_page(ItemState<NT>& st, const PageRegs& 
         // C_hi / C_lo parts of the token
         // FP8 keys: columns 2c / 2c+1 = Q_hi / Q_lo of head c, rows g / g+8
         // = tokens 2g / 2g+1, chains ks even / odd
-        const float d0 = LAYOUT == TQB_LAYOUT_SOA_K8
+        const float d0 = layout_fp8_keys(LAYOUT)
                              ? (dq[nt][0][0] + dq[nt][0][1]) + (dq[nt][1][0] + dq[nt][1][1])
                              : (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
-        const float d1 = LAYOUT == TQB_LAYOUT_SOA_K8
+        const float d1 = layout_fp8_keys(LAYOUT)
                              ? (dq[nt][0][2] + dq[nt][0][3]) + (dq[nt][1][2] + dq[nt][1][3])
                              : (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
         float s0 = d0 * kn0 * st.kfac[nt];
@@ -480,7 +509,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     // copies of {C_hi pair, C_lo pair}; AoS keeps 16 copies that also carry
     // the byte's squared centroid sum for the in-kernel norm correction),
     // then one output staging row set per warp.
-    constexpr int kEntry = LAYOUT == TQB_LAYOUT_AOS ? 16 : 8;
+    constexpr bool kNormCorr = layout_is_aos(LAYOUT) && !layout_fp8_keys(LAYOUT);
+    constexpr bool kFp8 = layout_fp8_keys(LAYOUT);
+    constexpr int kEntry = kNormCorr ? 16 : 8;
     constexpr int kCopies = kLutStride / kEntry;
     extern __shared__ __align__(1024) uint8_t smem[];
     float* stage_all = reinterpret_cast<float*>(smem + kLutBytes);
@@ -492,25 +523,25 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     // ---- centroid table -------------------------------------------------
     // (FP8 keys need no table: their fp16 form is exact, scale exponent 0.)
     // 3-bit keys: 8 centroids, table entries for the 64 6-bit dim pairs.
-    constexpr bool kKey3 = LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3;
+    constexpr bool kKey3 = layout_3bit_keys(LAYOUT);
     constexpr int kNc = kKey3 ? 8 : kNumCentroids;
     constexpr int kPairs = kKey3 ? 64 : 256;
     constexpr int kLowBits = kKey3 ? 3 : 4;
     float cmax = 0.0f;
-    if (LAYOUT != TQB_LAYOUT_SOA_K8) {
+    if (!kFp8) {
 #pragma unroll
         for (int k = 0; k < kNc; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     }
-    const int ec = LAYOUT == TQB_LAYOUT_SOA_K8 ? 0 : fp16_scale_exp(cmax);
+    const int ec = kFp8 ? 0 : fp16_scale_exp(cmax);
     const float cscale = exp2i(ec);
-    for (int e = tid; LAYOUT != TQB_LAYOUT_SOA_K8 && e < kPairs * kCopies; e += kThreads) {
+    for (int e = tid; !kFp8 && e < kPairs * kCopies; e += kThreads) {
         const int byte = e / kCopies;
         const float a = __ldg(P.cents + (byte & (kNc - 1))), b = __ldg(P.cents + (byte >> kLowBits));
         const float clo = a * cscale, chi = b * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
         uint8_t* dst = smem + (size_t)e * kEntry;
-        if (LAYOUT != TQB_LAYOUT_AOS) {
+        if (!kNormCorr) {
             *reinterpret_cast<uint2*>(dst) = make_uint2(h2_as_u32(h), h2_as_u32(l));
         } else {
             *reinterpret_cast<uint4*>(dst) =
@@ -735,6 +766,19 @@ int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     if (stage1_ring_supported(P) && !force_register_kernel()) {
         const int rc = launch_stage1_ring(P, stream, num_sms);
         if (rc != TQB_ERR_UNSUPPORTED) return rc;  // else: tensor maps refused, use the register kernel
+    }
+    switch (P.layout) {
+        case TQB_LAYOUT_AOS_K8:
+            return P.G <= 4 ? launch_t<1, TQB_LAYOUT_AOS_K8>(P, stream, num_sms)
+                            : launch_t<2, TQB_LAYOUT_AOS_K8>(P, stream, num_sms);
+        case TQB_LAYOUT_AOS_K3:
+            return P.G <= 4 ? launch_t<1, TQB_LAYOUT_AOS_K3>(P, stream, num_sms)
+                            : launch_t<2, TQB_LAYOUT_AOS_K3>(P, stream, num_sms);
+        case TQB_LAYOUT_AOS_K3V3:
+            return P.G <= 4 ? launch_t<1, TQB_LAYOUT_AOS_K3V3>(P, stream, num_sms)
+                            : launch_t<2, TQB_LAYOUT_AOS_K3V3>(P, stream, num_sms);
+        default:
+            break;
     }
     if (P.layout == TQB_LAYOUT_SOA_K8)
         return P.G <= 4 ? launch_t<1, TQB_LAYOUT_SOA_K8>(P, stream, num_sms)

@@ -1,4 +1,4 @@
-// tqb_store.cu — sm_100a TurboQuant 4bit_nc cache store.
+// tqb_store.cu — sm_100a TurboQuant cache store (all presets, SoA and AoS).
 //
 // Reference: _tq_fused_store_mse in reference/soa_store.py:223-373 (SoA) and
 // reference/aos_store.py:221-340 (AoS).  One warp per token-head, each lane
@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     const int64_t blk = slot / kBlockSize, off = slot % kBlockSize;
 
     const float4 yv = __ldg(reinterpret_cast<const float4*>(P.y + pid * kHeadDim) + lane);
-    const bool k8 = P.layout == TQB_LAYOUT_SOA_K8;
+    const bool k8 = layout_fp8_keys(P.layout);
+    const bool k3 = layout_3bit_keys(P.layout);
     uint32_t kpack = 0;
     float vn = 0.0f;
     if (k8) {
@@ -53,7 +54,6 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     const float ys[4] = {yv.x, yv.y, yv.z, yv.w};
     // 3-bit keys: 8 centroids, 3 search steps (reference/soa_store.py:305-314
     // with MSE_BITS = 3)
-    const bool k3 = P.layout == TQB_LAYOUT_SOA_K3 || P.layout == TQB_LAYOUT_SOA_K3V3;
     const int nc = k3 ? 8 : kNumCentroids, steps = k3 ? 3 : 4;
     int idx[4];
 #pragma unroll
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     }
     // 3-bit values (reference/soa_store.py:49-84): 7 levels, codes packed
     // little-endian at bit 3d; 4-bit: 15 levels, two codes per byte.
-    const bool v3 = P.layout == TQB_LAYOUT_SOA_K3V3;
+    const bool v3 = layout_3bit_values(P.layout);
     const int vtop = v3 ? 7 : 15;
     float scale = __fdiv_rn(__fsub_rn(vmax, vmin), v3 ? 7.0f : 15.0f);
     scale = scale > 1e-8f ? scale : 1e-8f;
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
     const unsigned short vn_h = __half_as_ushort(__float2half_rn(vn));
     const unsigned short sc_h = __half_as_ushort(__float2half_rn(scale));
     const unsigned short zr_h = __half_as_ushort(__float2half_rn(vmin));
-    if (k8) {
+    if (P.layout == TQB_LAYOUT_SOA_K8) {
         uint8_t* dp = base + off * ((int64_t)P.H * kK8DataBytes) + (int64_t)h * kK8DataBytes;
         reinterpret_cast<uint32_t*>(dp)[lane] = kpack;  // dims 4 lane .. 4 lane + 3
         reinterpret_cast<unsigned short*>(dp + kK8KeyBytes)[lane] = (unsigned short)vpack;
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
             meta[off] = sc_h;
             meta[kBlockSize + off] = zr_h;
         }
-    } else if (v3) {
+    } else if (P.layout == TQB_LAYOUT_SOA_K3V3) {
         uint8_t* dp = base + off * ((int64_t)P.H * kK3V3DataBytes) + (int64_t)h * kK3V3DataBytes;
         // keys and values: lanes 2m and 2m+1 hold dims 8m .. 8m+7, bytes
         // 3m .. 3m+2 of each 48-byte stream
@@ -191,15 +191,44 @@ __global__ void __launch_bounds__(kStoreWarps * 32) store_kernel(const StorePara
             meta[2 * kBlockSize + off] = zr_h;
         }
     } else {
+        // AoS slot (layout_is_aos): [key codes | fp16 norm | value codes |
+        // fp16 scale | fp16 zero], 2-byte aligned, so 16-bit and byte stores
+        // (reference/aos_store.py:26-116, :183-203, :296-325).
         uint8_t* sp = base + off * P.pos_stride + (int64_t)h * P.head_stride;
-        reinterpret_cast<unsigned short*>(sp)[lane] = (unsigned short)kpack;
-        reinterpret_cast<unsigned short*>(sp + kKBytes + 2)[lane] = (unsigned short)vpack;
+        const int L = P.layout;
+        const uint32_t kup = __shfl_down_sync(0xffffffffu, kpack, 1);
+        const uint32_t vup = __shfl_down_sync(0xffffffffu, vpack, 1);
+        if (k8) {  // e4m3 bytes of dims 4 lane .. 4 lane + 3
+            reinterpret_cast<unsigned short*>(sp)[2 * lane] = (unsigned short)kpack;
+            reinterpret_cast<unsigned short*>(sp)[2 * lane + 1] = (unsigned short)(kpack >> 16);
+        } else if (k3) {  // lanes 2m and 2m+1: bytes 3m .. 3m+2 of the 3-bit stream
+            if ((lane & 1) == 0) {
+                const uint32_t k24 = kpack | (kup << 12);
+                uint8_t* kb = sp + 3 * (lane >> 1);
+                kb[0] = (uint8_t)k24; kb[1] = (uint8_t)(k24 >> 8); kb[2] = (uint8_t)(k24 >> 16);
+            }
+        } else {
+            reinterpret_cast<unsigned short*>(sp)[lane] = (unsigned short)kpack;
+        }
+        uint8_t* vp = sp + aos_val_off(L);
+        if (v3) {
+            if ((lane & 1) == 0) {
+                const uint32_t v24 = vpack | (vup << 12);
+                uint8_t* vb = vp + 3 * (lane >> 1);
+                vb[0] = (uint8_t)v24; vb[1] = (uint8_t)(v24 >> 8); vb[2] = (uint8_t)(v24 >> 16);
+            }
+        } else {
+            reinterpret_cast<unsigned short*>(vp)[lane] = (unsigned short)vpack;
+        }
         if (lane == 0) {
-            // AoS stores the raw norm (no folding, reference/aos_store.py:317-325).
-            const unsigned short raw = __half_as_ushort(__float2half_rn(__ldg(P.norms + pid)));
-            reinterpret_cast<unsigned short*>(sp + kKBytes)[0] = raw;
-            reinterpret_cast<unsigned short*>(sp + kKBytes + 2 + kVBytes)[0] = sc_h;
-            reinterpret_cast<unsigned short*>(sp + kKBytes + 4 + kVBytes)[0] = zr_h;
+            // AoS stores the raw norm (no folding, reference/aos_store.py:317-325);
+            // e4m3 keys have none.
+            if (!k8) {
+                const unsigned short raw = __half_as_ushort(__float2half_rn(__ldg(P.norms + pid)));
+                reinterpret_cast<unsigned short*>(sp + aos_norm_off(L))[0] = raw;
+            }
+            reinterpret_cast<unsigned short*>(sp + aos_scale_off(L))[0] = sc_h;
+            reinterpret_cast<unsigned short*>(sp + aos_scale_off(L) + 2)[0] = zr_h;
         }
     }
 }

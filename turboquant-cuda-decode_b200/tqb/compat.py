@@ -141,18 +141,21 @@ def triton_turboquant_decode_attention(
                             max_num_kv_splits=max_num_kv_splits, sinks=sinks)
 
 
-def _preset_layout(key_fp8: bool, mse_bits: int, value_quant_bits: int) -> str:
-    """Cache layout of a TurboQuant preset (reference/config.py:20-41)."""
+def _preset_layout(key_fp8: bool, mse_bits: int, value_quant_bits: int, family: str = "soa") -> str:
+    """Cache layout of a TurboQuant preset (reference/config.py:20-41) in the
+    SoA or AoS ``family``."""
     if key_fp8 and value_quant_bits == 4:
-        return "soa_k8"        # turboquant_k8v4
-    if not key_fp8 and mse_bits == 4 and value_quant_bits == 4:
-        return "soa"           # turboquant_4bit_nc
-    if not key_fp8 and mse_bits == 3 and value_quant_bits == 4:
-        return "soa_k3"        # turboquant_k3v4_nc
-    if not key_fp8 and mse_bits == 3 and value_quant_bits == 3:
-        return "soa_k3v3"      # turboquant_3bit_nc
-    raise NotImplementedError(f"no TurboQuant preset with key_fp8={key_fp8}, mse_bits={mse_bits}, "
-                              f"value_quant_bits={value_quant_bits}")
+        suffix = "_k8"         # turboquant_k8v4
+    elif not key_fp8 and mse_bits == 4 and value_quant_bits == 4:
+        suffix = ""            # turboquant_4bit_nc
+    elif not key_fp8 and mse_bits == 3 and value_quant_bits == 4:
+        suffix = "_k3"         # turboquant_k3v4_nc
+    elif not key_fp8 and mse_bits == 3 and value_quant_bits == 3:
+        suffix = "_k3v3"       # turboquant_3bit_nc
+    else:
+        raise NotImplementedError(f"no TurboQuant preset with key_fp8={key_fp8}, mse_bits={mse_bits}, "
+                                  f"value_quant_bits={value_quant_bits}")
+    return family + suffix
 
 
 def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, *, PiT=None,
@@ -163,7 +166,7 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
     both reference launchers (reference/soa_decode_v1.py:486-643,
     reference/aos_decode.py:486-...) with the buffer reuse they offer."""
     B, Hq, D = query.shape
-    if layout in ("soa_k8", "k8v4"):
+    if layout in ("soa_k8", "k8v4", "aos_k8"):
         # FP8 keys score against the query itself, read as fp32
         # (reference/soa_decode_v1.py:532-533)
         q_rot = query.float().contiguous()
@@ -230,15 +233,16 @@ def triton_turboquant_store(
     part (norm, normalise, rotation GEMM) is the reference launcher's
     (reference/soa_store.py:482-487); the quantise/pack kernel is sm_100a.
     ``key_fp8=True`` (``turboquant_k8v4``) casts the raw key to e4m3 in the
-    kernel, SoA layout with 196 bytes per token-head
-    (reference/soa_store.py:446-479)."""
-    preset = _preset_layout(key_fp8, mse_bits, value_quant_bits)
-    if preset != "soa":
-        layout = preset  # the other presets' caches are SoA only
+    kernel, 196 bytes per token-head (reference/soa_store.py:446-479,
+    reference/aos_store.py:386-412).  ``layout="aos"`` writes the AoS slot
+    form of the preset (reference/aos_store.py:350-447), storing the raw key
+    norm."""
+    family = "aos" if str(layout).lower().startswith("aos") else "soa"
+    layout = _preset_layout(key_fp8, mse_bits, value_quant_bits, family)
     N, H, D = key.shape
     if key_fp8:
         ops.store(key.float().reshape(N * H, D).contiguous(), None, value.float().reshape(N * H, D).contiguous(),
-                  kv_cache, slot_mapping, None, None, layout="soa_k8", norm_correction=False)
+                  kv_cache, slot_mapping, None, None, layout=layout, norm_correction=False)
         return
     k_flat = key.float().reshape(N * H, D)
     norms = k_flat.norm(dim=1, keepdim=True)

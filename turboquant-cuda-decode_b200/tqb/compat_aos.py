@@ -6,10 +6,13 @@ site that imports the AoS one switches to::
 
     from tqb.compat_aos import triton_turboquant_decode_attention
 
-The AoS Stage1 kernels implement the norm-corrected decode of the
-``turboquant_4bit_nc`` preset (the reference's ``NORM_CORRECTION=1``, as
-``baseline/triton_v1.py`` launches it); other presets raise
-``NotImplementedError``.
+Every preset of ``reference/config.py:20-41`` is served on its AoS slot
+layout: ``turboquant_4bit_nc`` (the default), FP8 keys (``key_fp8=True``,
+``turboquant_k8v4``), 3-bit keys with 4-bit or 3-bit values (``mse_bits=3``,
+``turboquant_k3v4_nc`` / ``turboquant_3bit_nc``).  The Lloyd-Max presets
+are decoded with the in-kernel norm correction (the reference's
+``NORM_CORRECTION=1``, as ``baseline/triton_v1.py`` launches it), so
+``norm_correction=False`` raises ``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -18,7 +21,7 @@ from typing import Any, Optional
 
 import torch
 
-from .compat import decode_attention
+from .compat import _preset_layout, decode_attention
 
 
 def triton_turboquant_decode_attention(
@@ -41,14 +44,13 @@ def triton_turboquant_decode_attention(
     buf_holder: Any = None,
     max_num_kv_splits: int = 32,
 ) -> torch.Tensor:
-    """Decode over an AoS cache ``[num_blocks, 16, Hk, 134]``; returns
-    ``[B, Hq, D]`` in the query's dtype."""
-    if key_fp8 or mse_bits != 4 or value_quant_bits != 4:
-        raise NotImplementedError("the AoS cache serves the turboquant_4bit_nc preset; the FP8-key and 3-bit "
-                                  "presets use the SoA cache (tqb.compat.triton_turboquant_decode_attention)")
-    if not norm_correction:
+    """Decode over an AoS cache ``[num_blocks, 16, Hk, slot]`` (slot 134,
+    196, 118 or 102 bytes by preset); returns ``[B, Hq, D]`` in the query's
+    dtype."""
+    layout = _preset_layout(key_fp8, mse_bits, value_quant_bits, "aos")
+    if not key_fp8 and not norm_correction:
         raise NotImplementedError("the AoS kernels implement the norm-corrected decode (norm_correction=True) "
-                                  "of the turboquant_4bit_nc preset")
-    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, "aos", PiT=PiT,
+                                  "of the Lloyd-Max presets")
+    return decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scale, layout, PiT=PiT,
                             mid_o_buf=mid_o_buf, output_buf=output_buf, lse_buf=lse_buf, buf_holder=buf_holder,
                             max_num_kv_splits=max_num_kv_splits)

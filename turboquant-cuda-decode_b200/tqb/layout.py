@@ -50,6 +50,18 @@ K3_SLOT_SIZE = K3_KEY_BYTES + VAL_DATA_BYTES + 6  # 118
 # turboquant_3bit_nc: 3-bit keys and 3-bit values (48 + 48 B), same meta
 LAYOUT_SOA_K3V3 = 4
 K3V3_SLOT_SIZE = K3_KEY_BYTES + HEAD_DIM * 3 // 8 + 6  # 102
+# AoS forms of the three presets (reference/aos_store.py:26-340): one slot per
+# (token, KV head), [key codes | raw fp16 norm (Lloyd-Max keys) | value codes
+# | fp16 vscale | fp16 vzero], the same byte counts as their SoA forms
+LAYOUT_AOS_K8 = 5    # 128 e4m3 key bytes, no norm, 64 value bytes: 196
+LAYOUT_AOS_K3 = 6    # 48 key bytes, norm, 64 value bytes: 118
+LAYOUT_AOS_K3V3 = 7  # 48 key bytes, norm, 48 value bytes: 102
+AOS_FAMILY = (LAYOUT_AOS, LAYOUT_AOS_K8, LAYOUT_AOS_K3, LAYOUT_AOS_K3V3)
+FP8_KEY_LAYOUTS = (LAYOUT_SOA_K8, LAYOUT_AOS_K8)
+KEY3_LAYOUTS = (LAYOUT_SOA_K3, LAYOUT_SOA_K3V3, LAYOUT_AOS_K3, LAYOUT_AOS_K3V3)
+SLOT_BYTES = {LAYOUT_SOA: SLOT_SIZE, LAYOUT_AOS: SLOT_SIZE, LAYOUT_SOA_K8: K8_SLOT_SIZE,
+              LAYOUT_SOA_K3: K3_SLOT_SIZE, LAYOUT_SOA_K3V3: K3V3_SLOT_SIZE, LAYOUT_AOS_K8: K8_SLOT_SIZE,
+              LAYOUT_AOS_K3: K3_SLOT_SIZE, LAYOUT_AOS_K3V3: K3V3_SLOT_SIZE}
 
 
 def layout_id(layout) -> int:
@@ -63,7 +75,14 @@ def layout_id(layout) -> int:
         return LAYOUT_SOA_K3
     if layout in (LAYOUT_SOA_K3V3, "soa_k3v3", "3bit"):
         return LAYOUT_SOA_K3V3
-    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos', 'soa_k8', 'soa_k3' or 'soa_k3v3')")
+    if layout in (LAYOUT_AOS_K8, "aos_k8"):
+        return LAYOUT_AOS_K8
+    if layout in (LAYOUT_AOS_K3, "aos_k3"):
+        return LAYOUT_AOS_K3
+    if layout in (LAYOUT_AOS_K3V3, "aos_k3v3"):
+        return LAYOUT_AOS_K3V3
+    raise ValueError(f"unknown cache layout {layout!r} (expected 'soa', 'aos', 'soa_k8', 'soa_k3', 'soa_k3v3', "
+                     "'aos_k8', 'aos_k3' or 'aos_k3v3')")
 
 
 def block_bytes(num_kv_heads: int, block_size: int = BLOCK_SIZE) -> int:

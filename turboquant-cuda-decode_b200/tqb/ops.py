@@ -17,8 +17,8 @@ import torch
 
 from . import _lib
 from ._lib import MergeArgs, RotateArgs, SinkArgs, Stage1Args, Stage2Args, StoreArgs, TqbError
-from .layout import (BLOCK_SIZE, HEAD_DIM, LAYOUT_AOS, LAYOUT_SOA, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3, LAYOUT_SOA_K8,
-                     layout_id)
+from .layout import (BLOCK_SIZE, FP8_KEY_LAYOUTS, HEAD_DIM, KEY3_LAYOUTS, LAYOUT_AOS, LAYOUT_SOA, LAYOUT_SOA_K3,
+                     LAYOUT_SOA_K3V3, LAYOUT_SOA_K8, layout_id)
 
 _SOA_FAMILY = (LAYOUT_SOA, LAYOUT_SOA_K8, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3)  # block-as-raw-bytes layouts
 
@@ -81,7 +81,7 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     _cuda(kv_cache, "kv_cache", torch.uint8)
     _cuda(block_table, "block_table", torch.int32)
     _cuda(seq_lens, "seq_lens", torch.int32)
-    if centroids is not None or lay != LAYOUT_SOA_K8:  # FP8 keys use no centroids
+    if centroids is not None or lay not in FP8_KEY_LAYOUTS:  # FP8 keys use no centroids
         _cuda(centroids, "centroids", torch.float32)
     _cuda(mid_o, "mid_o", torch.float32)
     _require(q_rot.dim() == 3 and q_rot.stride(2) == 1, "q_rot must be [B, Hq, D] with unit inner stride")
@@ -259,10 +259,12 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
           layout="soa", norm_correction: bool = True, stream: Optional[int] = None) -> None:
     """Quantise ``N*H`` token-heads into the cache (kernel stage of the
     reference store; ``y``/``norms``/``value`` are its inputs).  With
-    ``layout="soa_k8"`` (FP8 keys) ``y`` is the raw key, cast to e4m3, and
-    ``norms``/``midpoints``/``centroids`` are unused (may be None)."""
+    ``layout="soa_k8"`` or ``"aos_k8"`` (FP8 keys) ``y`` is the raw key, cast
+    to e4m3, and ``norms``/``midpoints``/``centroids`` are unused (may be
+    None).  AoS layouts store the raw norm (their decoders apply the norm
+    correction), so ``norm_correction`` only affects the SoA layouts."""
     lay = layout_id(layout)
-    k8 = lay == LAYOUT_SOA_K8
+    k8 = lay in FP8_KEY_LAYOUTS
     _cuda(y, "y", torch.float32)
     _cuda(value, "value", torch.float32)
     _cuda(kv_cache, "kv_cache", torch.uint8)
@@ -296,7 +298,7 @@ def store(y: torch.Tensor, norms: torch.Tensor, value: torch.Tensor, kv_cache: t
         kv_cache.stride(0), kv_cache.stride(1), kv_cache.stride(2))
     a.num_blocks = nb
     a.num_tokens, a.num_kv_heads, a.head_dim, a.block_size = N, H, HEAD_DIM, bs
-    a.n_centroids = 8 if lay in (LAYOUT_SOA_K3, LAYOUT_SOA_K3V3) else 16
+    a.n_centroids = 8 if lay in KEY3_LAYOUTS else 16
     a.norm_correction = int(bool(norm_correction)) if lay in (LAYOUT_SOA, LAYOUT_SOA_K3, LAYOUT_SOA_K3V3) else 0
     with torch.cuda.device(kv_cache.device):
         _lib.check(_lib.load().tqb_store(a, stream if stream is not None else _stream(kv_cache.device)))
