@@ -210,6 +210,24 @@ typedef struct tqb_rotate_args {
 int tqb_rotate_query(const tqb_rotate_args* args, cudaStream_t stream);
 
 /*
+ * Query rotation fused into Stage1 (reference/soa_decode_v1.py:535-608, the
+ * launcher's cast + rotation GEMM + copy followed by the Stage1 launch; the
+ * reference's unified attention rotates inside its kernel,
+ * reference/soa_unified.py:88-124).  rot describes the rotation exactly as
+ * for tqb_rotate_query, and its output must be Stage1's query: rot->q_rot ==
+ * s1->q_rot with the same strides, batch and heads.  On return q_rot holds
+ * float(query) @ rotation (bit-identical to tqb_rotate_query) and mid_o the
+ * Stage1 result.  Where the page-ring Stage1 serves the cache (SoA, or AoS
+ * with Hk dividing 8) and the GQA group is at most 4, this is ONE kernel: a
+ * cooperative launch of one CTA per SM whose prologue rotates an equal
+ * share of the rows, followed by a grid barrier (a static counter of the
+ * library, bounded wait); otherwise tqb_rotate_query then tqb_stage1 on the
+ * same stream.  Fused calls on one device must not overlap in time (issue
+ * them on one stream): they share that counter.
+ */
+int tqb_stage1_rotated(const tqb_rotate_args* rot, const tqb_stage1_args* s1, cudaStream_t stream);
+
+/*
  * Cross-GPU merge: partials[g, b, h, 0:D] / partials[g, b, h, D] are the
  * (O, LSE) of G disjoint KV ranges (one per GPU, already gathered into this
  * GPU's memory).  Ranges whose LSE is -inf (no tokens) are skipped.

@@ -207,3 +207,20 @@ def test_missing_library_raises_promptly(tmp_path: Path):
 def test_status_text_matches_library(lib):
     for status, text in _lib.STATUS_TEXT.items():
         assert lib.tqb_strerror(status).decode() == text
+
+
+def test_stage1_rotated_rejects_on_the_host(lib):
+    """tqb_stage1_rotated checks, before any device call, that the rotation
+    writes Stage1's own query buffer and that the query dtype is known."""
+    r = _lib.RotateArgs()
+    a = _lib.Stage1Args()
+    r.q_rot, a.q_rot = 0x1000, 0x2000  # different buffers
+    r.batch = a.batch = 2
+    r.num_q_heads = a.num_q_heads = 32
+    r.head_dim = a.head_dim = 128
+    assert lib.tqb_stage1_rotated(ctypes.byref(r), ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    assert b"rotation's output" in lib.tqb_last_error_detail()
+    r.q_rot = a.q_rot
+    r.query_dtype = 7
+    assert lib.tqb_stage1_rotated(ctypes.byref(r), ctypes.byref(a), None) == _lib.TQB_ERR_INVALID_ARG
+    assert b"query_dtype" in lib.tqb_last_error_detail()

@@ -175,3 +175,72 @@ def test_rotate_query_vs_torch(cuda_device, dtype):
     assert err <= 1e-5 * max(1.0, ref.abs().max().item()), err
     assert torch.equal(out[:, 2:34], got)
     assert torch.all(out[:, :2] == -7.0) and torch.all(out[:, 34:] == -7.0)
+
+
+def _value_edge_rows(rng, n, top):
+    """Value rows that stress the quantiser's division (v - min) / scale:
+    quotients a few ulps either side of every k + 1/2 (where the code
+    changes), constant rows (scale clamped to 1e-8), tiny (1e-30) and huge
+    (1e37) magnitudes, and plain rows at scales from 1e-6 to 1e6."""
+    rows = np.empty((n, 128), np.float32)
+    for i in range(n):
+        kind = i % 5
+        s = np.float32(10.0 ** rng.uniform(-6, 6))
+        if kind == 0:
+            vmin, vmax = np.float32(-rng.uniform(0.1, 3) * s), np.float32(rng.uniform(0.1, 3) * s)
+            scale = np.float32((vmax - vmin) / np.float32(top))
+            k = rng.integers(0, top, 126)
+            a = ((k + 0.5) * np.float64(scale)).astype(np.float32)
+            a = np.nextafter(a, np.float32(np.inf) * rng.choice([-1, 1], 126)).astype(np.float32)
+            a[::3] = ((k[::3] + 0.5) * np.float64(scale)).astype(np.float32)
+            rows[i, :126] = np.minimum(np.maximum(vmin + a, vmin), vmax)
+            rows[i, 126:] = (vmin, vmax)
+        elif kind == 1:
+            rows[i] = np.float32(rng.standard_normal())
+        elif kind == 2:
+            rows[i] = rng.standard_normal(128).astype(np.float32) * np.float32(1e-30)
+        elif kind == 3:
+            rows[i] = rng.uniform(-1, 1, 128).astype(np.float32) * np.float32(1e37)
+        else:
+            rows[i] = rng.standard_normal(128).astype(np.float32) * s
+    return rows
+
+
+@pytest.mark.parametrize("layout", ["soa", "soa_k8", "soa_k3", "soa_k3v3", "aos"])
+def test_store_value_rounding_edges(cuda_device, layout):
+    """The store's value codes at the rounding edges of (v - min) / scale,
+    bit-exact against the oracle's IEEE float32 division (the kernel divides
+    by a correctly rounded reciprocal plus two FMA corrections)."""
+    rng = np.random.default_rng(11)
+    H, N, nb = 4, 1200, 320
+    k3 = layout in ("soa_k3", "soa_k3v3")
+    top = 7 if layout == "soa_k3v3" else 15
+    val = _value_edge_rows(rng, N * H, top)
+    y = (rng.standard_normal((N * H, 128)) * (3.0 if layout == "soa_k8" else 0.09)).astype(np.float32)
+    norms = np.abs(rng.standard_normal(N * H)).astype(np.float32) * 7
+    cents = tqb.get_centroids(128, 3 if k3 else 4).numpy()
+    mids = ((cents[:-1] + cents[1:]) * 0.5).astype(np.float32) if k3 else tqb.get_midpoints(
+        torch.from_numpy(cents)).numpy()
+    slots = rng.permutation(nb * 16)[:N].astype(np.int32)
+    slots[::89] = -1
+    slot_bytes = {"soa": 134, "aos": 134, "soa_k8": 196, "soa_k3": 118, "soa_k3v3": 102}[layout]
+    base = rng.integers(0, 256, (nb, 16, H, slot_bytes), dtype=np.uint8)
+    ref = base.copy()
+    if layout == "soa_k8":
+        O.store_k8_np(y.reshape(N, H, 128), val.reshape(N, H, 128), slots, ref)
+    elif k3:
+        O.store_k3_np(y, norms, val, mids, cents, slots, ref, vbits=3 if layout == "soa_k3v3" else 4)
+    else:
+        lay = O.LAYOUT_SOA if layout == "soa" else O.LAYOUT_AOS
+        O.store(lay, y, norms, val, mids, cents, slots, ref, norm_correction=layout == "soa")
+    dev = cuda_device
+    cache = torch.from_numpy(base).to(dev)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    if layout == "soa_k8":
+        tqb.store(d(y), None, d(val), cache, d(slots), None, None, layout=layout, norm_correction=False)
+    else:
+        tqb.store(d(y), d(norms), d(val), cache, d(slots), d(mids), d(cents), layout=layout,
+                  norm_correction=layout != "aos")
+    torch.cuda.synchronize()
+    got = cache.cpu().numpy()
+    assert np.array_equal(got, ref), f"{(got != ref).sum()} bytes differ from the oracle store"

@@ -112,8 +112,8 @@ const char* tqb_strerror(int status) {
 
 const char* tqb_last_error_detail(void) { return g_detail; }
 
-int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
-    g_detail[0] = '\0';
+// Validates Stage1 arguments and fills p (for batch > 0).
+static int stage1_check(const tqb_stage1_args* a, tqb::Stage1Params& p) {
     TQB_REQUIRE(a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
     TQB_REQUIRE(a->batch >= 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 && a->num_splits > 0,
                 TQB_ERR_INVALID_ARG, "batch/heads/num_splits must be positive");
@@ -167,12 +167,6 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                     "AoS strides must describe [blocks, 16, Hk, >= slot] slots (slot 134, 196, 118 or 102 bytes "
                     "by layout), token- or head-major");
     }
-    DeviceGuard guard(a->mid_o);
-    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
-    const int nsm = sm_count();
-    TQB_REQUIRE(nsm > 0, TQB_ERR_CUDA, "cannot query the current CUDA device");
-
-    tqb::Stage1Params p{};
     p.q = a->q_rot;
     p.qsb = a->q_stride_b;
     p.qsh = a->q_stride_h;
@@ -203,9 +197,60 @@ int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
                 "batch * num_splits * num_kv_heads must be < 2^31");
     p.div_hk = tqb::FastDiv((uint32_t)a->num_kv_heads);
     p.div_s = tqb::FastDiv((uint32_t)a->num_splits);
-    const int rc = tqb::launch_stage1(p, stream, nsm);
-    if (rc != TQB_OK) return rc;
     return TQB_OK;
+}
+
+int tqb_stage1(const tqb_stage1_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    tqb::Stage1Params p{};
+    const int rc = stage1_check(a, p);
+    if (rc != TQB_OK || a->batch == 0) return rc;
+    DeviceGuard guard(a->mid_o);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
+    const int nsm = sm_count();
+    TQB_REQUIRE(nsm > 0, TQB_ERR_CUDA, "cannot query the current CUDA device");
+    return tqb::launch_stage1(p, stream, nsm);
+}
+
+int tqb_stage1_rotated(const tqb_rotate_args* r, const tqb_stage1_args* a, cudaStream_t stream) {
+    g_detail[0] = '\0';
+    TQB_REQUIRE(r != nullptr && a != nullptr, TQB_ERR_INVALID_ARG, "args is NULL");
+    TQB_REQUIRE(r->q_rot == a->q_rot && r->out_stride_b == a->q_stride_b && r->out_stride_h == a->q_stride_h &&
+                    r->batch == a->batch && r->num_q_heads == a->num_q_heads && r->head_dim == a->head_dim,
+                TQB_ERR_INVALID_ARG,
+                "the rotation's output must be Stage1's q_rot (same pointer, strides, batch and heads)");
+    TQB_REQUIRE(r->query_dtype == TQB_DTYPE_F32 || r->query_dtype == TQB_DTYPE_F16 ||
+                    r->query_dtype == TQB_DTYPE_BF16,
+                TQB_ERR_INVALID_ARG, "query_dtype must be TQB_DTYPE_F32, TQB_DTYPE_F16 or TQB_DTYPE_BF16");
+    tqb::Stage1Params p{};
+    int rc = stage1_check(a, p);
+    if (rc != TQB_OK || a->batch == 0) return rc;
+    TQB_REQUIRE(r->query && r->rotation, TQB_ERR_INVALID_ARG, "query or rotation is NULL");
+    TQB_REQUIRE(aligned(r->query, r->query_dtype == TQB_DTYPE_F32 ? 4 : 2) && aligned(r->rotation, 16),
+                TQB_ERR_ALIGNMENT, "query must be aligned to its element size, rotation to 16 bytes");
+    DeviceGuard guard(a->mid_o);
+    TQB_REQUIRE(guard.ok, TQB_ERR_CUDA, "cannot select the device owning mid_o");
+    const int nsm = sm_count();
+    TQB_REQUIRE(nsm > 0, TQB_ERR_CUDA, "cannot query the current CUDA device");
+    // One kernel where the page ring runs with a group of at most 4 query
+    // heads per KV head (its rotation prologue stages the 64 KB rotation in
+    // a ring it has not started yet); otherwise the rotation kernel, then
+    // Stage1.
+    if (p.G <= 4 && !tqb::stage1_register_kernel_forced() && tqb::stage1_ring_supported(p)) {
+        tqb::Stage1Params pr = p;
+        pr.rq = r->query;
+        pr.rq_dtype = r->query_dtype;
+        pr.rqsb = r->q_stride_b;
+        pr.rqsh = r->q_stride_h;
+        pr.rot = r->rotation;
+        pr.q_out = r->q_rot;
+        rc = tqb::launch_stage1_ring(pr, stream, nsm);
+        if (rc != TQB_ERR_UNSUPPORTED) return rc;
+        g_detail[0] = '\0';
+    }
+    rc = tqb_rotate_query(r, stream);
+    if (rc != TQB_OK) return rc;
+    return tqb::launch_stage1(p, stream, nsm);
 }
 
 // Stage2 with the output written as `dtype` to `out` (a->output ignored).
@@ -489,6 +534,8 @@ int tqb_store(const tqb_store_args* a, cudaStream_t stream) {
     TQB_REQUIRE(!(fp8 && a->norm_correction), TQB_ERR_INVALID_ARG,
                 "the FP8-key layouts have no norm correction");
     if (a->num_tokens == 0) return TQB_OK;
+    TQB_REQUIRE((int64_t)a->num_tokens * a->num_kv_heads < ((int64_t)1 << 31), TQB_ERR_UNSUPPORTED,
+                "num_tokens x num_kv_heads must be below 2^31");
     TQB_REQUIRE(a->y && a->value && a->slot_mapping && a->kv_cache && (fp8 || (a->norms && a->midpoints)),
                 TQB_ERR_INVALID_ARG, "a required pointer is NULL");
     TQB_REQUIRE(!a->norm_correction || a->centroids, TQB_ERR_INVALID_ARG,

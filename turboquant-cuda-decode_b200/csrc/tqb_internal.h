@@ -77,6 +77,14 @@ struct Stage1Params {
     float attn_scale;
     int64_t num_items;  // B * S * Hk work items, KV head fastest (< 2^31)
     FastDiv div_hk, div_s;
+    // Fused query rotation (the page-ring kernel only; rot == nullptr: off):
+    // q_out[b, h, :] = float(rq[b, h, :]) @ rot, written by the kernel's
+    // prologue before its producers load the rows from q (== q_out).
+    const void* rq;
+    int rq_dtype;  // TQB_DTYPE_*
+    int64_t rqsb, rqsh;
+    const float* rot;  // [D, D] row-major
+    float* q_out;
 };
 
 struct Stage2Params {
@@ -163,6 +171,9 @@ int launch_stage1(const Stage1Params& p, cudaStream_t stream, int num_sms);
 // SoA Stage1 fed by the TMA page ring (tqb_stage1_ring.cu); supported when
 // the cache and query rows are 16-byte aligned.
 bool stage1_ring_supported(const Stage1Params& p);
+// TQB_STAGE1_KERNEL=regs in the environment (read on every call) selects the
+// register-ring kernel for caches the page ring also serves.
+bool stage1_register_kernel_forced();
 int launch_stage1_ring(const Stage1Params& p, cudaStream_t stream, int num_sms);
 // Reads (and optionally clears) the count of bounded device waits that ran
 // out on the current device.

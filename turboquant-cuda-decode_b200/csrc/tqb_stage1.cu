@@ -757,13 +757,13 @@ int launch_t(const Stage1Params& P, cudaStream_t stream, int num_sms) {
 
 // TQB_STAGE1_KERNEL=regs selects the register-ring kernel for an SoA cache
 // too (the TMA page-ring kernel is the default there); read on every call.
-static bool force_register_kernel() {
+bool stage1_register_kernel_forced() {
     const char* v = getenv("TQB_STAGE1_KERNEL");
     return v != nullptr && strcmp(v, "regs") == 0;
 }
 
 int launch_stage1(const Stage1Params& P, cudaStream_t stream, int num_sms) {
-    if (stage1_ring_supported(P) && !force_register_kernel()) {
+    if (stage1_ring_supported(P) && !stage1_register_kernel_forced()) {
         const int rc = launch_stage1_ring(P, stream, num_sms);
         if (rc != TQB_ERR_UNSUPPORTED) return rc;  // else: tensor maps refused, use the register kernel
     }

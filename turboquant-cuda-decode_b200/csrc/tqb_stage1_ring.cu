@@ -35,6 +35,8 @@
 //    a device counter (tqb_wait_timeouts) and the warp leaves its loops, so a
 //    protocol fault ends the kernel instead of hanging the GPU.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched at run time
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -44,6 +46,13 @@ namespace tqb {
 
 // Number of bounded mbarrier waits that ran out (read by tqb_wait_timeouts).
 __device__ unsigned int g_wait_timeouts = 0;
+// Grid barrier of the fused query rotation (stage1 with rot != nullptr): the
+// cooperative-groups arrival scheme, block 0 adds 2^31 - (grid - 1) and every
+// other block 1, so bit 31 flips once per launch and the word never needs a
+// reset.  Two such launches never interleave their arrivals: each is a
+// cooperative launch of one CTA per SM, so the next starts only after every
+// CTA of the previous one has ended.
+__device__ unsigned int g_rot_barrier = 0;
 
 namespace {
 
@@ -436,6 +445,85 @@ struct GroupSmem {
 };
 
 // ---------------------------------------------------------------------------
+// Fused query rotation (P.rot set; the one-group-per-warpgroup layout, GQA
+// <= 4): before the roles split, the CTA computes rows [r0, r1) of
+// q_out = float(rq) @ rot (an equal share of the B * Hq rows per CTA) with
+// the arithmetic of the rotation kernel (tqb_rotate.cu: fp32 FMAs in k order,
+// so the rows are bit-identical to it).  rot (64 KB) is staged in group 1's
+// ring and query area, the input rows in group 0's query area, 32 at a time;
+// the producers' TMA copies overwrite both only after the CTA barrier that
+// ends the prologue.
+// ---------------------------------------------------------------------------
+template <int NT>
+__device__ void rotate_share(const Stage1Params& P, uint8_t* smem, int tid) {
+    using C = Cfg<NT>;
+    static_assert(NT == 1, "the fused rotation stages rot in group 1's ring");
+    static_assert(C::q_off(1) + C::kQBytes - C::ring_off(1) >= kHeadDim * kHeadDim * 4, "rot staging");
+    static_assert(C::kQBytes >= 32 * kQRowBytes, "row staging");
+    constexpr int kChunk = 32;
+    float* rs = reinterpret_cast<float*>(smem + C::ring_off(1));
+    float* qs = reinterpret_cast<float*>(smem + C::q_off(0));
+    const int64_t rows = (int64_t)P.B * P.Hq;
+    const int64_t per = (rows + gridDim.x - 1) / gridDim.x;
+    const int64_t r0 = (int64_t)blockIdx.x * per, r1 = min(rows, r0 + per);
+    if (r0 >= r1) return;  // uniform over the CTA
+    const float4* R4 = reinterpret_cast<const float4*>(P.rot);
+    for (int e = tid; e < kHeadDim * kHeadDim / 4; e += C::kThreads)
+        reinterpret_cast<float4*>(rs)[e] = __ldg(R4 + e);
+    const int j = tid % kHeadDim;
+    for (int64_t c0 = r0; c0 < r1; c0 += kChunk) {
+        const int n = (int)min((int64_t)kChunk, r1 - c0);
+        __syncthreads();  // rot staged / the previous chunk's rows read
+        for (int e = tid; e < n * kHeadDim; e += C::kThreads) {
+            const int64_t r = c0 + e / kHeadDim;
+            const int64_t off = (r / P.Hq) * P.rqsb + (r % P.Hq) * P.rqsh + e % kHeadDim;
+            float v;
+            if (P.rq_dtype == TQB_DTYPE_F16)
+                v = __half2float(static_cast<const __half*>(P.rq)[off]);
+            else if (P.rq_dtype == TQB_DTYPE_BF16)
+                v = __bfloat162float(static_cast<const __nv_bfloat16*>(P.rq)[off]);
+            else
+                v = static_cast<const float*>(P.rq)[off];
+            qs[e] = v;
+        }
+        __syncthreads();
+        for (int i = tid / kHeadDim; i < n; i += C::kThreads / kHeadDim) {
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int k = 0; k < kHeadDim; k++) acc = fmaf(qs[i * kHeadDim + k], rs[k * kHeadDim + j], acc);
+            const int64_t r = c0 + i;
+            P.q_out[(r / P.Hq) * P.qsb + (r % P.Hq) * P.qsh + j] = acc;
+        }
+    }
+}
+
+// Producer 0 of a group, before its first query copy: wait (bounded) until
+// every CTA's rotated rows are written (bit 31 of the barrier word differs
+// from the value this CTA's arrival saw).
+__device__ __forceinline__ bool rot_barrier_wait(uint32_t seen, int lane) {
+    int ok = 1;
+    if (lane == 0) {
+        const long long t0 = clock64();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(&g_rot_barrier) : "memory");
+            if ((v ^ seen) & 0x80000000u) break;
+            if (clock64() - t0 > kWaitCycles) {
+                atomicAdd(&g_wait_timeouts, 1u);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    // the rows came from other CTAs through the generic proxy; the tensor
+    // copies that read them are async-proxy operations
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");
+    return ok != 0;
+}
+
+// ---------------------------------------------------------------------------
 // Producer warp: query rows and pages of each tile into the group's ring.
 // Runs at kProducerRegs registers, so run parameters live one run per lane
 // and block ids are fetched one stage ahead into a single register.
@@ -487,7 +575,12 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
     ItemInfo ir;
     int np = 0, np_tile = 0;
     uint32_t t = next_tile(lds32(gs.tiles()), ir, np, np_tile);
-    if (t < t_end && !issue_query(ir, np)) abort = true;
+    if (P.rot != nullptr && pj == 0 && t < t_end) {
+        // fused rotation: the query rows are written by every CTA's prologue
+        const uint32_t base = gs.bars - (uint32_t)gi * kBarStride - Cfg<NT>::kBarOff;
+        if (!rot_barrier_wait(lds32(base + Cfg<NT>::kBarOff + 112u), lane)) abort = true;
+    }
+    if (t < t_end && !abort && !issue_query(ir, np)) abort = true;
     while (t < t_end && !abort) {
         // The next tile is decoded now; its query rows go out once page 0 of
         // this tile has been released (the compute warps have read this
@@ -1045,6 +1138,23 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     }
     __syncthreads();
 
+    if constexpr (NT == 1) {
+        if (P.rot != nullptr) {
+            rotate_share<NT>(P, smem, tid);
+            // generic writes to the ring and query areas, before the tensor
+            // copies (async proxy) that will overwrite them
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();  // this CTA's rows, before its arrival
+                const uint32_t seen =
+                    atomicAdd(&g_rot_barrier, blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u);
+                sts32(base + C::kBarOff + 112u, seen);
+            }
+            __syncthreads();
+        }
+    }
+
     if (producer) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::kProducerRegs));
         const int pj = (warp - C::kComputeWarps) / C::kGroups;
@@ -1134,6 +1244,27 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
             return report_launch(cudaGetLastError());
         configured_dev = dev;
+    }
+    if (P.rot != nullptr) {
+        // Fused query rotation: every SM's CTA takes a share of the rows and
+        // the grid barrier needs all of them resident at once, which a
+        // cooperative launch guarantees (or refuses).
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)num_sms);
+        cfg.blockDim = dim3(C::kThreads);
+        cfg.dynamicSmemBytes = C::kSmem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P, M);
+        if (e == cudaErrorCooperativeLaunchTooLarge) {
+            cudaGetLastError();
+            return TQB_ERR_UNSUPPORTED;  // the caller rotates in a kernel of its own
+        }
+        return report_launch(e);
     }
     const int64_t tiles = (P.num_items + kGroupWarps - 1) / kGroupWarps;
     const int64_t need = (tiles + C::kGroups - 1) / C::kGroups;

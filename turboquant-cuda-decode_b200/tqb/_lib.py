@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "tqb_stage2_typed",
     "tqb_fold_sinks",
     "tqb_rotate_query",
+    "tqb_stage1_rotated",
     "tqb_p2p_buffer_bytes",
     "tqb_p2p_alloc",
     "tqb_p2p_free",
@@ -209,6 +210,8 @@ def load() -> ctypes.CDLL:
             lib.tqb_fold_sinks.restype = ctypes.c_int
             lib.tqb_rotate_query.argtypes = [ctypes.POINTER(RotateArgs), _vp]
             lib.tqb_rotate_query.restype = ctypes.c_int
+            lib.tqb_stage1_rotated.argtypes = [ctypes.POINTER(RotateArgs), ctypes.POINTER(Stage1Args), _vp]
+            lib.tqb_stage1_rotated.restype = ctypes.c_int
             lib.tqb_p2p_buffer_bytes.argtypes = [_i32, _i64]
             lib.tqb_p2p_buffer_bytes.restype = _i64
             lib.tqb_p2p_alloc.argtypes = [_i64, ctypes.POINTER(_vp)]

@@ -166,6 +166,7 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
     both reference launchers (reference/soa_decode_v1.py:486-643,
     reference/aos_decode.py:486-...) with the buffer reuse they offer."""
     B, Hq, D = query.shape
+    fused = None  # (query, rotation) rotated inside the Stage1 launch
     if layout in ("soa_k8", "k8v4", "aos_k8"):
         # FP8 keys score against the query itself, read as fp32
         # (reference/soa_decode_v1.py:532-533)
@@ -173,11 +174,12 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
     else:
         if PiT is None:
             PiT = Pi.T.contiguous()
-        # cast + rotation in one kernel (the reference: query.float() @ PiT,
-        # reference/soa_decode_v1.py:535-538)
         if query.dtype in (torch.float32, torch.float16, torch.bfloat16):
-            q_rot = ops.rotate_query(query if query.stride(2) == 1 else query.contiguous(),
-                                     PiT.float().contiguous())
+            # q_rot = query.float() @ PiT (reference/soa_decode_v1.py:535-538)
+            # computed by Stage1 itself (tqb_stage1_rotated: one kernel on the
+            # page ring, else the fused cast + rotation kernel first)
+            q_rot = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
+            fused = (query if query.stride(2) == 1 else query.contiguous(), PiT.float().contiguous())
         else:
             q_rot = (query.float() @ PiT).contiguous()
     S = max_num_kv_splits
@@ -190,7 +192,8 @@ def decode_attention(query, kv_cache, block_table, seq_lens, Pi, centroids, scal
     if sinks is not None:
         sinks = sinks.to(device=query.device, dtype=torch.float32).contiguous()
     ops.stage1(q_rot, kv_cache, block_table, seq_lens, centroids, mid_o, layout=layout,
-               attn_scale=scale, sinks=sinks)
+               attn_scale=scale, sinks=sinks, query=None if fused is None else fused[0],
+               rotation=None if fused is None else fused[1])
     if output_buf is not None and output_buf.shape[0] >= B:
         # the caller's workspace, in its own dtype (vLLM hands it out in the
         # query's dtype, reference/turboquant_attn.py:1133-1141); Stage2

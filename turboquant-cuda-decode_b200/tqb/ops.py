@@ -65,8 +65,14 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
            seq_lens: torch.Tensor, centroids: torch.Tensor, mid_o: torch.Tensor, *,
            layout="soa", num_splits_per_seq: Optional[torch.Tensor] = None,
            pair_lut: Optional[torch.Tensor] = None, attn_scale: Optional[float] = None,
-           sinks: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> torch.Tensor:
+           sinks: Optional[torch.Tensor] = None, query: Optional[torch.Tensor] = None,
+           rotation: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> torch.Tensor:
     """Decode Stage1 into ``mid_o [B, Hq, S, D+1]`` (S = ``mid_o.shape[2]``).
+
+    With ``query`` and ``rotation`` given, ``q_rot`` is an output: Stage1
+    first computes ``q_rot = float(query) @ rotation`` (:func:`rotate_query`)
+    and decodes with it; ``tqb_stage1_rotated`` does both in one kernel where
+    the page ring serves the cache and the GQA group is at most 4.
 
     ``kv_cache`` is the ``[num_blocks, 16, Hk, 134]`` uint8 cache (a view
     with a non-unit block stride is accepted; SoA needs the inner three dims
@@ -109,6 +115,10 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
         _cuda(sinks, "sinks", torch.float32)
         _require(sinks.shape == (Hq,) and sinks.is_contiguous() and sinks.device == mid_o.device,
                  "sinks must be a contiguous [Hq] float32 tensor on mid_o's device")
+    r = None
+    if query is not None or rotation is not None:
+        _require(query is not None and rotation is not None, "query and rotation go together")
+        r = _rotate_args(query, rotation, q_rot)
     a = Stage1Args()
     a.q_rot = q_rot.data_ptr()
     a.q_stride_b, a.q_stride_h = q_rot.stride(0), q_rot.stride(1)
@@ -132,7 +142,10 @@ def stage1(q_rot: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tenso
     a.attn_scale = float(attn_scale) if attn_scale is not None else 1.0 / math.sqrt(D)
     with torch.cuda.device(mid_o.device):
         st = stream if stream is not None else _stream(mid_o.device)
-        _lib.check(_lib.load().tqb_stage1(a, st))
+        if r is None:
+            _lib.check(_lib.load().tqb_stage1(a, st))
+        else:
+            _lib.check(_lib.load().tqb_stage1_rotated(r, a, st))
     if sinks is not None:
         fold_sinks(mid_o, seq_lens, sinks, stream=stream)
     return mid_o
@@ -202,13 +215,7 @@ def stage2(mid_o: torch.Tensor, seq_lens: torch.Tensor, output: torch.Tensor, ls
     return output, lse
 
 
-def rotate_query(query: torch.Tensor, rotation: torch.Tensor, out: Optional[torch.Tensor] = None, *,
-                 stream: Optional[int] = None) -> torch.Tensor:
-    """``float(query) @ rotation`` for ``query [B, Hq, D]`` (float32, float16
-    or bfloat16, unit stride over D) and ``rotation = Pi^T [D, D]`` float32:
-    the launcher's cast + GEMM + copy (reference/soa_decode_v1.py:535-538) in
-    one kernel, fp32 accumulation.  Writes ``out`` (float32 [B, Hq, D],
-    allocated when None) and returns it."""
+def _rotate_args(query: torch.Tensor, rotation: torch.Tensor, out: torch.Tensor) -> RotateArgs:
     _require(isinstance(query, torch.Tensor) and query.is_cuda and query.dtype in _DTYPE_ID,
              "query must be a float32/float16/bfloat16 CUDA tensor")
     _cuda(rotation, "rotation", torch.float32)
@@ -217,8 +224,6 @@ def rotate_query(query: torch.Tensor, rotation: torch.Tensor, out: Optional[torc
     _require(tuple(rotation.shape) == (HEAD_DIM, HEAD_DIM) and rotation.is_contiguous(),
              "rotation must be a contiguous [128, 128] matrix")
     B, Hq, D = query.shape
-    if out is None:
-        out = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
     _cuda(out, "out", torch.float32)
     _require(tuple(out.shape) == (B, Hq, D) and out.stride(2) == 1, "out must be [B, Hq, 128]")
     a = RotateArgs()
@@ -227,6 +232,21 @@ def rotate_query(query: torch.Tensor, rotation: torch.Tensor, out: Optional[torc
     a.rotation, a.q_rot = rotation.data_ptr(), out.data_ptr()
     a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
     a.batch, a.num_q_heads, a.head_dim = B, Hq, D
+    return a
+
+
+def rotate_query(query: torch.Tensor, rotation: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                 stream: Optional[int] = None) -> torch.Tensor:
+    """``float(query) @ rotation`` for ``query [B, Hq, D]`` (float32, float16
+    or bfloat16, unit stride over D) and ``rotation = Pi^T [D, D]`` float32:
+    the launcher's cast + GEMM + copy (reference/soa_decode_v1.py:535-538) in
+    one kernel, fp32 accumulation.  Writes ``out`` (float32 [B, Hq, D],
+    allocated when None) and returns it."""
+    _require(isinstance(query, torch.Tensor) and query.is_cuda and query.dim() == 3,
+             "query must be a [B, Hq, 128] CUDA tensor")
+    if out is None:
+        out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+    a = _rotate_args(query, rotation, out)
     with torch.cuda.device(query.device):
         _lib.check(_lib.load().tqb_rotate_query(a, stream if stream is not None else _stream(query.device)))
     return out
