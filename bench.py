@@ -358,7 +358,7 @@ def measure_store(w, dev, peak: float, reps: int = 20) -> dict:
     return {"token_heads": N * H, "us_per_launch": us, "token_heads_per_s": N * H / (us * 1e-6),
             "algorithmic_bytes_per_launch": alg, "bytes_per_token_head": per_th,
             "achieved_gbs": alg / (us * 1e-6) / 1e9, "frac_of_peak": alg / (us * 1e-6) / 1e9 / peak,
-            "kernel": "tqb store_kernel (warp per token-head, 4-bit SoA with norm correction)"}
+            "kernel": "tqb store_kernel (half a warp per token-head, 4-bit SoA with norm correction)"}
 
 
 def cpu_baseline(w, min_seconds=10.0):
@@ -1146,7 +1146,7 @@ def main():
                      else "fallback 6.65 TB/s",
                      "algorithmic_bytes_per_launch": alg,
                      "kernel": ("tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)" if args.layout == "soa"
-                                else "tqb stage1_kernel (register page ring, FP8 keys)" if args.layout == "soa_k8"
+                                else "tqb stage1_ring_kernel (TMA page ring: whole FP8-key blocks by bulk copy)" if args.layout == "soa_k8"
                                 else "tqb stage1_kernel (register page ring, 3-bit keys)" if args.layout == "soa_k3"
                                 else "tqb stage1_kernel (register page ring, 3-bit keys and values)" if args.layout == "soa_k3v3"
                                 else "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)")},

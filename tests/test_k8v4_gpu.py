@@ -169,3 +169,53 @@ def test_launchers_store_and_decode(cuda_device):
     assert_close(got[live], ref16, rtol=RTOL + 2.0 ** -10, what="k8v4 decode out")
     assert_close(lse.cpu().numpy()[live], ref_lse[live], what="k8v4 decode lse")
     assert np.all(np.isnan(got[~live]))
+
+
+@pytest.mark.parametrize("hq,hk", [(32, 8), (8, 2), (4, 1), (12, 4), (16, 8), (8, 8), (20, 4)])
+@pytest.mark.parametrize("kernel", ["default", "regs"])
+def test_stage1_page_ring_and_register_kernel(cuda_device, hq, hk, kernel, monkeypatch):
+    """FP8 keys on both Stage1 kernels: the TMA page ring (GQA <= 4 with Hk
+    dividing 8: whole FP8 blocks per page, e4m3 converted in registers) and
+    the register-ring kernel (TQB_STAGE1_KERNEL=regs, and GQA-5 always).
+    Ragged lengths with an empty sequence, a split of more than 32 pages and
+    splits starting mid-page, against the float64 oracle."""
+    if kernel == "regs":
+        monkeypatch.setenv("TQB_STAGE1_KERNEL", "regs")
+    lens = [1, 0, 1100, 45, 300, 517, 2100]
+    z = _k8_case(71 + hq + 3 * hk, len(lens), hq, hk, lens, pool_extra=7)
+    S = 6
+    ref = O.stage1_np(z["query"], z["kv_cache"], z["block_table"], z["seq_lens"], None, S, layout=O.LAYOUT_SOA_K8)
+    _check(_stage1(cuda_device, z, S), ref, f"k8v4 Stage1 Hq{hq}/Hk{hk} ({kernel})")
+
+
+def test_c1_fp8_decode_vs_oracle(cuda_device):
+    """The c1 shape (B64 x 4096, Hq32/Hk8, S32) with FP8 keys, on the page
+    ring: every partial, then Stage2, against the float64 oracle on the
+    same cache (written by the FP8-key store from seeded N(0,1) K/V)."""
+    dev = cuda_device
+    B, L, Hq, Hk, S = 64, 4096, 32, 8, 32
+    gen = torch.Generator(device=dev).manual_seed(23)
+    pages = L // 16
+    nblk = B * pages
+    bt = torch.randperm(nblk, device=dev, generator=gen).view(B, pages).to(torch.int32)
+    kv = torch.zeros(nblk, 16, Hk, 196, dtype=torch.uint8, device=dev)
+    tok = torch.arange(L, device=dev)
+    for b in range(B):  # one sequence per store call
+        slots = (bt[b, tok // 16] * 16 + tok % 16).to(torch.int32)
+        key = torch.randn(L * Hk, 128, device=dev, generator=gen) * 3.0
+        val = torch.randn(L * Hk, 128, device=dev, generator=gen)
+        tqb.store(key, None, val, kv, slots, None, None, layout="soa_k8", norm_correction=False)
+    q = torch.randn(B, Hq, 128, device=dev, generator=gen) * 0.5
+    sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+    mid = torch.full((B, Hq, S, 129), SENTINEL, device=dev)
+    tqb.stage1(q, kv, bt, sl, None, mid, layout="soa_k8")
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, sl, out, lse)
+    torch.cuda.synchronize()
+    ref = O.stage1_np(q.cpu().numpy(), kv.cpu().numpy(), bt.cpu().numpy(), sl.cpu().numpy(), None, S,
+                      layout=O.LAYOUT_SOA_K8)
+    _check(mid.cpu().numpy(), ref, "c1 FP8 Stage1")
+    ref_out, ref_lse = O.stage2_np(ref, sl.cpu().numpy())
+    assert_close(out.cpu().numpy(), ref_out, what="c1 FP8 Stage2 out")
+    assert_close(lse.cpu().numpy(), ref_lse, what="c1 FP8 Stage2 lse")

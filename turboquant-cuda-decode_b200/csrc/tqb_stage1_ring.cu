@@ -37,6 +37,7 @@
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched at run time
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include "tqb_common.cuh"
@@ -68,6 +69,18 @@ constexpr int kLutStride = 256;                                // bytes per tabl
 constexpr int kLutCopies = 32;                                 // one copy per lane
 constexpr int kAosSlot = 134;                                   // AoS bytes per (token, head)
 constexpr int kAosHead = kBlockSize * kAosSlot;                 // 2144: one head's slots of a page
+constexpr int kK8Head = kBlockSize * kSlotBytesK8;              // 3136: one head's share of an FP8-key block
+constexpr int kK8StageBytes = 25600;                           // 8 x 3136, 1024-aligned
+static_assert(kGroupWarps * kK8Head <= kK8StageBytes && kK8StageBytes % 1024 == 0, "FP8-key stage");
+// Bytes of one ring stage, and of one head's page in it (SoA: 2048 data +
+// 96 metadata, AoS: 16 slots, FP8 keys: 16 x 192 data + 64 metadata).
+__host__ __device__ constexpr int stage_bytes(int layout) {
+    return layout == TQB_LAYOUT_SOA_K8 ? kK8StageBytes : kStageBytes;
+}
+__host__ __device__ constexpr int head_page_bytes(int layout) {
+    return layout == TQB_LAYOUT_SOA_K8 ? kK8Head : kAosHead;
+}
+static_assert(kBlockSize * kDataBytes + kMetaSlot == kAosHead, "SoA and AoS heads take the same page bytes");
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
 constexpr int kLutAddr = 0x10000;                              // shared address of the table
 constexpr int kDynBase = 0x400;  // shared address of dynamic shared memory (1 KB reserved below it)
@@ -84,13 +97,14 @@ constexpr float kWMax = 32768.0f;                              // largest W on t
 // setmaxnreg moves registers from the producer warpgroup to the compute
 // warpgroups; the shares add up to at most the launch allocation
 // (kThreads x kLaunchRegs), so every setmaxnreg.inc can be satisfied.
-template <int NT>
+template <int NT, int LAYOUT = TQB_LAYOUT_SOA>
 struct Cfg {
+    static constexpr bool kTable = LAYOUT != TQB_LAYOUT_SOA_K8;  // FP8 keys convert without the K table
     static constexpr int kGroups = NT == 1 ? 2 : 1;
     static constexpr int kStages = 3;
     static constexpr int kHeadsPerWarp = 4 * NT;
     static constexpr int kQBytes = kGroupWarps * kHeadsPerWarp * kQRowBytes;
-    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kRingBytes = kStages * stage_bytes(LAYOUT);
     static constexpr int kComputeWarps = kGroups * kGroupWarps;
     static constexpr int kWarps = kComputeWarps + 4;
     static constexpr int kThreads = kWarps * 32;
@@ -105,16 +119,19 @@ struct Cfg {
     // K byte, lane copy offset) is its complete LDS address.  Below it: group
     // 0's ring and the barrier blocks; above it: the query areas and group
     // 1's ring.  Every ring stage and query area is 1024-byte aligned.
+    // Without the table (FP8 keys) the query areas start at the first 1 KB
+    // boundary after the barrier blocks.
     static constexpr int kLutOff = kLutAddr - kDynBase;            // 64512
     static constexpr int kBarOff = kRingBytes;                     // after group 0's ring
-    static constexpr int kHighOff = kLutOff + kLutBytes;           // 130048
+    static constexpr int kHighOff = kTable ? kLutOff + kLutBytes   // 130048
+                                           : (kBarOff + kGroups * kBarStride + 1023) / 1024 * 1024;
     static __host__ __device__ constexpr int ring_off(int gi) { return gi == 0 ? 0 : kHighOff + kQBytes; }
     static __host__ __device__ constexpr int q_off(int gi) { return gi == 0 ? kHighOff : kHighOff + kQBytes + kRingBytes; }
     // Output staging: 1 KB per compute warp (two fp32 rows of 128) after the
     // rest, never written by a copy engine.
     static constexpr int kStgOff = kGroups == 1 ? kHighOff + kQBytes : kHighOff + 2 * kQBytes + kRingBytes;
     static constexpr int kSmem = kStgOff + kComputeWarps * kStgBytes;
-    static_assert(kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
+    static_assert(!kTable || kBarOff + kGroups * kBarStride <= kLutOff, "barriers below the table");
     static_assert(8 * (2 * kStages + 2) + 4 * kStages + 12 <= 96 && 96 + 12 <= kBarStride, "barrier block");
     static_assert((16 * kStages + 16 + 4 * kStages + 4) % 8 == 0, "handoff barrier alignment");
     static_assert(kSmem <= 232448, "shared memory per CTA");
@@ -240,6 +257,11 @@ __device__ __forceinline__ uint2 lds64_a2(uint32_t a) {
     const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
     const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8);
     return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+// Two e4m3 bytes (low byte first) to an exact f16x2 (low half first).
+__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {
     const uint4 u = lds128(a);
@@ -425,7 +447,8 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
 // Shared-memory map of one group.
 struct GroupSmem {
     uint32_t ring, qarea, bars, stg;
-    __device__ uint32_t stage(int s) const { return ring + (uint32_t)s * kStageBytes; }
+    template <int LAYOUT>
+    __device__ uint32_t stage(int s) const { return ring + (uint32_t)s * (uint32_t)stage_bytes(LAYOUT); }
     __device__ uint32_t full(int s) const { return bars + 8u * s; }
     template <int NS>
     __device__ uint32_t empty(int s) const { return bars + 8u * (NS + s); }
@@ -531,7 +554,9 @@ __device__ __forceinline__ bool rot_barrier_wait(uint32_t seen, int lane) {
 template <int NT, int LAYOUT>
 __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M, const GroupSmem& gs, int gi,
                                         int lane, int pj, int npj) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, LAYOUT>;
+    constexpr bool kWholeBlock = LAYOUT != TQB_LAYOUT_SOA;  // pages copied as whole blocks
+    constexpr uint32_t kHeadPage = (uint32_t)head_page_bytes(LAYOUT);
     constexpr int NS = C::kStages;
     const uint32_t t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
@@ -577,8 +602,8 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
     uint32_t t = next_tile(lds32(gs.tiles()), ir, np, np_tile);
     if (P.rot != nullptr && pj == 0 && t < t_end) {
         // fused rotation: the query rows are written by every CTA's prologue
-        const uint32_t base = gs.bars - (uint32_t)gi * kBarStride - Cfg<NT>::kBarOff;
-        if (!rot_barrier_wait(lds32(base + Cfg<NT>::kBarOff + 112u), lane)) abort = true;
+        const uint32_t base = gs.bars - (uint32_t)gi * kBarStride - C::kBarOff;
+        if (!rot_barrier_wait(lds32(base + C::kBarOff + 112u), lane)) abort = true;
     }
     if (t < t_end && !abort && !issue_query(ir, np)) abort = true;
     while (t < t_end && !abort) {
@@ -619,7 +644,7 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             const bool here = k < np_r;
             const bool ok = (uint32_t)id < nblocks;
             const uint32_t bytes =
-                __reduce_add_sync(0xffffffffu, here ? (uint32_t)r_nw * (kBlockSize * kDataBytes + kMetaSlot) : 0u);
+                __reduce_add_sync(0xffffffffu, here ? (uint32_t)r_nw * kHeadPage : 0u);
             const uint32_t vm = __reduce_or_sync(0xffffffffu, (here && ok) ? ((1u << r_nw) - 1u) << col : 0u);
             const uint32_t my_id = ok ? (uint32_t)id : 0u;  // a masked page copies block 0
             if (k == NS && !next_query_sent) {
@@ -640,13 +665,14 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             __syncwarp();
             // Lane r < nruns copies run r: its head slices as boxes of 8/4/2/1
             // heads (one box when the run is a whole group) and its metadata
-            // (SoA), or its whole block, unchanged, in one bulk copy (AoS:
-            // a run is all Hk heads of one (b, s), Hk dividing 8).
-            if (LAYOUT == TQB_LAYOUT_AOS && mine && here) {
-                bulk_g2s(gs.stage(slot) + (uint32_t)col * kAosHead, P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes,
-                         (uint32_t)r_nw * kAosHead, gs.full(slot), stream_policy);
+            // (SoA), or its whole block, unchanged, in one bulk copy (AoS and
+            // FP8 keys: a run is all Hk heads of one (b, s), Hk dividing 8).
+            if (kWholeBlock && mine && here) {
+                bulk_g2s(gs.template stage<LAYOUT>(slot) + (uint32_t)col * kHeadPage,
+                         P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes, (uint32_t)r_nw * kHeadPage, gs.full(slot),
+                         stream_policy);
             } else if (mine && here) {
-                const uint32_t dst = gs.stage(slot);
+                const uint32_t dst = gs.template stage<LAYOUT>(slot);
                 int off = 0;
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -711,10 +737,22 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     // its next page is fetched while this one is computed.  The arrive has
     // release semantics: the reads above it are performed before the
     // producer can observe the arrival.
-    uint4 k0, k1;
+    constexpr bool kFp8 = LAYOUT == TQB_LAYOUT_SOA_K8;
+    uint4 k0, k1, k0b, k1b;
     uint32_t kn, vsp, vzp;
     uint2 v[4];
-    if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
+    if constexpr (kFp8) {
+        // whole block [16 tokens][Hk][K 128 e4m3 | V 64] + [Hk][vscale 16 |
+        // vzero 16]: key bytes [32c, 32c+32) of tokens tau(g), tau(g)+1
+        k0 = lds128(sb + o.k0);
+        k0b = lds128(sb + o.k0 + 16u);
+        k1 = lds128(sb + o.k1);
+        k1b = lds128(sb + o.k1 + 16u);
+        kn = 0x3C003C00u;  // no key norm: fp16 1.0 for both tokens
+        vsp = lds32(sb + o.meta);
+        vzp = lds32(sb + o.meta + 32u);
+        // V is read (and the slot released) after Q.K, as for AoS
+    } else if constexpr (LAYOUT == TQB_LAYOUT_SOA) {
         k0 = lds128(sb + o.k0);
         k1 = lds128(sb + o.k1);
         kn = lds32(sb + o.meta);
@@ -756,6 +794,26 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     for (int mt = 0; mt < 2; mt++)
 #pragma unroll
         for (int k = 0; k < 4; k++) dcs[mt][k] = 0.0f;
+    if constexpr (kFp8) {
+        // e4m3 converts exactly to fp16, so one M tile holds the page: row g
+        // = token tau(g), row g+8 = token tau(g)+1, k columns the dims
+        // 32c + 4ks + {0,1 | 2,3} of the query fragments.  Even and odd ks
+        // accumulate in the two tiles' registers (two chains).
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const uint32_t w0 = word_of(ks < 4 ? k0 : k0b, ks & 3), w1 = word_of(ks < 4 ? k1 : k1b, ks & 3);
+            const uint32_t a0 = fp8x2_to_h2(w0 & 0xFFFFu), a1 = fp8x2_to_h2(w1 & 0xFFFFu);
+            const uint32_t a2 = fp8x2_to_h2(w0 >> 16), a3 = fp8x2_to_h2(w1 >> 16);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+                mma_16816(dq[nt][ks & 1], a0, a1, a2, a3, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
+        }
+        v[0] = lds64(sb + o.v0);
+        v[1] = lds64(sb + o.v1);
+        v[2] = lds64(sb + o.v0 + (o.row << 3));
+        v[3] = lds64(sb + o.v1 + (o.row << 3));
+        mbar_arrive(release_bar);
+    } else {
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(k0, ks >> 1), w1 = word_of(k1, ks >> 1);
@@ -775,6 +833,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
             mma_16816(dcs[1], e2.x, e2.y, e3.x, e3.y, e2.x, e3.x);
         }
     }
+    }  // table-decoded keys
     float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
     if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
         // norm correction c / |c| (reference/aos_decode.py:199-206), with
@@ -808,9 +867,12 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         // columns 2c / 2c+1: Q_hi / Q_lo parts of head c; rows g / g+8:
-        // C_hi / C_lo parts of the token
-        const float d0 = (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
-        const float d1 = (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
+        // C_hi / C_lo parts of the token (FP8 keys: tokens tau(g) / tau(g)+1,
+        // chains ks even / odd)
+        const float d0 = kFp8 ? (dq[nt][0][0] + dq[nt][0][1]) + (dq[nt][1][0] + dq[nt][1][1])
+                              : (dq[nt][0][0] + dq[nt][0][2]) + (dq[nt][0][1] + dq[nt][0][3]);
+        const float d1 = kFp8 ? (dq[nt][0][2] + dq[nt][0][3]) + (dq[nt][1][2] + dq[nt][1][3])
+                              : (dq[nt][1][0] + dq[nt][1][2]) + (dq[nt][1][1] + dq[nt][1][3]);
         float s0 = d0 * kn0 * st.kfac[nt];
         float s1 = d1 * kn1 * st.kfac[nt];
         s0 = va ? s0 : -INFINITY;
@@ -939,13 +1001,13 @@ template <int NT, int LAYOUT, int S>
 __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs, const LaneSmem& o, uint32_t& cbits,
                                           int k, int my_np, int w, int tok_first, int start, int end,
                                           uint32_t lut_sel_src, int g, int c, int src_a, float csq_unscale) {
-    constexpr int NS = Cfg<NT>::kStages;
+    constexpr int NS = Cfg<NT, LAYOUT>::kStages;
     if (!mbar_wait(gs.full(S), (cbits >> S) & 1u)) return false;
     cbits ^= 1u << S;
     // all 32 lanes arrive on the slot's release barrier (no branch on the lane)
     if (k < my_np) {
         const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
-        page_math<NT, LAYOUT>(st, (uint32_t)(S * kStageBytes), o, page_ok, tok_first + k * kBlockSize, start, end,
+        page_math<NT, LAYOUT>(st, (uint32_t)(S * stage_bytes(LAYOUT)), o, page_ok, tok_first + k * kBlockSize, start, end,
                       lut_sel_src, g, c, src_a, gs.empty<NS>(S), csq_unscale);
     } else {
         mbar_arrive(gs.empty<NS>(S));
@@ -956,7 +1018,7 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
 template <int NT, int LAYOUT>
 __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& gs, int gi, int w, int lane,
                                         int ec) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, LAYOUT>;
     constexpr int NS = C::kStages;
     const int g = lane >> 2, c = lane & 3;
     const uint32_t t_first = lds32(gs.tiles()), t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
@@ -975,6 +1037,20 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
         o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
         o.row = 0;
+    } else if constexpr (LAYOUT == TQB_LAYOUT_SOA_K8) {
+        // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
+        // (w - kvh) * 3136 bytes of the stage: [16 tokens][Hk][K 128 | V 64]
+        // then [Hk][vscale 16 | vzero 16] fp16.
+        const int kvh = w % P.Hk;
+        const uint32_t row = (uint32_t)P.Hk * kK8DataBytes;
+        const uint32_t run = gs.ring + (uint32_t)(w - kvh) * kK8Head;
+        const uint32_t head = run + (uint32_t)kvh * kK8DataBytes;
+        o.k0 = head + (uint32_t)tau * row + 32u * c;
+        o.k1 = o.k0 + row;
+        o.v0 = head + (uint32_t)(2 * c) * row + kK8KeyBytes + 8u * g;
+        o.v1 = o.v0 + row;
+        o.meta = run + (uint32_t)kBlockSize * row + (uint32_t)kvh * (2 * kBlockSize * 2) + 2u * tau;
+        o.row = row;
     } else {
         // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
         // (w - kvh) * 2144 bytes of the stage: [16 tokens][Hk][134-byte slot].
@@ -1077,15 +1153,16 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 template <int NT, int LAYOUT>
 __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     stage1_ring_kernel(const Stage1Params P, const __grid_constant__ RingMaps M) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, LAYOUT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---- K table: 256 entries x 32 lane copies of {C_hi pair, C_lo pair} ----
+    // (FP8 keys: no table, no centroids, no scale)
     float cmax = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
-    const int ec = fp16_scale_exp(cmax);
+    for (int k = 0; k < kNumCentroids; k++) cmax = C::kTable ? fmaxf(cmax, fabsf(__ldg(P.cents + k))) : 0.0f;
+    const int ec = C::kTable ? fp16_scale_exp(cmax) : 0;
     const float cscale = exp2i(ec);
     // The last kGroups warps plan the groups' tile walks (reading seq_lens)
     // while the others build the table.
@@ -1094,7 +1171,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     uint32_t walk[3] = {0u, 0u, 0u};
     if (planner >= 0)
         tile_walk(P, planner, C::kGroups, num_tiles, walk, lane);
-    else
+    else if (C::kTable)
         for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
         const int byte = e / kLutCopies;
         const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
@@ -1138,7 +1215,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     }
     __syncthreads();
 
-    if constexpr (NT == 1) {
+    if constexpr (NT == 1 && C::kTable) {  // the fused rotation (not for FP8 keys)
         if (P.rot != nullptr) {
             rotate_share<NT>(P, smem, tid);
             // generic writes to the ring and query areas, before the tensor
@@ -1170,7 +1247,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
 // so the ring kernel is not used).
 template <int NT, int LAYOUT>
 bool ring_registers_ok() {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, LAYOUT>;
     static int ok = -1;
     if (ok < 0) {
         cudaFuncAttributes a{};
@@ -1235,7 +1312,7 @@ bool encode_maps(const Stage1Params& P, RingMaps& M) {
 
 template <int NT, int LAYOUT>
 int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream, int num_sms) {
-    using C = Cfg<NT>;
+    using C = Cfg<NT, LAYOUT>;
     auto kern = stage1_ring_kernel<NT, LAYOUT>;
     static thread_local int configured_dev = -1;
     int dev = 0;
@@ -1278,14 +1355,22 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
 
 bool stage1_ring_supported(const Stage1Params& P) {
     const bool soa = P.layout == TQB_LAYOUT_SOA;
-    const bool regs_ok = soa ? (P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>())
-                             : (P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>());
     // AoS: a tile's runs are whole blocks (Hk divides 8) of packed slots, each
     // copied as one run of Hk * 2144 bytes.
     const bool aos_ok = P.layout == TQB_LAYOUT_AOS && kGroupWarps % P.Hk == 0 && P.head_stride == kAosSlot &&
                         P.pos_stride == (int64_t)P.Hk * kAosSlot;
+    // FP8 keys (SoA blocks, GQA <= 4): whole blocks too, Hk * 3136 bytes.
+    const bool k8_ok = P.layout == TQB_LAYOUT_SOA_K8 && kGroupWarps % P.Hk == 0 && P.G <= 4 &&
+                       P.block_bytes >= (int64_t)kBlockSize * P.Hk * kSlotBytesK8;
+    bool regs_ok = false;
+    if (soa)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>();
+    else if (aos_ok)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>();
+    else if (k8_ok)
+        regs_ok = ring_registers_ok<1, TQB_LAYOUT_SOA_K8>();
     // Query rows are copied by a tensor map: 16-byte row strides, >= one row.
-    return regs_ok && (soa || aos_ok) && P.G >= 1 && P.G <= 8 &&
+    return regs_ok && (soa || aos_ok || k8_ok) && P.G >= 1 && P.G <= 8 &&
            (reinterpret_cast<uintptr_t>(P.cache) & 15) == 0 && (P.block_bytes & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(P.q) & 15) == 0 && P.qsh >= kHeadDim && (P.qsh & 3) == 0 &&
            P.qsb >= P.qsh && (P.qsb & 3) == 0 && encoder() != nullptr;
@@ -1297,6 +1382,10 @@ int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) 
     if (P.layout == TQB_LAYOUT_SOA)
         return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA>(P, M, stream, num_sms)
                         : launch_ring_t<2, TQB_LAYOUT_SOA>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K8) {
+        if (P.rot != nullptr) return TQB_ERR_UNSUPPORTED;  // no rotation prologue in this instance
+        return launch_ring_t<1, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms);
+    }
     return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS>(P, M, stream, num_sms)
                     : launch_ring_t<2, TQB_LAYOUT_AOS>(P, M, stream, num_sms);
 }
