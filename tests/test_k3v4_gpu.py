@@ -165,3 +165,85 @@ def test_launchers_store_and_decode(cuda_device, layout, name, vbits, slot):
     assert_close(got[live], ref16, rtol=RTOL + 2.0 ** -7, what=f"{name} decode out")
     assert_close(lse.cpu().numpy()[live], ref_lse[live], what=f"{name} decode lse")
     assert np.all(np.isnan(got[~live]))
+
+
+def _k3_case(seed, lens, hq, hk, slot, vbits, pool_extra=3):
+    rng = np.random.default_rng(seed)
+    B = len(lens)
+    pages = [max(1, math.ceil(n / 16)) for n in lens]
+    nblk = sum(pages) + pool_extra
+    cache = rng.integers(0, 256, size=(nblk, 16, hk, slot), dtype=np.uint8)
+    perm = rng.permutation(nblk)
+    bt = np.zeros((B, max(pages)), np.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]]
+        k += pages[b]
+    slots = np.concatenate([bt[b, np.arange(n) // 16] * 16 + np.arange(n) % 16
+                            for b, n in enumerate(lens)]).astype(np.int32)
+    cents = tqb.get_centroids(128, 3).numpy()
+    mids = ((cents[:-1] + cents[1:]) * 0.5).astype(np.float32)
+    key = rng.standard_normal((len(slots) * hk, 128)).astype(np.float32)
+    norms = np.linalg.norm(key, axis=1).astype(np.float32)
+    R = np.linalg.qr(rng.standard_normal((128, 128)))[0].astype(np.float32)
+    y = ((key / norms[:, None]) @ R).astype(np.float32)
+    val = rng.standard_normal((len(slots) * hk, 128)).astype(np.float32)
+    O.store_k3_np(y, norms, val, mids, cents, slots, cache, vbits=vbits)
+    q = rng.standard_normal((B, hq, 128)).astype(np.float32)
+    return q, cache, bt, np.asarray(lens, np.int32), cents
+
+
+@pytest.mark.parametrize("layout,name,vbits,slot", PRESETS)
+@pytest.mark.parametrize("hq,hk", [(32, 8), (8, 2), (4, 1), (12, 4), (16, 8), (20, 4)])
+@pytest.mark.parametrize("kernel", ["default", "regs"])
+def test_stage1_page_ring_and_register_kernel(cuda_device, hq, hk, kernel, layout, name, vbits, slot, monkeypatch):
+    """3-bit keys on both Stage1 kernels: the TMA page ring (GQA <= 4 with Hk
+    dividing 8: whole blocks per page, keys decoded through the 6-bit-field
+    table, 3-bit values spread to nibbles) and the register-ring kernel
+    (TQB_STAGE1_KERNEL=regs, and GQA-5 always).  Ragged lengths with an empty
+    sequence and a split of more than 32 pages, against the float64 oracle."""
+    if kernel == "regs":
+        monkeypatch.setenv("TQB_STAGE1_KERNEL", "regs")
+    lens = [1, 0, 1100, 45, 300, 517, 2100]
+    q, cache, bt, sl, cents = _k3_case(91 + hq + 5 * hk + vbits, lens, hq, hk, slot, vbits, pool_extra=7)
+    S = 6
+    ref = O.stage1_np(q, cache, bt, sl, cents, S, layout=LAYOUT_ID[layout])
+    _check(_stage1(cuda_device, q, cache, bt, sl, cents, S, layout), ref, f"{name} Stage1 Hq{hq}/Hk{hk} ({kernel})")
+
+
+@pytest.mark.parametrize("layout,name,vbits,slot", PRESETS)
+def test_c1_3bit_decode_vs_oracle(cuda_device, layout, name, vbits, slot):
+    """The c1 shape (B64 x 4096, Hq32/Hk8, S32) with 3-bit keys (and
+    values), on the page ring: every partial, then Stage2, against the
+    float64 oracle on a cache written by the sm_100a store from seeded K/V."""
+    dev = cuda_device
+    B, L, Hq, Hk, S = 64, 4096, 32, 8, 32
+    gen = torch.Generator(device=dev).manual_seed(29 + vbits)
+    pages = L // 16
+    nblk = B * pages
+    bt = torch.randperm(nblk, device=dev, generator=gen).view(B, pages).to(torch.int32)
+    kv = torch.zeros(nblk, 16, Hk, slot, dtype=torch.uint8, device=dev)
+    cents = tqb.get_centroids(128, 3).to(dev)
+    mids = ((cents[:-1] + cents[1:]) * 0.5).contiguous()
+    tok = torch.arange(L, device=dev)
+    for b in range(B):  # one sequence per store call
+        slots = (bt[b, tok // 16] * 16 + tok % 16).to(torch.int32)
+        key = torch.randn(L * Hk, 128, device=dev, generator=gen)
+        norms = key.norm(dim=1)
+        y = (key / norms[:, None]).contiguous()  # unit keys (the rotation does not matter here)
+        val = torch.randn(L * Hk, 128, device=dev, generator=gen)
+        tqb.store(y, norms, val, kv, slots, mids, cents, layout=layout)
+    q = torch.randn(B, Hq, 128, device=dev, generator=gen)
+    sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+    mid = torch.full((B, Hq, S, 129), SENTINEL, device=dev)
+    tqb.stage1(q, kv, bt, sl, cents, mid, layout=layout)
+    out = torch.empty(B, Hq, 128, device=dev)
+    lse = torch.empty(B, Hq, device=dev)
+    tqb.stage2(mid, sl, out, lse)
+    torch.cuda.synchronize()
+    ref = O.stage1_np(q.cpu().numpy(), kv.cpu().numpy(), bt.cpu().numpy(), sl.cpu().numpy(), cents.cpu().numpy(), S,
+                      layout=LAYOUT_ID[layout])
+    _check(mid.cpu().numpy(), ref, f"c1 {name} Stage1")
+    ref_out, ref_lse = O.stage2_np(ref, sl.cpu().numpy())
+    assert_close(out.cpu().numpy(), ref_out, what=f"c1 {name} Stage2 out")
+    assert_close(lse.cpu().numpy(), ref_lse, what=f"c1 {name} Stage2 lse")

@@ -178,28 +178,6 @@ __device__ __forceinline__ void prefetch_block(const uint8_t* block, uint32_t by
     if (leader) prefetch_l2_bulk(block, bytes);
 }
 
-// Eight 3-bit fields (bits 3i .. 3i+2 of h, 24 bits) to eight nibbles
-// (bits 4i .. 4i+2): halves, then quarters, then pairs move apart.
-__device__ __forceinline__ uint32_t spread3to4(uint32_t h) {
-    const uint32_t z = (h & 0xFFFu) | ((h & 0xFFF000u) << 4);
-    const uint32_t w = (z & 0x003F003Fu) | ((z & 0x0FC00FC0u) << 2);
-    return (w & 0x07070707u) | ((w & 0x38383838u) << 1);
-}
-
-// Bits [o, o + 6) of the little-endian 96-bit stream k.x | k.y | k.z (o a
-// compile-time constant after unrolling, o + 6 <= 96).
-__device__ __forceinline__ uint32_t bits6(const uint4& k, int o) {
-    const int i = o >> 5;
-    const uint32_t lo = i == 0 ? k.x : i == 1 ? k.y : k.z;
-    const uint32_t hi = i == 0 ? k.y : i == 1 ? k.z : 0u;
-    return __funnelshift_r(lo, hi, (uint32_t)(o & 31)) & 63u;
-}
-
-// Two e4m3 bytes (low byte first) to an exact f16x2 (low half first).
-__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
-    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
-    return (uint32_t)h.x | ((uint32_t)h.y << 16);
-}
 
 // AoS slots are only 2-byte aligned: gather with 16-bit loads.
 __device__ __forceinline__ uint32_t ld2x16(const uint8_t* p) {

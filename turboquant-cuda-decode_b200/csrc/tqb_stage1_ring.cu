@@ -73,13 +73,18 @@ constexpr int kK8Head = kBlockSize * kSlotBytesK8;              // 3136: one hea
 constexpr int kK8StageBytes = 25600;                           // 8 x 3136, 1024-aligned
 static_assert(kGroupWarps * kK8Head <= kK8StageBytes && kK8StageBytes % 1024 == 0, "FP8-key stage");
 // Bytes of one ring stage, and of one head's page in it (SoA: 2048 data +
-// 96 metadata, AoS: 16 slots, FP8 keys: 16 x 192 data + 64 metadata).
+// 96 metadata, AoS: 16 slots, FP8 keys: 16 x 192 data + 64 metadata, 3-bit
+// keys: 16 x 112 (or 96 with 3-bit values) data + 96 metadata).
 __host__ __device__ constexpr int stage_bytes(int layout) {
     return layout == TQB_LAYOUT_SOA_K8 ? kK8StageBytes : kStageBytes;
 }
 __host__ __device__ constexpr int head_page_bytes(int layout) {
-    return layout == TQB_LAYOUT_SOA_K8 ? kK8Head : kAosHead;
+    return layout == TQB_LAYOUT_SOA_K8     ? kK8Head
+           : layout == TQB_LAYOUT_SOA_K3   ? kBlockSize * kSlotBytesK3    // 1888
+           : layout == TQB_LAYOUT_SOA_K3V3 ? kBlockSize * kSlotBytesK3V3  // 1632
+                                           : kAosHead;
 }
+static_assert(kGroupWarps * kBlockSize * kSlotBytesK3 <= kStageBytes, "3-bit-key stage");
 static_assert(kBlockSize * kDataBytes + kMetaSlot == kAosHead, "SoA and AoS heads take the same page bytes");
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
 constexpr int kLutAddr = 0x10000;                              // shared address of the table
@@ -257,11 +262,6 @@ __device__ __forceinline__ uint2 lds64_a2(uint32_t a) {
     const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
     const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8);
     return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
-}
-// Two e4m3 bytes (low byte first) to an exact f16x2 (low half first).
-__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
-    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
-    return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {
     const uint4 u = lds128(a);
@@ -738,10 +738,33 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     // release semantics: the reads above it are performed before the
     // producer can observe the arrival.
     constexpr bool kFp8 = LAYOUT == TQB_LAYOUT_SOA_K8;
+    constexpr bool kKey3 = layout_3bit_keys(LAYOUT);
     uint4 k0, k1, k0b, k1b;
     uint32_t kn, vsp, vzp;
     uint2 v[4];
-    if constexpr (kFp8) {
+    if constexpr (kKey3) {
+        // whole block [16 tokens][Hk][K 48 (3-bit) | V 64 (or 48, 3-bit)] +
+        // [Hk][knorm 16 | vscale 16 | vzero 16]: key bits of dims
+        // [32c, 32c+32) = bytes [12c, 12c+12) of tokens tau(g), tau(g)+1
+        k0 = make_uint4(lds32(sb + o.k0), lds32(sb + o.k0 + 4u), lds32(sb + o.k0 + 8u), 0u);
+        k1 = make_uint4(lds32(sb + o.k1), lds32(sb + o.k1 + 4u), lds32(sb + o.k1 + 8u), 0u);
+        kn = lds32(sb + o.meta);
+        vsp = lds32(sb + o.meta + 32u);
+        vzp = lds32(sb + o.meta + 64u);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t va = sb + (j & 1 ? o.v1 : o.v0) + (j & 2 ? (o.row << 3) : 0u);
+            if constexpr (layout_3bit_values(LAYOUT)) {
+                // 16 3-bit codes (6 bytes, 2-byte aligned) spread to the
+                // nibble layout of the 4-bit values (low nibble = even dim)
+                const uint32_t a = lds16(va), b = lds16(va + 2u), cc = lds16(va + 4u);
+                v[j] = make_uint2(spread3to4((a | (b << 16)) & 0xFFFFFFu), spread3to4((b >> 8) | (cc << 8)));
+            } else {
+                v[j] = lds64(va);
+            }
+        }
+        mbar_arrive(release_bar);
+    } else if constexpr (kFp8) {
         // whole block [16 tokens][Hk][K 128 e4m3 | V 64] + [Hk][vscale 16 |
         // vzero 16]: key bytes [32c, 32c+32) of tokens tau(g), tau(g)+1
         k0 = lds128(sb + o.k0);
@@ -814,15 +837,27 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         v[3] = lds64(sb + o.v1 + (o.row << 3));
         mbar_arrive(release_bar);
     } else {
+    // 3-bit keys: table address 0x10000 | (6-bit field << 8) | lane copy offset
+    const uint32_t lut_lane = __byte_perm(lut_sel_src, 0u, 0x4140u);
 #pragma unroll
     for (int ks = 0; ks < 8; ks++) {
         const uint32_t w0 = word_of(k0, ks >> 1), w1 = word_of(k1, ks >> 1);
         const uint32_t jA = 2 * (ks & 1), jB = jA + 1;
-        // address 0x10000 | (K byte << 8) | lane copy offset, in one PRMT
-        const uint2 e0 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jA << 4)));
-        const uint2 e1 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jB << 4)));
-        const uint2 e2 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jA << 4)));
-        const uint2 e3 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jB << 4)));
+        uint2 e0, e1, e2, e3;
+        if constexpr (kKey3) {
+            // dim pairs 32c + 4ks + {0,1} and {2,3}: the 6-bit fields at bits
+            // 12ks and 12ks + 6 of the lane's 96 bits
+            e0 = lut_ld((bits6(k0, 12 * ks) << 8) + lut_lane);
+            e1 = lut_ld((bits6(k0, 12 * ks + 6) << 8) + lut_lane);
+            e2 = lut_ld((bits6(k1, 12 * ks) << 8) + lut_lane);
+            e3 = lut_ld((bits6(k1, 12 * ks + 6) << 8) + lut_lane);
+        } else {
+            // address 0x10000 | (K byte << 8) | lane copy offset, in one PRMT
+            e0 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jA << 4)));
+            e1 = lut_ld(prmt(w0, lut_sel_src, 0x6504u | (jB << 4)));
+            e2 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jA << 4)));
+            e3 = lut_ld(prmt(w1, lut_sel_src, 0x6504u | (jB << 4)));
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
@@ -1037,6 +1072,22 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
         o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
         o.row = 0;
+    } else if constexpr (layout_3bit_keys(LAYOUT)) {
+        // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
+        // (w - kvh) * 16 * slot bytes of the stage: [16 tokens][Hk][K 48 | V]
+        // then [Hk][knorm 16 | vscale 16 | vzero 16] fp16.
+        constexpr uint32_t kDps = layout_3bit_values(LAYOUT) ? kK3V3DataBytes : kK3DataBytes;
+        constexpr uint32_t kValLane = layout_3bit_values(LAYOUT) ? 6u : 8u;  // V bytes of dims 16g .. 16g+15
+        const int kvh = w % P.Hk;
+        const uint32_t row = (uint32_t)P.Hk * kDps;
+        const uint32_t run = gs.ring + (uint32_t)(w - kvh) * (uint32_t)head_page_bytes(LAYOUT);
+        const uint32_t head = run + (uint32_t)kvh * kDps;
+        o.k0 = head + (uint32_t)tau * row + 12u * c;
+        o.k1 = o.k0 + row;
+        o.v0 = head + (uint32_t)(2 * c) * row + kK3KeyBytes + kValLane * g;
+        o.v1 = o.v0 + row;
+        o.meta = run + (uint32_t)kBlockSize * row + (uint32_t)kvh * kMetaSlot + 2u * tau;
+        o.row = row;
     } else if constexpr (LAYOUT == TQB_LAYOUT_SOA_K8) {
         // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
         // (w - kvh) * 3136 bytes of the stage: [16 tokens][Hk][K 128 | V 64]
@@ -1158,10 +1209,13 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---- K table: 256 entries x 32 lane copies of {C_hi pair, C_lo pair} ----
-    // (FP8 keys: no table, no centroids, no scale)
+    // (FP8 keys: no table, no centroids, no scale; 3-bit keys: 8 centroids,
+    // entry = 6-bit field of two codes, low code in bits 0-2)
+    constexpr bool kKey3 = layout_3bit_keys(LAYOUT);
+    constexpr int kNc = C::kTable ? (kKey3 ? 8 : kNumCentroids) : 0;
     float cmax = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kNumCentroids; k++) cmax = C::kTable ? fmaxf(cmax, fabsf(__ldg(P.cents + k))) : 0.0f;
+    for (int k = 0; k < kNc; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
     const int ec = C::kTable ? fp16_scale_exp(cmax) : 0;
     const float cscale = exp2i(ec);
     // The last kGroups warps plan the groups' tile walks (reading seq_lens)
@@ -1174,7 +1228,8 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     else if (C::kTable)
         for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
         const int byte = e / kLutCopies;
-        const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
+        const int ilo = kKey3 ? (byte & 7) : (byte & 15), ihi = kKey3 ? ((byte >> 3) & 7) : (byte >> 4);
+        const float clo = __ldg(P.cents + ilo) * cscale, chi = __ldg(P.cents + ihi) * cscale;
         const __half2 h = __floats2half2_rn(clo, chi);
         const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
         *reinterpret_cast<uint2*>(smem + C::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
@@ -1362,6 +1417,10 @@ bool stage1_ring_supported(const Stage1Params& P) {
     // FP8 keys (SoA blocks, GQA <= 4): whole blocks too, Hk * 3136 bytes.
     const bool k8_ok = P.layout == TQB_LAYOUT_SOA_K8 && kGroupWarps % P.Hk == 0 && P.G <= 4 &&
                        P.block_bytes >= (int64_t)kBlockSize * P.Hk * kSlotBytesK8;
+    // 3-bit keys (SoA blocks, GQA <= 4): whole blocks, Hk * 1888 (or 1632) bytes.
+    const bool k3_ok = (P.layout == TQB_LAYOUT_SOA_K3 || P.layout == TQB_LAYOUT_SOA_K3V3) &&
+                       kGroupWarps % P.Hk == 0 && P.G <= 4 &&
+                       P.block_bytes >= (int64_t)P.Hk * head_page_bytes(P.layout);
     bool regs_ok = false;
     if (soa)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>();
@@ -1369,8 +1428,11 @@ bool stage1_ring_supported(const Stage1Params& P) {
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>();
     else if (k8_ok)
         regs_ok = ring_registers_ok<1, TQB_LAYOUT_SOA_K8>();
+    else if (k3_ok)
+        regs_ok = P.layout == TQB_LAYOUT_SOA_K3 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K3>()
+                                                : ring_registers_ok<1, TQB_LAYOUT_SOA_K3V3>();
     // Query rows are copied by a tensor map: 16-byte row strides, >= one row.
-    return regs_ok && (soa || aos_ok || k8_ok) && P.G >= 1 && P.G <= 8 &&
+    return regs_ok && (soa || aos_ok || k8_ok || k3_ok) && P.G >= 1 && P.G <= 8 &&
            (reinterpret_cast<uintptr_t>(P.cache) & 15) == 0 && (P.block_bytes & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(P.q) & 15) == 0 && P.qsh >= kHeadDim && (P.qsh & 3) == 0 &&
            P.qsb >= P.qsh && (P.qsb & 3) == 0 && encoder() != nullptr;
@@ -1386,6 +1448,8 @@ int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) 
         if (P.rot != nullptr) return TQB_ERR_UNSUPPORTED;  // no rotation prologue in this instance
         return launch_ring_t<1, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms);
     }
+    if (P.layout == TQB_LAYOUT_SOA_K3) return launch_ring_t<1, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K3V3) return launch_ring_t<1, TQB_LAYOUT_SOA_K3V3>(P, M, stream, num_sms);
     return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS>(P, M, stream, num_sms)
                     : launch_ring_t<2, TQB_LAYOUT_AOS>(P, M, stream, num_sms);
 }
