@@ -84,7 +84,19 @@ __host__ __device__ constexpr int head_page_bytes(int layout) {
            : layout == TQB_LAYOUT_SOA_K3V3 ? kBlockSize * kSlotBytesK3V3  // 1632
                                            : kAosHead;
 }
-static_assert(kGroupWarps * kBlockSize * kSlotBytesK3 <= kStageBytes, "3-bit-key stage");
+// Shared-memory bytes per head of a page: 3-bit-key blocks land row by row,
+// token row t at t * row + 16 * (t >> 1) (112 bytes of padding in all), so
+// that the eight token rows tau(g) the compute warps read at once start 4
+// banks apart (a whole block copied unchanged has rows 896 or 768 bytes
+// apart, all on the same banks).
+constexpr int kK3RowPad = 16 * (kBlockSize / 2 - 1);  // 112
+__host__ __device__ constexpr int head_stride_bytes(int layout) {
+    return layout == TQB_LAYOUT_SOA_K3 || layout == TQB_LAYOUT_SOA_K3V3 ? head_page_bytes(layout) + kK3RowPad
+                                                                        : head_page_bytes(layout);
+}
+static_assert(kGroupWarps * head_stride_bytes(TQB_LAYOUT_SOA_K3) <= kStageBytes &&
+                  head_stride_bytes(TQB_LAYOUT_SOA_K3) % 16 == 0 && head_stride_bytes(TQB_LAYOUT_SOA_K3V3) % 16 == 0,
+              "3-bit-key stage");
 static_assert(kBlockSize * kDataBytes + kMetaSlot == kAosHead, "SoA and AoS heads take the same page bytes");
 constexpr int kLutBytes = 256 * kLutStride;                    // 64 KB
 constexpr int kLutAddr = 0x10000;                              // shared address of the table
@@ -556,7 +568,10 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
                                         int lane, int pj, int npj) {
     using C = Cfg<NT, LAYOUT>;
     constexpr bool kWholeBlock = LAYOUT != TQB_LAYOUT_SOA;  // pages copied as whole blocks
+    constexpr bool kRowCopies = layout_3bit_keys(LAYOUT);   // ... row by row, rows padded apart
     constexpr uint32_t kHeadPage = (uint32_t)head_page_bytes(LAYOUT);
+    constexpr uint32_t kHeadStride = (uint32_t)head_stride_bytes(LAYOUT);
+    constexpr uint32_t kDps = layout_3bit_values(LAYOUT) ? kK3V3DataBytes : kK3DataBytes;
     constexpr int NS = C::kStages;
     const uint32_t t_end = lds32(gs.tiles() + 4u), t_stride = lds32(gs.tiles() + 8u);
     const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
@@ -667,7 +682,29 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             // heads (one box when the run is a whole group) and its metadata
             // (SoA), or its whole block, unchanged, in one bulk copy (AoS and
             // FP8 keys: a run is all Hk heads of one (b, s), Hk dividing 8).
-            if (kWholeBlock && mine && here) {
+            if (kRowCopies) {
+                // 3-bit keys: run r's block as 16 token rows (row t at
+                // t * row + 16 * (t >> 1)) and its metadata after them, lanes
+                // 0-15 a row each, lane 16 the metadata.
+                if (mine) {
+                    for (int r = 0; r < nruns; r++) {
+                        const int rcol = __shfl_sync(0xffffffffu, col, r);
+                        const uint32_t rid = __shfl_sync(0xffffffffu, my_id, r);
+                        const int rhere = __shfl_sync(0xffffffffu, here ? r_nw : 0, r);
+                        if (rhere > 0 && lane <= kBlockSize) {
+                            const uint32_t rowb = (uint32_t)rhere * kDps;  // a run is a whole block: Hk heads
+                            const uint32_t dst = gs.template stage<LAYOUT>(slot) + (uint32_t)rcol * kHeadStride;
+                            const uint8_t* src = P.cache + (uint64_t)rid * (uint64_t)P.block_bytes;
+                            if (lane < kBlockSize)
+                                bulk_g2s(dst + (uint32_t)lane * rowb + 16u * (uint32_t)(lane >> 1),
+                                         src + (uint32_t)lane * rowb, rowb, gs.full(slot), stream_policy);
+                            else
+                                bulk_g2s(dst + kBlockSize * rowb + (uint32_t)kK3RowPad, src + kBlockSize * rowb,
+                                         (uint32_t)rhere * kMetaSlot, gs.full(slot), stream_policy);
+                        }
+                    }
+                }
+            } else if (kWholeBlock && mine && here) {
                 bulk_g2s(gs.template stage<LAYOUT>(slot) + (uint32_t)col * kHeadPage,
                          P.cache + (uint64_t)my_id * (uint64_t)P.block_bytes, (uint32_t)r_nw * kHeadPage, gs.full(slot),
                          stream_policy);
@@ -753,7 +790,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         vzp = lds32(sb + o.meta + 64u);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint32_t va = sb + (j & 1 ? o.v1 : o.v0) + (j & 2 ? (o.row << 3) : 0u);
+            const uint32_t va = sb + (j & 1 ? o.v1 : o.v0) + (j & 2 ? (o.row << 3) + 64u : 0u);
             if constexpr (layout_3bit_values(LAYOUT)) {
                 // 16 3-bit codes (6 bytes, 2-byte aligned) spread to the
                 // nibble layout of the 4-bit values (low nibble = even dim)
@@ -1078,15 +1115,18 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         // then [Hk][knorm 16 | vscale 16 | vzero 16] fp16.
         constexpr uint32_t kDps = layout_3bit_values(LAYOUT) ? kK3V3DataBytes : kK3DataBytes;
         constexpr uint32_t kValLane = layout_3bit_values(LAYOUT) ? 6u : 8u;  // V bytes of dims 16g .. 16g+15
+        // Rows sit padded apart (token t at t * row + 16 * (t >> 1)); tokens
+        // 2m and 2m+1 share a pad, so o.k1 = o.k0 + row, and tokens 2c+8,
+        // 2c+9 are 8 rows and 64 pad bytes after 2c, 2c+1.
         const int kvh = w % P.Hk;
         const uint32_t row = (uint32_t)P.Hk * kDps;
-        const uint32_t run = gs.ring + (uint32_t)(w - kvh) * (uint32_t)head_page_bytes(LAYOUT);
+        const uint32_t run = gs.ring + (uint32_t)(w - kvh) * (uint32_t)head_stride_bytes(LAYOUT);
         const uint32_t head = run + (uint32_t)kvh * kDps;
-        o.k0 = head + (uint32_t)tau * row + 12u * c;
+        o.k0 = head + (uint32_t)tau * row + 8u * (uint32_t)tau + 12u * c;
         o.k1 = o.k0 + row;
-        o.v0 = head + (uint32_t)(2 * c) * row + kK3KeyBytes + kValLane * g;
+        o.v0 = head + (uint32_t)(2 * c) * row + 16u * c + kK3KeyBytes + kValLane * g;
         o.v1 = o.v0 + row;
-        o.meta = run + (uint32_t)kBlockSize * row + (uint32_t)kvh * kMetaSlot + 2u * tau;
+        o.meta = run + (uint32_t)kBlockSize * row + (uint32_t)kK3RowPad + (uint32_t)kvh * kMetaSlot + 2u * tau;
         o.row = row;
     } else if constexpr (LAYOUT == TQB_LAYOUT_SOA_K8) {
         // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
