@@ -683,21 +683,21 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
             // (SoA), or its whole block, unchanged, in one bulk copy (AoS and
             // FP8 keys: a run is all Hk heads of one (b, s), Hk dividing 8).
             if (kRowCopies) {
-                // 3-bit keys: run r's block as 16 token rows (row t at
-                // t * row + 16 * (t >> 1)) and its metadata after them, lanes
-                // 0-15 a row each, lane 16 the metadata.
+                // 3-bit keys: run r's block as 8 pairs of token rows (rows
+                // 2m and 2m + 1 at 2m * row + 16m, one copy) and its metadata
+                // after them, lanes 0-7 a pair each, lane 8 the metadata.
                 if (mine) {
                     for (int r = 0; r < nruns; r++) {
                         const int rcol = __shfl_sync(0xffffffffu, col, r);
                         const uint32_t rid = __shfl_sync(0xffffffffu, my_id, r);
                         const int rhere = __shfl_sync(0xffffffffu, here ? r_nw : 0, r);
-                        if (rhere > 0 && lane <= kBlockSize) {
+                        if (rhere > 0 && lane <= kBlockSize / 2) {
                             const uint32_t rowb = (uint32_t)rhere * kDps;  // a run is a whole block: Hk heads
                             const uint32_t dst = gs.template stage<LAYOUT>(slot) + (uint32_t)rcol * kHeadStride;
                             const uint8_t* src = P.cache + (uint64_t)rid * (uint64_t)P.block_bytes;
-                            if (lane < kBlockSize)
-                                bulk_g2s(dst + (uint32_t)lane * rowb + 16u * (uint32_t)(lane >> 1),
-                                         src + (uint32_t)lane * rowb, rowb, gs.full(slot), stream_policy);
+                            if (lane < kBlockSize / 2)
+                                bulk_g2s(dst + (uint32_t)(2 * lane) * rowb + 16u * (uint32_t)lane,
+                                         src + (uint32_t)(2 * lane) * rowb, 2u * rowb, gs.full(slot), stream_policy);
                             else
                                 bulk_g2s(dst + kBlockSize * rowb + (uint32_t)kK3RowPad, src + kBlockSize * rowb,
                                          (uint32_t)rhere * kMetaSlot, gs.full(slot), stream_policy);
