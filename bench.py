@@ -993,9 +993,11 @@ def main():
         return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
-    if args.layout in ("soa_k8", "soa_k3", "soa_k3v3") and args.config != "c1":
-        raise SystemExit("--layout soa_k8 / soa_k3 / soa_k3v3 run the single-GPU c1 workload only")
-    if args.impl == "ours" and args.config != "c1":
+    preset = args.layout in ("soa_k8", "soa_k3", "soa_k3v3")
+    if preset and (args.config not in ("c1", "c3") or world > 1):
+        raise SystemExit("--layout soa_k8 / soa_k3 / soa_k3v3 run on one GPU: the c1 workload, or c3's GQA-8 "
+                         "shape unsharded")
+    if args.impl == "ours" and args.config != "c1" and not preset:
         for c in args.config.split(","):
             args.config = c
             run_sharded(args, world, rank, local)
@@ -1018,6 +1020,8 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = CONFIGS[args.config]
+    if args.config == "c3":  # a preset cache at c3's GQA-8 shape, on one GPU
+        cfg = dict(cfg, workload=cfg["workload"].replace("TP by KV head", "one GPU, unsharded"))
     w = build_workload(cfg, args.seed + 1000 * rank, dev, args.layout)
     B, Hq, S = w["B"], w["Hq"], w["S"]
     mid = torch.empty(B, Hq, S, 129, device=dev)

@@ -1454,23 +1454,23 @@ bool stage1_ring_supported(const Stage1Params& P) {
     // copied as one run of Hk * 2144 bytes.
     const bool aos_ok = P.layout == TQB_LAYOUT_AOS && kGroupWarps % P.Hk == 0 && P.head_stride == kAosSlot &&
                         P.pos_stride == (int64_t)P.Hk * kAosSlot;
-    // FP8 keys (SoA blocks, GQA <= 4): whole blocks too, Hk * 3136 bytes.
-    const bool k8_ok = P.layout == TQB_LAYOUT_SOA_K8 && kGroupWarps % P.Hk == 0 && P.G <= 4 &&
+    // FP8 keys (SoA blocks): whole blocks too, Hk * 3136 bytes.
+    const bool k8_ok = P.layout == TQB_LAYOUT_SOA_K8 && kGroupWarps % P.Hk == 0 &&
                        P.block_bytes >= (int64_t)kBlockSize * P.Hk * kSlotBytesK8;
-    // 3-bit keys (SoA blocks, GQA <= 4): whole blocks, Hk * 1888 (or 1632) bytes.
+    // 3-bit keys (SoA blocks): whole blocks, Hk * 1888 (or 1632) bytes.
     const bool k3_ok = (P.layout == TQB_LAYOUT_SOA_K3 || P.layout == TQB_LAYOUT_SOA_K3V3) &&
-                       kGroupWarps % P.Hk == 0 && P.G <= 4 &&
-                       P.block_bytes >= (int64_t)P.Hk * head_page_bytes(P.layout);
+                       kGroupWarps % P.Hk == 0 && P.block_bytes >= (int64_t)P.Hk * head_page_bytes(P.layout);
     bool regs_ok = false;
     if (soa)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>();
     else if (aos_ok)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>();
     else if (k8_ok)
-        regs_ok = ring_registers_ok<1, TQB_LAYOUT_SOA_K8>();
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K8>() : ring_registers_ok<2, TQB_LAYOUT_SOA_K8>();
+    else if (k3_ok && P.layout == TQB_LAYOUT_SOA_K3)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K3>() : ring_registers_ok<2, TQB_LAYOUT_SOA_K3>();
     else if (k3_ok)
-        regs_ok = P.layout == TQB_LAYOUT_SOA_K3 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K3>()
-                                                : ring_registers_ok<1, TQB_LAYOUT_SOA_K3V3>();
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K3V3>() : ring_registers_ok<2, TQB_LAYOUT_SOA_K3V3>();
     // Query rows are copied by a tensor map: 16-byte row strides, >= one row.
     return regs_ok && (soa || aos_ok || k8_ok || k3_ok) && P.G >= 1 && P.G <= 8 &&
            (reinterpret_cast<uintptr_t>(P.cache) & 15) == 0 && (P.block_bytes & 15) == 0 &&
@@ -1486,10 +1486,15 @@ int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) 
                         : launch_ring_t<2, TQB_LAYOUT_SOA>(P, M, stream, num_sms);
     if (P.layout == TQB_LAYOUT_SOA_K8) {
         if (P.rot != nullptr) return TQB_ERR_UNSUPPORTED;  // no rotation prologue in this instance
-        return launch_ring_t<1, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms);
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms);
     }
-    if (P.layout == TQB_LAYOUT_SOA_K3) return launch_ring_t<1, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms);
-    if (P.layout == TQB_LAYOUT_SOA_K3V3) return launch_ring_t<1, TQB_LAYOUT_SOA_K3V3>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K3)
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_SOA_K3V3)
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA_K3V3>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_SOA_K3V3>(P, M, stream, num_sms);
     return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS>(P, M, stream, num_sms)
                     : launch_ring_t<2, TQB_LAYOUT_AOS>(P, M, stream, num_sms);
 }
