@@ -217,8 +217,10 @@ int tqb_rotate_query(const tqb_rotate_args* args, cudaStream_t stream);
  * for tqb_rotate_query, and its output must be Stage1's query: rot->q_rot ==
  * s1->q_rot with the same strides, batch and heads.  On return q_rot holds
  * float(query) @ rotation (bit-identical to tqb_rotate_query) and mid_o the
- * Stage1 result.  Where the page-ring Stage1 serves the cache (SoA, or AoS
- * with Hk dividing 8) and the GQA group is at most 4, this is ONE kernel: a
+ * Stage1 result.  Where the page-ring Stage1 serves the cache (4-bit or
+ * 3-bit-key SoA, or 4-bit AoS, the whole-block forms with Hk dividing 8; not
+ * FP8 keys, whose query the reference does not rotate) and the GQA group is
+ * at most 4, this is ONE kernel: a
  * cooperative launch of one CTA per SM whose prologue rotates an equal
  * share of the rows, followed by a grid barrier (a static counter of the
  * library, bounded wait); otherwise tqb_rotate_query then tqb_stage1 on the
@@ -360,8 +362,8 @@ typedef struct tqb_sp_merge_args {
 
 int tqb_sp_merge(const tqb_sp_merge_args* args, cudaStream_t stream);
 
-/* Diagnostics (no reference counterpart).  The SoA Stage1 kernel paces its
- * TMA page ring with mbarrier waits that give up after about a second; each
+/* Diagnostics (no reference counterpart).  The page-ring Stage1 kernel paces
+ * its TMA page ring with mbarrier waits that give up after about a second; each
  * wait that gives up adds one to a per-device counter (the kernel then ends
  * early and its mid_o is not valid).  Copies the counter of the current
  * device into *count and clears it when `reset` is non-zero.  Synchronous:
