@@ -913,6 +913,11 @@ def measure_e2e(args, w, dev, world: int, B: int, Hq: int, S: int) -> dict:
     K = args.e2e_steps
     sets = [make_set(), make_set()]
     streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    # the output every step must reproduce (the computation is deterministic)
+    with torch.cuda.stream(streams[0]):
+        e2e_step(sets[0])
+    streams[0].synchronize()
+    expected = sets[0]["hout"].clone()
 
     def timed(run) -> float:
         torch.cuda.synchronize(dev)
@@ -969,13 +974,21 @@ def measure_e2e(args, w, dev, world: int, B: int, Hq: int, S: int) -> dict:
                 graphs[i % 2].replay()
 
     serial_ms = timed(run_serial)
+    for st_ in sets:
+        st_["hout"].zero_()
     piped_ms = timed(run_pipelined)
     del graphs
+    # the last step of each buffer set, copied back to the host, against the
+    # eager output: a race between the pipelined steps would show here
+    same = [bool(torch.equal(st_["hout"].view(torch.int16), expected.view(torch.int16))) for st_ in sets]
+    if not all(same):
+        raise RuntimeError(f"e2e: the pipelined steps' outputs differ from the eager output ({same})")
     st = sets[0]
     h2d = st["hbuf"].numel()  # the packed buffer, padding included
     d2h = st["hout"].numel() * st["hout"].element_size()
     return {"value": world * B / (piped_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": piped_ms, "steps": K,
+            "output_check": "the last pipelined step of each buffer set equals the eager output bit for bit",
             "serial_graph": {"value": world * B / (serial_ms * 1e-3), "ms_per_step": serial_ms},
             "serial_eager": {"value": world * B / (eager_ms * 1e-3), "ms_per_step": eager_ms},
             "path": "tqb.triton_turboquant_decode_attention (fused query cast + rotation, Stage1, Stage2 "

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
 
@@ -105,6 +106,34 @@ __device__ __forceinline__ int fp16_scale_exp(float max_abs) {
 
 // 2^e for integer e in [-126, 127], built from the exponent bits.
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// Programmatic dependent launch (PTX griddepcontrol, sm_90 and later).  A
+// kernel launched by launch_pdl may be scheduled while the kernel before it
+// on the stream is still running; pdl_wait blocks until that kernel has
+// completed and its memory operations are visible, so it comes before the
+// first global access.  pdl_trigger lets the next kernel be scheduled once
+// every CTA of this one has issued it.  Both are no-ops in a kernel launched
+// without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+#ifdef __CUDACC__
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+#endif
 
 // Hardware reciprocal and base-2 logarithm (relative error about 2^-23).
 __device__ __forceinline__ float rcp_approx(float x) {

@@ -92,6 +92,8 @@ __device__ __forceinline__ unsigned long long call_epoch(unsigned long long give
 // One CTA (kExchangeWarps warps) per (b, h): Stage2 merge of the local
 // splits, then the tagged row to every rank (threads 0-127).
 __global__ void __launch_bounds__(kExchangeWarps * 32) sp_exchange_kernel(const SpExchangeParams P) {
+    pdl_trigger();
+    pdl_wait();  // the local Stage1's partials
     const int64_t item = blockIdx.x;  // b * Hq + h
     const int b = (int)(item / P.s2.Hq), h = (int)(item % P.s2.Hq);
     const P2PLayout L(P.world, P.cap_rows);
@@ -114,6 +116,8 @@ __global__ void __launch_bounds__(kExchangeWarps * 32) sp_exchange_kernel(const 
 // of this row from every rank (waiting for this epoch's tags), then merges
 // them; the last CTA advances the device epoch.
 __global__ void __launch_bounds__(kHeadDim) sp_merge_kernel(const SpMergeParams P) {
+    pdl_trigger();
+    pdl_wait();  // the local exchange (its reads of step happen before this kernel stores it)
     const int64_t item = blockIdx.x;
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
     const int d = threadIdx.x;
@@ -199,15 +203,13 @@ int64_t p2p_buffer_bytes(int world, int64_t cap_rows) { return P2PLayout(world, 
 int launch_sp_exchange(const SpExchangeParams& P, cudaStream_t stream) {
     const int64_t items = (int64_t)P.s2.B * P.s2.Hq;
     if (items == 0) return TQB_OK;
-    sp_exchange_kernel<<<(unsigned)items, kExchangeWarps * 32, 0, stream>>>(P);
-    return report_launch(cudaGetLastError());
+    return report_launch(launch_pdl(sp_exchange_kernel, dim3((unsigned)items), dim3(kExchangeWarps * 32), 0, stream, P));
 }
 
 int launch_sp_merge(const SpMergeParams& P, cudaStream_t stream) {
     const int64_t items = (int64_t)P.B * P.Hq;
     if (items == 0) return TQB_OK;
-    sp_merge_kernel<<<(unsigned)items, kHeadDim, 0, stream>>>(P);
-    return report_launch(cudaGetLastError());
+    return report_launch(launch_pdl(sp_merge_kernel, dim3((unsigned)items), dim3(kHeadDim), 0, stream, P));
 }
 
 int read_p2p_timeouts(unsigned int* count, bool reset) {

@@ -492,6 +492,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kMinBlocksNT1 : 1)
     constexpr int kEntry = kNormCorr ? 16 : 8;
     constexpr int kCopies = kLutStride / kEntry;
     extern __shared__ __align__(1024) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();  // the kernel before on the stream (e.g. the previous step's Stage2 reading mid_o)
     float* stage_all = reinterpret_cast<float*>(smem + kLutBytes);
 
     const int tid = threadIdx.x;
@@ -727,8 +729,7 @@ int launch_t(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     const int64_t need = (P.num_items + kWarps - 1) / kWarps;
     const int64_t grid = need < (int64_t)num_sms * per_sm ? need : (int64_t)num_sms * per_sm;
     if (grid <= 0) return TQB_OK;
-    kern<<<(unsigned)grid, kThreads, smem, stream>>>(P);
-    return report_launch(cudaGetLastError());
+    return report_launch(launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), smem, stream, P));
 }
 
 }  // namespace

@@ -1247,6 +1247,8 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     using C = Cfg<NT, LAYOUT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    pdl_wait();  // the kernel before on the stream (e.g. the previous step's Stage2 reading mid_o)
 
     // ---- K table: 256 entries x 32 lane copies of {C_hi pair, C_lo pair} ----
     // (FP8 keys: no table, no centroids, no scale; 3-bit keys: 8 centroids,
@@ -1442,8 +1444,7 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
     const int64_t need = (tiles + C::kGroups - 1) / C::kGroups;
     const int64_t grid = need < num_sms ? need : num_sms;
     if (grid <= 0) return TQB_OK;
-    kern<<<(unsigned)grid, C::kThreads, C::kSmem, stream>>>(P, M);
-    return report_launch(cudaGetLastError());
+    return report_launch(launch_pdl(kern, dim3((unsigned)grid), dim3(C::kThreads), C::kSmem, stream, P, M));
 }
 
 }  // namespace

@@ -34,6 +34,8 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 // row's non-empty splits; thread d writes output dim d, thread 0 the LSE.
 template <typename OutT>
 __global__ void __launch_bounds__(kHeadDim, 8) stage2_kernel(const Stage2Params P) {
+    pdl_trigger();
+    pdl_wait();  // Stage1's partials, when it ran just before on the stream
     const int64_t item = blockIdx.x;  // b * Hq + h
     const int b = (int)(item / P.Hq), h = (int)(item % P.Hq);
     float o, lse;
@@ -104,12 +106,12 @@ int launch_stage2(const Stage2Params& P, cudaStream_t stream) {
     const int64_t items = (int64_t)P.B * P.Hq;
     if (items == 0) return TQB_OK;
     switch (P.out_dtype) {
-        case TQB_DTYPE_F32: stage2_kernel<float><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
-        case TQB_DTYPE_F16: stage2_kernel<__half><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
-        case TQB_DTYPE_BF16: stage2_kernel<__nv_bfloat16><<<(unsigned)items, kHeadDim, 0, stream>>>(P); break;
+        case TQB_DTYPE_F32: return report_launch(launch_pdl(stage2_kernel<float>, dim3((unsigned)items), dim3(kHeadDim), 0, stream, P));
+        case TQB_DTYPE_F16: return report_launch(launch_pdl(stage2_kernel<__half>, dim3((unsigned)items), dim3(kHeadDim), 0, stream, P));
+        case TQB_DTYPE_BF16:
+            return report_launch(launch_pdl(stage2_kernel<__nv_bfloat16>, dim3((unsigned)items), dim3(kHeadDim), 0, stream, P));
         default: return TQB_ERR_INVALID_ARG;
     }
-    return report_launch(cudaGetLastError());
 }
 
 int launch_merge(const MergeParams& P, cudaStream_t stream) {
