@@ -73,6 +73,24 @@ CONFIGS = {
                         "the merge kernel combines any split count)"),
 }
 FALLBACK_HBM_GBS = 6650.0
+# The arithmetic each cache layout computes in, by its key/value code suffix.
+LAYOUT_DTYPE = {
+    "_k4": "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)",
+    "_k8": "f32 (e4m3 K, 4-bit V codes, fp16 tensor-core MMA, fp32 accumulate)",
+    "_k3": "f32 (3-bit K / 4-bit V codes, fp16-split tensor-core MMA, fp32 accumulate)",
+    "_k3v3": "f32 (3-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)",
+}
+# The Stage1 kernel each layout runs on (Hk dividing 8, as in every config).
+STAGE1_KERNEL = {
+    "soa": "tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)",
+    "aos": "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)",
+    "soa_k8": "tqb stage1_ring_kernel (TMA page ring: whole FP8-key blocks by bulk copy)",
+    "soa_k3": "tqb stage1_ring_kernel (TMA page ring: 3-bit-key blocks as padded row pairs by bulk copy)",
+    "soa_k3v3": "tqb stage1_ring_kernel (TMA page ring: 3-bit-key blocks as padded row pairs by bulk copy)",
+    "aos_k8": "tqb stage1_kernel (register page ring, AoS FP8-key slots)",
+    "aos_k3": "tqb stage1_kernel (register page ring, AoS 3-bit-key slots)",
+    "aos_k3v3": "tqb stage1_kernel (register page ring, AoS 3-bit-key slots)",
+}
 
 
 def parse_args():
@@ -84,10 +102,12 @@ def parse_args():
     ap.add_argument("--config", default="c1",
                     help="one of " + ", ".join(sorted(CONFIGS)) + "; a comma-separated list of the sharded "
                          "configs (c2,c3,c4) runs them one after another in one process, one line each")
-    ap.add_argument("--layout", choices=["soa", "aos", "soa_k8", "soa_k3", "soa_k3v3"], default="soa",
+    ap.add_argument("--layout", choices=["soa", "aos", "soa_k8", "soa_k3", "soa_k3v3", "aos_k8", "aos_k3", "aos_k3v3"],
+                    default="soa",
                     help="cache layout; soa_k8 = the turboquant_k8v4 preset (FP8 keys, 4-bit values), "
                          "soa_k3 = turboquant_k3v4_nc (3-bit keys, 4-bit values), soa_k3v3 = "
-                         "turboquant_3bit_nc (3-bit keys and values); these three c1 only")
+                         "turboquant_3bit_nc (3-bit keys and values); aos_* = the same presets in the AoS "
+                         "slot layout; the presets run one GPU, c1 or c3's shape")
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
@@ -172,7 +192,7 @@ def build_workload(cfg: dict, seed: int, dev: torch.device, layout: str):
     R = orthogonal(seed + 1).to(dev)
     perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
     bt = perm.reshape(B, pages).to(dev)
-    k8, k3, v3 = layout == "soa_k8", layout in ("soa_k3", "soa_k3v3"), layout == "soa_k3v3"
+    k8, k3, v3 = layout.endswith("_k8"), layout.endswith(("_k3", "_k3v3")), layout.endswith("_k3v3")
     if k3:  # 3-bit keys: 8 centroids
         cents = tqb.get_centroids(128, 3).to(dev)
         mids = tqb.get_midpoints(cents)
@@ -215,7 +235,7 @@ def algorithmic_bytes(w) -> int:
     196 B with FP8 keys), the fp32 query, the block-table entries used,
     seq_lens, the centroid table, and the fp32 mid_o write."""
     B, Hq, Hk, S, Lc = w["B"], w["Hq"], w["Hk"], w["S"], w["L"]
-    cache = B * Lc * Hk * {"soa_k8": 196, "soa_k3": 118, "soa_k3v3": 102}.get(w["layout"], 134)
+    cache = B * Lc * Hk * {"_k8": 196, "_k3": 118, "3v3": 102}.get(w["layout"][-3:], 134)
     q = B * Hq * 128 * 4
     bt = B * math.ceil(Lc / 16) * 4
     mid = B * Hq * S * 129 * 4
@@ -659,7 +679,7 @@ def run_reference(args, world, rank):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm runs the c1 headline config only"}),
               flush=True)
         return
-    if args.layout in ("soa_k8", "soa_k3", "soa_k3v3"):
+    if args.layout not in ("soa", "aos"):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm restates the 4-bit key presets only"}),
               flush=True)
         return
@@ -877,7 +897,9 @@ def measure_e2e(args, w, dev, world: int, B: int, Hq: int, S: int) -> dict:
       * ``serial_eager``: the Python call every step, one stream.
     Device time by CUDA events over `e2e_steps` steps, max over ranks."""
     import tqb
+    import tqb.compat_aos  # noqa: F401  (the AoS launcher)
 
+    k8, k3, v3 = args.layout.endswith("_k8"), args.layout.endswith(("_k3", "_k3v3")), args.layout.endswith("_k3v3")
     srcs = [w["query"], w["bt"], w["seq_lens"]]
     offs, n = [], 0
     for t in srcs:
@@ -899,14 +921,15 @@ def measure_e2e(args, w, dev, world: int, B: int, Hq: int, S: int) -> dict:
         st["dq"], st["dbt"], st["dsl"] = views(st["dbuf"])
         return st
 
+    decode = tqb.compat_aos.triton_turboquant_decode_attention if args.layout.startswith("aos") \
+        else tqb.triton_turboquant_decode_attention
+
     def e2e_step(st):
         st["dbuf"].copy_(st["hbuf"], non_blocking=True)
-        o = tqb.triton_turboquant_decode_attention(
+        o = decode(
             st["dq"], w["kv"], st["dbt"], st["dsl"], w["R"].T, w["cents"], 1.0 / math.sqrt(128),
-            {"soa_k8": 8, "soa_k3": 3, "soa_k3v3": 3}.get(args.layout, 4),
-            {"soa_k8": 128, "soa_k3": 50, "soa_k3v3": 50}.get(args.layout, 66),
-            3 if args.layout == "soa_k3v3" else 4,
-            key_fp8=args.layout == "soa_k8", norm_correction=args.layout != "soa_k8", PiT=w["R"],
+            8 if k8 else 3 if k3 else 4, 128 if k8 else 50 if k3 else 66, 3 if v3 else 4,
+            key_fp8=k8, norm_correction=not k8, PiT=w["R"],
             mid_o_buf=st["mbuf"], output_buf=st["obuf"], lse_buf=st["lbuf"], max_num_kv_splits=S)
         st["hout"].copy_(o, non_blocking=True)
 
@@ -1006,9 +1029,9 @@ def main():
         return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
-    preset = args.layout in ("soa_k8", "soa_k3", "soa_k3v3")
+    preset = args.layout not in ("soa", "aos")
     if preset and (args.config not in ("c1", "c3") or world > 1):
-        raise SystemExit("--layout soa_k8 / soa_k3 / soa_k3v3 run on one GPU: the c1 workload, or c3's GQA-8 "
+        raise SystemExit("the FP8 / 3-bit preset layouts run on one GPU: the c1 workload, or c3's GQA-8 "
                          "shape unsharded")
     if args.impl == "ours" and args.config != "c1" and not preset:
         for c in args.config.split(","):
@@ -1144,11 +1167,7 @@ def main():
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": ("f32 (e4m3 K, 4-bit V codes, fp16 tensor-core MMA, fp32 accumulate)" if args.layout == "soa_k8"
-                  else "f32 (3-bit K / 4-bit V codes, fp16-split tensor-core MMA, fp32 accumulate)"
-                  if args.layout == "soa_k3" else "f32 (3-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"
-                  if args.layout == "soa_k3v3"
-                  else "f32 (4-bit K/V codes, fp16-split tensor-core MMA, fp32 accumulate)"),
+        "dtype": LAYOUT_DTYPE[args.layout[3:] or "_k4"],
         "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
         "config": c1_config(cfg, args.layout, B, w["L"], S, world, w["kv"].numel() / 1e6),
         "stage1_us": s1_avg_ms * 1e3,
@@ -1162,11 +1181,7 @@ def main():
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
                      "algorithmic_bytes_per_launch": alg,
-                     "kernel": ("tqb stage1_ring_kernel (TMA page ring: tensor-map page copies)" if args.layout == "soa"
-                                else "tqb stage1_ring_kernel (TMA page ring: whole FP8-key blocks by bulk copy)" if args.layout == "soa_k8"
-                                else "tqb stage1_kernel (register page ring, 3-bit keys)" if args.layout == "soa_k3"
-                                else "tqb stage1_kernel (register page ring, 3-bit keys and values)" if args.layout == "soa_k3v3"
-                                else "tqb stage1_ring_kernel (TMA page ring: whole AoS blocks by bulk copy)")},
+                     "kernel": STAGE1_KERNEL[args.layout]},
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "e2e": e2e,
@@ -1179,7 +1194,7 @@ def main():
             line["speedup_vs_v2_fixed"] = ref_gpu["speedup_vs_v2_fixed"]["tqb (graph replay)"]
     if args.layout == "soa":
         line["store"] = measure_store(w, dev, peak)
-    if not args.no_cpu_baseline and world == 1 and args.layout not in ("soa_k8", "soa_k3", "soa_k3v3"):
+    if not args.no_cpu_baseline and world == 1 and args.layout in ("soa", "aos"):
         # the C restatement covers the 4-bit keys only
         line["cpu_baseline"], oracle_res = cpu_baseline(w)
         line["parity"] = parity_vs_oracle(mid, out, lse, oracle_res)

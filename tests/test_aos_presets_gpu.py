@@ -164,3 +164,53 @@ def test_aos_presets_reject_wrong_slot(cuda_device):
     with pytest.raises(tqb.TqbError, match="AoS strides"):
         tqb.stage1(q, kv, torch.zeros(1, 2, dtype=torch.int32, device=dev),
                    torch.tensor([20], dtype=torch.int32, device=dev), None, mid, layout="aos_k8")
+
+
+@pytest.mark.parametrize("hq,hk", [(32, 8), (8, 2), (4, 1), (12, 4), (20, 4)])
+@pytest.mark.parametrize("kernel", ["default", "regs"])
+@pytest.mark.parametrize("preset", list(PRESETS))
+def test_stage1_page_ring_and_register_kernel(cuda_device, preset, hq, hk, kernel, monkeypatch):
+    """The AoS presets on both Stage1 kernels: the TMA page ring (Hk dividing
+    8: whole blocks of packed slots per page, realigned shared loads, the
+    norm correction of the 3-bit forms in the kernel) and the register-ring
+    kernel (TQB_STAGE1_KERNEL=regs).  GQA 1-5, ragged lengths with an empty
+    sequence and a split of more than 32 pages, against the float64 oracle
+    on a cache written by the oracle's AoS store."""
+    if kernel == "regs":
+        monkeypatch.setenv("TQB_STAGE1_KERNEL", "regs")
+    _, lay, olay, (fp8, _, vbits) = PRESETS[preset]
+    rng = np.random.default_rng(600 + hq + 7 * hk + vbits + (50 if fp8 else 0))
+    lens = [1, 0, 1100, 45, 300, 517, 2100]
+    B = len(lens)
+    pages = [max(1, math.ceil(n / 16)) for n in lens]
+    nblk = sum(pages) + 7
+    slot = O.aos_slot_bytes(olay)
+    cache = rng.integers(0, 256, size=(nblk, 16, hk, slot), dtype=np.uint8)
+    perm = rng.permutation(nblk)
+    bt = np.zeros((B, max(pages)), np.int32)
+    k = 0
+    for b in range(B):
+        bt[b, : pages[b]] = perm[k : k + pages[b]]
+        k += pages[b]
+    slots = np.concatenate([bt[b, np.arange(n) // 16] * 16 + np.arange(n) % 16 for b, n in enumerate(lens)])
+    n = len(slots)
+    cents = tqb.get_centroids(128, 3).numpy()
+    mids = ((cents[:-1] + cents[1:]) * 0.5).astype(np.float32)
+    val = rng.standard_normal((n * hk, 128)).astype(np.float32)
+    if fp8:
+        y = (rng.standard_normal((n * hk, 128)) * 3.0).astype(np.float32)
+        norms = None
+    else:
+        key = rng.standard_normal((n * hk, 128)).astype(np.float32)
+        norms = np.linalg.norm(key, axis=1).astype(np.float32)
+        y = (key / norms[:, None]).astype(np.float32)
+    O.store_aos_np(olay, y, norms, val, None if fp8 else mids, slots.astype(np.int32), cache)
+    q = rng.standard_normal((B, hq, 128)).astype(np.float32)
+    S = 6
+    ref = O.stage1_np(q, cache, bt, np.asarray(lens, np.int32), None if fp8 else cents, S, layout=olay)
+    dev = cuda_device
+    mid = torch.full((B, hq, S, 129), SENTINEL, device=dev)
+    tqb.stage1(_dev(q, dev), _dev(cache, dev), _dev(bt, dev), _dev(np.asarray(lens, np.int32), dev),
+               None if fp8 else _dev(cents, dev), mid, layout=lay)
+    torch.cuda.synchronize()
+    _written_check(mid.cpu().numpy(), ref, f"{preset} AoS Stage1 Hq{hq}/Hk{hk} ({kernel})")

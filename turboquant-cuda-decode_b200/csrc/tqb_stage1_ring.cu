@@ -75,15 +75,17 @@ static_assert(kGroupWarps * kK8Head <= kK8StageBytes && kK8StageBytes % 1024 == 
 // Bytes of one ring stage, and of one head's page in it (SoA: 2048 data +
 // 96 metadata, AoS: 16 slots, FP8 keys: 16 x 192 data + 64 metadata, 3-bit
 // keys: 16 x 112 (or 96 with 3-bit values) data + 96 metadata).
+// Both families of a preset take the same bytes per (token, head), so a
+// head's page is 16 slots' worth: 2144 (4-bit), 3136 (FP8 keys), 1888 (3-bit
+// keys) or 1632 (3-bit keys and values).
 __host__ __device__ constexpr int stage_bytes(int layout) {
-    return layout == TQB_LAYOUT_SOA_K8 ? kK8StageBytes : kStageBytes;
+    return layout_fp8_keys(layout) ? kK8StageBytes : kStageBytes;
 }
-__host__ __device__ constexpr int head_page_bytes(int layout) {
-    return layout == TQB_LAYOUT_SOA_K8     ? kK8Head
-           : layout == TQB_LAYOUT_SOA_K3   ? kBlockSize * kSlotBytesK3    // 1888
-           : layout == TQB_LAYOUT_SOA_K3V3 ? kBlockSize * kSlotBytesK3V3  // 1632
-                                           : kAosHead;
-}
+__host__ __device__ constexpr int head_page_bytes(int layout) { return kBlockSize * aos_slot_bytes(layout); }
+static_assert(head_page_bytes(TQB_LAYOUT_SOA_K8) == kK8Head && head_page_bytes(TQB_LAYOUT_AOS) == kAosHead &&
+                  kBlockSize * kSlotBytesK3 == head_page_bytes(TQB_LAYOUT_SOA_K3) &&
+                  kBlockSize * kSlotBytesK3V3 == head_page_bytes(TQB_LAYOUT_SOA_K3V3),
+              "head page bytes");
 // Shared-memory bytes per head of a page: 3-bit-key blocks land row by row,
 // token row t at t * row + 16 * (t >> 1) (112 bytes of padding in all), so
 // that the eight token rows tau(g) the compute warps read at once start 4
@@ -116,7 +118,7 @@ constexpr float kWMax = 32768.0f;                              // largest W on t
 // (kThreads x kLaunchRegs), so every setmaxnreg.inc can be satisfied.
 template <int NT, int LAYOUT = TQB_LAYOUT_SOA>
 struct Cfg {
-    static constexpr bool kTable = LAYOUT != TQB_LAYOUT_SOA_K8;  // FP8 keys convert without the K table
+    static constexpr bool kTable = !layout_fp8_keys(LAYOUT);  // FP8 keys convert without the K table
     static constexpr int kGroups = NT == 1 ? 2 : 1;
     static constexpr int kStages = 3;
     static constexpr int kHeadsPerWarp = 4 * NT;
@@ -269,6 +271,17 @@ __device__ __forceinline__ uint4 lds128_a2(uint32_t a) {
     const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
     return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
                       __funnelshift_r(w3, w4, sh));
+}
+// 4-byte-aligned reads (AoS FP8-key slots are 196 bytes).
+__device__ __forceinline__ uint4 lds128_a4(uint32_t a) {
+    return make_uint4(lds32(a), lds32(a + 4), lds32(a + 8), lds32(a + 12));
+}
+__device__ __forceinline__ uint2 lds64_a4(uint32_t a) { return make_uint2(lds32(a), lds32(a + 4)); }
+// 12 bytes at a 2-byte-aligned address (AoS 3-bit key codes), in .x .. .z.
+__device__ __forceinline__ uint4 lds96_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12);
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh), 0u);
 }
 __device__ __forceinline__ uint2 lds64_a2(uint32_t a) {
     const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
@@ -568,7 +581,8 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
                                         int lane, int pj, int npj) {
     using C = Cfg<NT, LAYOUT>;
     constexpr bool kWholeBlock = LAYOUT != TQB_LAYOUT_SOA;  // pages copied as whole blocks
-    constexpr bool kRowCopies = layout_3bit_keys(LAYOUT);   // ... row by row, rows padded apart
+    // ... row by row, rows padded apart (SoA 3-bit keys; AoS slots are copied whole)
+    constexpr bool kRowCopies = LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3;
     constexpr uint32_t kHeadPage = (uint32_t)head_page_bytes(LAYOUT);
     constexpr uint32_t kHeadStride = (uint32_t)head_stride_bytes(LAYOUT);
     constexpr uint32_t kDps = layout_3bit_values(LAYOUT) ? kK3V3DataBytes : kK3DataBytes;
@@ -774,12 +788,37 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
     // its next page is fetched while this one is computed.  The arrive has
     // release semantics: the reads above it are performed before the
     // producer can observe the arrival.
-    constexpr bool kFp8 = LAYOUT == TQB_LAYOUT_SOA_K8;
+    constexpr bool kAos = layout_is_aos(LAYOUT);
+    constexpr bool kFp8 = layout_fp8_keys(LAYOUT);
     constexpr bool kKey3 = layout_3bit_keys(LAYOUT);
+    constexpr bool kVal3 = layout_3bit_values(LAYOUT);
     uint4 k0, k1, k0b, k1b;
     uint32_t kn, vsp, vzp;
     uint2 v[4];
-    if constexpr (kKey3) {
+    if constexpr (kAos) {
+        // AoS slot [key codes | fp16 knorm (Lloyd-Max keys) | value codes |
+        // vscale | vzero] (offsets by layout); o.meta = the slot of token
+        // tau(g), token tau(g)+1 one row (o.row) further.  Slots are 2-byte
+        // (4-byte for FP8 keys) aligned: keys of dims [32c, 32c+32) are read
+        // realigned.  V is read (and the slot released) after Q.K.
+        if constexpr (kFp8) {
+            k0 = lds128_a4(sb + o.k0);
+            k0b = lds128_a4(sb + o.k0 + 16u);
+            k1 = lds128_a4(sb + o.k1);
+            k1b = lds128_a4(sb + o.k1 + 16u);
+        } else if constexpr (kKey3) {
+            k0 = lds96_a2(sb + o.k0);
+            k1 = lds96_a2(sb + o.k1);
+        } else {
+            k0 = lds128_a2(sb + o.k0);
+            k1 = lds128_a2(sb + o.k1);
+        }
+        const uint32_t m0 = sb + o.meta, m1 = m0 + o.row;
+        constexpr uint32_t kNo = (uint32_t)aos_norm_off(LAYOUT), kSc = (uint32_t)aos_scale_off(LAYOUT);
+        kn = kFp8 ? 0x3C003C00u : __byte_perm(lds16(m0 + kNo), lds16(m1 + kNo), 0x5410);
+        vsp = __byte_perm(lds16(m0 + kSc), lds16(m1 + kSc), 0x5410);
+        vzp = __byte_perm(lds16(m0 + kSc + 2), lds16(m1 + kSc + 2), 0x5410);
+    } else if constexpr (kKey3) {
         // whole block [16 tokens][Hk][K 48 (3-bit) | V 64 (or 48, 3-bit)] +
         // [Hk][knorm 16 | vscale 16 | vzero 16]: key bits of dims
         // [32c, 32c+32) = bytes [12c, 12c+12) of tokens tau(g), tau(g)+1
@@ -822,17 +861,6 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         v[1] = lds64(sb + o.v1);
         v[2] = lds64(sb + o.v0 + 8u * kDataBytes);
         v[3] = lds64(sb + o.v1 + 8u * kDataBytes);
-    } else {
-        // AoS slot [K 64 | knorm | V 64 | vscale | vzero]; o.meta = knorm of
-        // token tau(g), token tau(g)+1 one row (o.row) further
-        k0 = lds128_a2(sb + o.k0);
-        k1 = lds128_a2(sb + o.k1);
-        const uint32_t m0 = sb + o.meta, m1 = m0 + o.row;
-        kn = __byte_perm(lds16(m0), lds16(m1), 0x5410);
-        vsp = __byte_perm(lds16(m0 + 2 + kVBytes), lds16(m1 + 2 + kVBytes), 0x5410);
-        vzp = __byte_perm(lds16(m0 + 4 + kVBytes), lds16(m1 + 4 + kVBytes), 0x5410);
-        // V is read (and the slot released) after Q.K: the Gram accumulators
-        // take its registers during the Q.K loop
     }
     if constexpr (LAYOUT == TQB_LAYOUT_SOA) mbar_arrive(release_bar);
     const bool va = page_ok && tok0 >= start && tok0 < end;
@@ -868,10 +896,17 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
             for (int nt = 0; nt < NT; nt++)
                 mma_16816(dq[nt][ks & 1], a0, a1, a2, a3, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
-        v[0] = lds64(sb + o.v0);
-        v[1] = lds64(sb + o.v1);
-        v[2] = lds64(sb + o.v0 + (o.row << 3));
-        v[3] = lds64(sb + o.v1 + (o.row << 3));
+        if constexpr (kAos) {
+            v[0] = lds64_a4(sb + o.v0);
+            v[1] = lds64_a4(sb + o.v1);
+            v[2] = lds64_a4(sb + o.v0 + (o.row << 3));
+            v[3] = lds64_a4(sb + o.v1 + (o.row << 3));
+        } else {
+            v[0] = lds64(sb + o.v0);
+            v[1] = lds64(sb + o.v1);
+            v[2] = lds64(sb + o.v0 + (o.row << 3));
+            v[3] = lds64(sb + o.v1 + (o.row << 3));
+        }
         mbar_arrive(release_bar);
     } else {
     // 3-bit keys: table address 0x10000 | (6-bit field << 8) | lane copy offset
@@ -900,14 +935,14 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
             mma_16816(dq[nt][0], e0.x, e0.y, e1.x, e1.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
             mma_16816(dq[nt][1], e2.x, e2.y, e3.x, e3.y, st.qf[nt][2 * ks], st.qf[nt][2 * ks + 1]);
         }
-        if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
+        if constexpr (kAos) {  // Lloyd-Max AoS keys (the FP8 ones take the branch above)
             mma_16816(dcs[0], e0.x, e0.y, e1.x, e1.y, e0.x, e1.x);
             mma_16816(dcs[1], e2.x, e2.y, e3.x, e3.y, e2.x, e3.x);
         }
     }
     }  // table-decoded keys
     float kn0 = half_bits_to_float(kn), kn1 = half_bits_to_float(kn >> 16);
-    if constexpr (LAYOUT == TQB_LAYOUT_AOS) {
+    if constexpr (kAos && !kFp8) {
         // norm correction c / |c| (reference/aos_decode.py:199-206), with
         // sum c^2 = sum (C_hi + C_lo)^2 = D[g][g] + 2 D[g+8][g] (+ sum C_lo^2,
         // 2^-22 of it, dropped); lane 4g + g/2 holds column g, element g & 1
@@ -918,10 +953,17 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         const float csq1 = __shfl_sync(0xffffffffu, o1, owner) * csq_unscale;
         kn0 *= rsqrtf(csq0 + 1e-16f);
         kn1 *= rsqrtf(csq1 + 1e-16f);
-        v[0] = lds64_a2(sb + o.v0);
-        v[1] = lds64_a2(sb + o.v1);
-        v[2] = lds64_a2(sb + o.v0 + (o.row << 3));
-        v[3] = lds64_a2(sb + o.v1 + (o.row << 3));
+#pragma unroll
+        for (int jv = 0; jv < 4; jv++) {
+            const uint32_t va_ = sb + (jv & 1 ? o.v1 : o.v0) + (jv & 2 ? (o.row << 3) : 0u);
+            if constexpr (kVal3) {
+                // 16 3-bit codes (6 bytes, 2-byte aligned) spread to nibbles
+                const uint32_t a = lds16(va_), b = lds16(va_ + 2u), cc = lds16(va_ + 4u);
+                v[jv] = make_uint2(spread3to4((a | (b << 16)) & 0xFFFFFFu), spread3to4((b >> 8) | (cc << 8)));
+            } else {
+                v[jv] = lds64_a2(va_);
+            }
+        }
         mbar_arrive(release_bar);
     }
     const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
@@ -1109,7 +1151,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.v1 = colw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
         o.meta = gs.ring + kMetaOff + (uint32_t)w * kMetaSlot + 2u * tau;
         o.row = 0;
-    } else if constexpr (layout_3bit_keys(LAYOUT)) {
+    } else if constexpr (LAYOUT == TQB_LAYOUT_SOA_K3 || LAYOUT == TQB_LAYOUT_SOA_K3V3) {
         // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
         // (w - kvh) * 16 * slot bytes of the stage: [16 tokens][Hk][K 48 | V]
         // then [Hk][knorm 16 | vscale 16 | vzero 16] fp16.
@@ -1143,16 +1185,22 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         o.meta = run + (uint32_t)kBlockSize * row + (uint32_t)kvh * (2 * kBlockSize * 2) + 2u * tau;
         o.row = row;
     } else {
-        // The page's block of run [w - kvh, w - kvh + Hk) sits unchanged at
-        // (w - kvh) * 2144 bytes of the stage: [16 tokens][Hk][134-byte slot].
+        // AoS: the page's block of run [w - kvh, w - kvh + Hk) sits unchanged
+        // at (w - kvh) * 16 slots of the stage: [16 tokens][Hk][slot] (134,
+        // 196, 118 or 102 bytes).  A lane's key bytes of dims [32c, 32c+32)
+        // are 16 (4-bit), 32 (e4m3) or 12 (3-bit) bytes at that multiple of
+        // c; its value codes of dims [16g, 16g+16) 8 (4-bit) or 6 (3-bit) bytes.
+        constexpr uint32_t kSlot = (uint32_t)aos_slot_bytes(LAYOUT);
+        constexpr uint32_t kKeyLane = layout_fp8_keys(LAYOUT) ? 32u : layout_3bit_keys(LAYOUT) ? 12u : 16u;
+        constexpr uint32_t kValLane = layout_3bit_values(LAYOUT) ? 6u : 8u;
         const int kvh = w % P.Hk;
-        const uint32_t row = (uint32_t)P.Hk * kAosSlot;
-        const uint32_t head = gs.ring + (uint32_t)(w - kvh) * kAosHead + (uint32_t)kvh * kAosSlot;
-        o.k0 = head + (uint32_t)tau * row + 16u * c;
+        const uint32_t row = (uint32_t)P.Hk * kSlot;
+        const uint32_t head = gs.ring + (uint32_t)(w - kvh) * (kBlockSize * kSlot) + (uint32_t)kvh * kSlot;
+        o.k0 = head + (uint32_t)tau * row + kKeyLane * c;
         o.k1 = o.k0 + row;
-        o.v0 = head + (uint32_t)(2 * c) * row + kKBytes + 2 + 8u * g;
+        o.v0 = head + (uint32_t)(2 * c) * row + (uint32_t)aos_val_off(LAYOUT) + kValLane * g;
         o.v1 = o.v0 + row;
-        o.meta = head + (uint32_t)tau * row + kKBytes;
+        o.meta = head + (uint32_t)tau * row;  // the slot; fields at their offsets
         o.row = row;
     }
     // Owner of token 2c in the Q.K layout: tau(g') = 2c for g' = bitswap(c).
@@ -1451,10 +1499,11 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
 
 bool stage1_ring_supported(const Stage1Params& P) {
     const bool soa = P.layout == TQB_LAYOUT_SOA;
-    // AoS: a tile's runs are whole blocks (Hk divides 8) of packed slots, each
-    // copied as one run of Hk * 2144 bytes.
-    const bool aos_ok = P.layout == TQB_LAYOUT_AOS && kGroupWarps % P.Hk == 0 && P.head_stride == kAosSlot &&
-                        P.pos_stride == (int64_t)P.Hk * kAosSlot;
+    // AoS (every preset): a tile's runs are whole blocks (Hk divides 8) of
+    // packed slots, each copied as one run of Hk * 16 slots.
+    const bool aos_ok = layout_is_aos(P.layout) && kGroupWarps % P.Hk == 0 &&
+                        P.head_stride == aos_slot_bytes(P.layout) &&
+                        P.pos_stride == (int64_t)P.Hk * aos_slot_bytes(P.layout);
     // FP8 keys (SoA blocks): whole blocks too, Hk * 3136 bytes.
     const bool k8_ok = P.layout == TQB_LAYOUT_SOA_K8 && kGroupWarps % P.Hk == 0 &&
                        P.block_bytes >= (int64_t)kBlockSize * P.Hk * kSlotBytesK8;
@@ -1464,8 +1513,14 @@ bool stage1_ring_supported(const Stage1Params& P) {
     bool regs_ok = false;
     if (soa)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA>() : ring_registers_ok<2, TQB_LAYOUT_SOA>();
-    else if (aos_ok)
+    else if (aos_ok && P.layout == TQB_LAYOUT_AOS)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS>() : ring_registers_ok<2, TQB_LAYOUT_AOS>();
+    else if (aos_ok && P.layout == TQB_LAYOUT_AOS_K8)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS_K8>() : ring_registers_ok<2, TQB_LAYOUT_AOS_K8>();
+    else if (aos_ok && P.layout == TQB_LAYOUT_AOS_K3)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS_K3>() : ring_registers_ok<2, TQB_LAYOUT_AOS_K3>();
+    else if (aos_ok)
+        regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_AOS_K3V3>() : ring_registers_ok<2, TQB_LAYOUT_AOS_K3V3>();
     else if (k8_ok)
         regs_ok = P.G <= 4 ? ring_registers_ok<1, TQB_LAYOUT_SOA_K8>() : ring_registers_ok<2, TQB_LAYOUT_SOA_K8>();
     else if (k3_ok && P.layout == TQB_LAYOUT_SOA_K3)
@@ -1490,6 +1545,17 @@ int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) 
         return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms)
                         : launch_ring_t<2, TQB_LAYOUT_SOA_K8>(P, M, stream, num_sms);
     }
+    if (P.layout == TQB_LAYOUT_AOS_K8) {
+        if (P.rot != nullptr) return TQB_ERR_UNSUPPORTED;  // no rotation prologue in this instance
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS_K8>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_AOS_K8>(P, M, stream, num_sms);
+    }
+    if (P.layout == TQB_LAYOUT_AOS_K3)
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS_K3>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_AOS_K3>(P, M, stream, num_sms);
+    if (P.layout == TQB_LAYOUT_AOS_K3V3)
+        return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_AOS_K3V3>(P, M, stream, num_sms)
+                        : launch_ring_t<2, TQB_LAYOUT_AOS_K3V3>(P, M, stream, num_sms);
     if (P.layout == TQB_LAYOUT_SOA_K3)
         return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms)
                         : launch_ring_t<2, TQB_LAYOUT_SOA_K3>(P, M, stream, num_sms);
