@@ -87,9 +87,9 @@ STAGE1_KERNEL = {
     "soa_k8": "tqb stage1_ring_kernel (TMA page ring: whole FP8-key blocks by bulk copy)",
     "soa_k3": "tqb stage1_ring_kernel (TMA page ring: 3-bit-key blocks as padded row pairs by bulk copy)",
     "soa_k3v3": "tqb stage1_ring_kernel (TMA page ring: 3-bit-key blocks as padded row pairs by bulk copy)",
-    "aos_k8": "tqb stage1_kernel (register page ring, AoS FP8-key slots)",
-    "aos_k3": "tqb stage1_kernel (register page ring, AoS 3-bit-key slots)",
-    "aos_k3v3": "tqb stage1_kernel (register page ring, AoS 3-bit-key slots)",
+    "aos_k8": "tqb stage1_ring_kernel (TMA page ring: whole AoS FP8-key blocks by bulk copy)",
+    "aos_k3": "tqb stage1_ring_kernel (TMA page ring: whole AoS 3-bit-key blocks by bulk copy)",
+    "aos_k3v3": "tqb stage1_ring_kernel (TMA page ring: whole AoS 3-bit-key blocks by bulk copy)",
 }
 
 
