@@ -1113,8 +1113,12 @@ def main():
     barrier(world)
     clocks.mark(w0, w1)
     clocks.stop()
-    total_ms = max_over_ranks(start.elapsed_time(end), world)
-    s1_avg_ms = max_over_ranks(a1.elapsed_time(b1) / K, world)
+    step_ms_local, s1_ms_local = start.elapsed_time(end) / K, a1.elapsed_time(b1) / K
+    total_ms = max_over_ranks(step_ms_local * K, world)
+    s1_avg_ms = max_over_ranks(s1_ms_local, world)
+    # Stage2 (+ the launch between) per rank, then the max: the difference of
+    # the two maxima would also carry the spread between GPUs
+    s2_ms = max_over_ranks(step_ms_local - s1_ms_local, world)
     ms_per_step = total_ms / K
     value = world * B / (ms_per_step * 1e-3)
     del g_step
@@ -1171,9 +1175,10 @@ def main():
         "data": "synthetic (seeded N(0,1) K/V written by the sm_100a store, seeded rotation)",
         "config": c1_config(cfg, args.layout, B, w["L"], S, world, w["kv"].numel() / 1e6),
         "stage1_us": s1_avg_ms * 1e3,
-        "stage2_us": (ms_per_step - s1_avg_ms) * 1e3,
+        "stage2_us": s2_ms * 1e3,
         "timing": ("value: exactly `steps` CUDA-graph replays of the decode step (Stage1 + Stage2) after "
                    "`warmup`, CUDA events; stage1_us: `steps` Stage1-only replays (the roofline's duration); "
+                   "stage2_us: the step minus Stage1 on each rank, max over ranks; "
                    "stage1_us_reference_protocol: the reference's protocol (benchmarks/stage1.py, 20 warm-up + "
                    "100 timed, 5 rotated rounds, median) in reference_gpu"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
