@@ -176,7 +176,7 @@ def test_c1_store_bit_exact(c1_soa, c1_soa_host):
     _store_matches_oracle(c1_soa, c1_soa_host)
 
 
-@pytest.mark.parametrize("kernel", ["ring", "warp", "regs"])
+@pytest.mark.parametrize("kernel", ["ring", "regs"])
 def test_c1_soa_decode(c1_soa, c1_soa_oracle, kernel, monkeypatch):
     monkeypatch.setenv("TQB_STAGE1_KERNEL", kernel)
     got = _decode_gpu(c1_soa, 32)

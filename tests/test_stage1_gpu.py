@@ -5,12 +5,10 @@ Bar: |got - ref| <= 1e-4 + 2e-3 |ref| on every written O and LSE element
 stored in the golden fixtures and (b) the CPU oracle on fresh seeded inputs.
 Empty splits must stay unwritten, exactly as in the reference.
 
-Every test runs three times: with the SoA cache served by the TMA group-ring
-kernel (the default), by the per-warp-ring kernel (TQB_STAGE1_KERNEL=warp;
-GQA <= 4, the group ring above) and by the register-ring kernel
-(TQB_STAGE1_KERNEL=regs); the AoS cache uses the group ring or the register
-kernel.  After each run the device's count of bounded waits that gave up
-must be zero.
+Every test runs twice: with the SoA cache served by the TMA page-ring kernel
+(the default) and by the register-ring kernel (TQB_STAGE1_KERNEL=regs); the
+AoS cache always uses the register-ring kernel.  After each run the device's
+count of bounded waits that gave up must be zero.
 """
 
 from __future__ import annotations
@@ -33,7 +31,7 @@ pytestmark = pytest.mark.gpu
 SENTINEL = -12345.0
 
 
-@pytest.fixture(autouse=True, params=["ring", "warp", "regs"])
+@pytest.fixture(autouse=True, params=["ring", "regs"])
 def stage1_kernel(request, cuda_device):
     old = os.environ.get("TQB_STAGE1_KERNEL")
     os.environ["TQB_STAGE1_KERNEL"] = request.param

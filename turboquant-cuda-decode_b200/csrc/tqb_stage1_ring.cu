@@ -39,8 +39,6 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
-#include <stdlib.h>
-#include <string.h>
 
 #include "tqb_common.cuh"
 #include "tqb_internal.h"
@@ -384,7 +382,6 @@ __device__ __forceinline__ long long warp_sum_ll(long long v) {
 // Tile of the first item of sequence b whose start weight reaches r (>= 1,
 // at most the sequence's weight): split s* = the last split starting below
 // r, then the KV head in it.
-template <int TI>
 __device__ __forceinline__ uint32_t cut_tile(const Stage1Params& P, const SeqSplit& q, int b, long long r,
                                              uint32_t num_tiles, bool by_count) {
     const long long unit = by_count ? (long long)P.Hk : (long long)P.Hk * (q.sl + kSplitCost);
@@ -394,14 +391,13 @@ __device__ __forceinline__ uint32_t cut_tile(const Stage1Params& P, const SeqSpl
         by_count ? 1 : (long long)(min((int)(ss + 1) * q.sl, q.L) - (int)ss * q.sl) + kSplitCost;
     const long long kv = (r - a + per - 1) / per;  // in [1, Hk]
     const long long item = ((long long)b * P.S + ss) * P.Hk + kv;
-    return (uint32_t)min((long long)num_tiles, (item + TI - 1) / TI);
+    return (uint32_t)min((long long)num_tiles, (item + kGroupWarps - 1) / kGroupWarps);
 }
 // Tile walk of group gi of this CTA: tiles first, first + stride, ... below
 // end, in res[0..2].  A batch whose sequences all have the same length and
 // split count takes the round-robin walk (already balanced); any other
 // batch the contiguous ranges of the weight cut.  One warp (compact loops:
 // this code runs once, cold, ahead of every other warp's first tile).
-template <int TI>
 __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uint32_t num_tiles, uint32_t (&res)[3],
                           int lane) {
     const uint32_t cuts = gridDim.x * (uint32_t)groups_per_cta;
@@ -432,7 +428,7 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
         return;
     }
     res[2] = 1u;
-    const bool by_count = cnt <= 2LL * TI * (long long)cuts;  // <= 2 non-empty tiles per group
+    const bool by_count = cnt <= 2LL * kGroupWarps * (long long)cuts;  // <= 2 non-empty tiles per group
     if (by_count) tot = cnt;
     const long long qt = tot / (long long)cuts, rt = tot % (long long)cuts;
 #pragma unroll 1
@@ -462,7 +458,7 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
                 const bool here = w > 0 && excl < tgt && tgt <= base + incl;
                 const uint32_t m = __ballot_sync(0xffffffffu, here);
                 if (m) {
-                    const uint32_t tl = here ? cut_tile<TI>(P, q, b, tgt - excl, num_tiles, by_count) : 0u;
+                    const uint32_t tl = here ? cut_tile(P, q, b, tgt - excl, num_tiles, by_count) : 0u;
                     t = __shfl_sync(0xffffffffu, tl, __ffs(m) - 1);
                     break;
                 }
@@ -506,7 +502,7 @@ struct GroupSmem {
 // the producers' TMA copies overwrite both only after the CTA barrier that
 // ends the prologue.
 // ---------------------------------------------------------------------------
-template <int NT, int THREADS = Cfg<NT>::kThreads>
+template <int NT>
 __device__ void rotate_share(const Stage1Params& P, uint8_t* smem, int tid) {
     using C = Cfg<NT>;
     static_assert(NT == 1, "the fused rotation stages rot in group 1's ring");
@@ -520,13 +516,13 @@ __device__ void rotate_share(const Stage1Params& P, uint8_t* smem, int tid) {
     const int64_t r0 = (int64_t)blockIdx.x * per, r1 = min(rows, r0 + per);
     if (r0 >= r1) return;  // uniform over the CTA
     const float4* R4 = reinterpret_cast<const float4*>(P.rot);
-    for (int e = tid; e < kHeadDim * kHeadDim / 4; e += THREADS)
+    for (int e = tid; e < kHeadDim * kHeadDim / 4; e += C::kThreads)
         reinterpret_cast<float4*>(rs)[e] = __ldg(R4 + e);
     const int j = tid % kHeadDim;
     for (int64_t c0 = r0; c0 < r1; c0 += kChunk) {
         const int n = (int)min((int64_t)kChunk, r1 - c0);
         __syncthreads();  // rot staged / the previous chunk's rows read
-        for (int e = tid; e < n * kHeadDim; e += THREADS) {
+        for (int e = tid; e < n * kHeadDim; e += C::kThreads) {
             const int64_t r = c0 + e / kHeadDim;
             const int64_t off = (r / P.Hq) * P.rqsb + (r % P.Hq) * P.rqsh + e % kHeadDim;
             float v;
@@ -539,7 +535,7 @@ __device__ void rotate_share(const Stage1Params& P, uint8_t* smem, int tid) {
             qs[e] = v;
         }
         __syncthreads();
-        for (int i = tid / kHeadDim; i < n; i += THREADS / kHeadDim) {
+        for (int i = tid / kHeadDim; i < n; i += C::kThreads / kHeadDim) {
             float acc = 0.0f;
 #pragma unroll 8
             for (int k = 0; k < kHeadDim; k++) acc = fmaf(qs[i * kHeadDim + k], rs[k * kHeadDim + j], acc);
@@ -784,13 +780,14 @@ struct LaneSmem {
     uint32_t row;     // AoS: bytes between consecutive tokens of a page
 };
 
-template <int NT, int LAYOUT, typename Release>
+template <int NT, int LAYOUT>
 __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, const LaneSmem& o, bool page_ok,
                                           int tok0, int start, int end, uint32_t lut_sel_src, int g,
-                                          int c, int src_a, Release release, float csq_unscale) {
-    // Every ring byte this lane uses is read first and the slot released
-    // (`release`, called by all 32 lanes), so its next page is fetched while
-    // this one is computed.
+                                          int c, int src_a, uint32_t release_bar, float csq_unscale) {
+    // Every ring byte this lane uses is read first and the slot released, so
+    // its next page is fetched while this one is computed.  The arrive has
+    // release semantics: the reads above it are performed before the
+    // producer can observe the arrival.
     constexpr bool kAos = layout_is_aos(LAYOUT);
     constexpr bool kFp8 = layout_fp8_keys(LAYOUT);
     constexpr bool kKey3 = layout_3bit_keys(LAYOUT);
@@ -842,7 +839,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
                 v[j] = lds64(va);
             }
         }
-        release();
+        mbar_arrive(release_bar);
     } else if constexpr (kFp8) {
         // whole block [16 tokens][Hk][K 128 e4m3 | V 64] + [Hk][vscale 16 |
         // vzero 16]: key bytes [32c, 32c+32) of tokens tau(g), tau(g)+1
@@ -865,7 +862,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
         v[2] = lds64(sb + o.v0 + 8u * kDataBytes);
         v[3] = lds64(sb + o.v1 + 8u * kDataBytes);
     }
-    if constexpr (LAYOUT == TQB_LAYOUT_SOA) release();
+    if constexpr (LAYOUT == TQB_LAYOUT_SOA) mbar_arrive(release_bar);
     const bool va = page_ok && tok0 >= start && tok0 < end;
     const bool vb = page_ok && tok0 + 1 >= start && tok0 + 1 < end;
 
@@ -910,7 +907,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
             v[2] = lds64(sb + o.v0 + (o.row << 3));
             v[3] = lds64(sb + o.v1 + (o.row << 3));
         }
-        release();
+        mbar_arrive(release_bar);
     } else {
     // 3-bit keys: table address 0x10000 | (6-bit field << 8) | lane copy offset
     const uint32_t lut_lane = __byte_perm(lut_sel_src, 0u, 0x4140u);
@@ -967,7 +964,7 @@ __device__ __forceinline__ void page_math(ItemState<NT>& st, const uint32_t sb, 
                 v[jv] = lds64_a2(va_);
             }
         }
-        release();
+        mbar_arrive(release_bar);
     }
     const float vs0 = va ? half_bits_to_float(vsp) : 0.0f;
     const float vs1 = vb ? half_bits_to_float(vsp >> 16) : 0.0f;
@@ -1124,11 +1121,8 @@ __device__ __forceinline__ bool page_step(ItemState<NT>& st, const GroupSmem& gs
     // all 32 lanes arrive on the slot's release barrier (no branch on the lane)
     if (k < my_np) {
         const bool page_ok = (lds32(gs.vmask<NS>(S)) >> w) & 1u;
-        // the arrive has release semantics: the reads before it are
-        // performed before the producer can observe the arrival
-        const uint32_t rb = gs.empty<NS>(S);
         page_math<NT, LAYOUT>(st, (uint32_t)(S * stage_bytes(LAYOUT)), o, page_ok, tok_first + k * kBlockSize, start, end,
-                      lut_sel_src, g, c, src_a, [rb] { mbar_arrive(rb); }, csq_unscale);
+                      lut_sel_src, g, c, src_a, gs.empty<NS>(S), csq_unscale);
     } else {
         mbar_arrive(gs.empty<NS>(S));
     }
@@ -1320,7 +1314,7 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
     const int planner = warp - (C::kWarps - C::kGroups);  // group planned by this warp, if >= 0
     uint32_t walk[3] = {0u, 0u, 0u};
     if (planner >= 0)
-        tile_walk<kGroupWarps>(P, planner, C::kGroups, num_tiles, walk, lane);
+        tile_walk(P, planner, C::kGroups, num_tiles, walk, lane);
     else if (C::kTable)
         for (int e = tid; e < 256 * kLutCopies; e += C::kThreads - 32 * C::kGroups) {
         const int byte = e / kLutCopies;
@@ -1391,342 +1385,6 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1)
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::kComputeRegs));
         consume<NT, LAYOUT>(P, gs, gi, warp % kGroupWarps, lane, ec);
     }
-}
-
-// ===========================================================================
-// Stage1 for the SoA cache with GQA <= 4 on per-warp page rings.
-//
-// A compute warp reads only its own KV head's column of a page (2 KB of
-// codes plus 96 B of metadata), so every warp can feed itself: it walks its
-// own sequence of work items (b, s, KV head) and keeps its next kNs pages in
-// flight with its own tensor copies (a one-head box of the page map) and
-// bulk copies (the metadata), each page completing on one of the warp's own
-// mbarriers.  A page is refilled by the warp that read it, right after the
-// read, with the next page of its stream (crossing into the next item), so
-// no warp waits for another: there is no producer warp, no release barrier
-// and no lockstep across a group.  Without a producer warpgroup the 16
-// compute warps (512 threads) each run with 128 registers.
-// ===========================================================================
-namespace wr {
-constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
-constexpr int kNs = 3;                                  // pages in flight per warp
-constexpr int kCol = kBlockSize * kDataBytes;           // 2048: one head's page of codes
-constexpr int kRingW = kNs * kCol;                      // 6144 per warp
-constexpr int kLowWarps = 10;                           // rings below the K table
-constexpr int kBarOff = kLowWarps * kRingW;             // 61440
-constexpr int kBarW = 64;                               // full[kNs], q_full, next item (b, s, head, start, end, pages)
-constexpr int kSeenOff = kBarOff + kWarps * kBarW;      // fused rotation: grid-barrier word seen
-constexpr int kLutOff = kLutAddr - kDynBase;            // 64512: the table at shared address 0x10000
-constexpr int kHighOff = kLutOff + kLutBytes;           // 130048
-constexpr int kMetaOff = kHighOff + (kWarps - kLowWarps) * kRingW;  // 166912
-constexpr int kQOff = kMetaOff + kNs * kCol;            // metadata of stage s: row s (2 KB) x warp (96 B)
-constexpr int kQW = 4 * kQRowBytes;                     // 2 KB: one item's query rows
-constexpr int kStgOff = kQOff + kWarps * kQW;
-constexpr int kSmem = kStgOff + kWarps * kStgBytes;     // 222208
-static_assert(kSeenOff + 16 <= kLutOff, "barriers below the table");
-static_assert(kWarps * kMetaSlot <= kCol && kMetaSlot % 16 == 0, "metadata rows");
-static_assert(kRingW % 1024 == 0 && kHighOff % 1024 == 0 && (kDynBase + kHighOff) % 1024 == 0,
-              "1024-byte aligned columns (128-byte swizzle)");
-static_assert(kSmem <= 232448, "shared memory per CTA");
-// The fused rotation stages rot and 32 query rows where the group ring does
-// (above the table), all of it free until the warps start.
-static_assert(Cfg<1>::q_off(0) >= kHighOff && Cfg<1>::ring_off(1) + kHeadDim * kHeadDim * 4 <= kSmem,
-              "rotation staging");
-__host__ __device__ constexpr int ring(int w) { return w < kLowWarps ? w * kRingW : kHighOff + (w - kLowWarps) * kRingW; }
-}  // namespace wr
-
-// The next non-empty item of a warp's walk at or after `it` (it += stride),
-// or it >= end; lanes agree.
-__device__ __forceinline__ uint32_t next_item(const Stage1Params& P, uint32_t it, uint32_t end, uint32_t stride,
-                                              ItemInfo& x) {
-    for (; it < end; it += stride)
-        if (decode_item(P, it, x)) return it;
-    return it;
-}
-
-template <int LAYOUT>
-__global__ void __launch_bounds__(wr::kThreads, 1)
-    stage1_wring_kernel(const Stage1Params P, const __grid_constant__ RingMaps M) {
-    static_assert(LAYOUT == TQB_LAYOUT_SOA, "the per-warp rings serve the 4-bit SoA cache");
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    pdl_trigger();
-    pdl_wait();  // the kernel before on the stream (e.g. the previous step's Stage2 reading mid_o)
-
-    // ---- K table: 256 entries x 32 lane copies of {C_hi pair, C_lo pair} ----
-    float cmax = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kNumCentroids; k++) cmax = fmaxf(cmax, fabsf(__ldg(P.cents + k)));
-    const int ec = fp16_scale_exp(cmax);
-    const float cscale = exp2i(ec);
-    for (int e = tid; e < 256 * kLutCopies; e += wr::kThreads) {
-        const int byte = e / kLutCopies;
-        const float clo = __ldg(P.cents + (byte & 15)) * cscale, chi = __ldg(P.cents + (byte >> 4)) * cscale;
-        const __half2 h = __floats2half2_rn(clo, chi);
-        const __half2 l = __floats2half2_rn(clo - __low2float(h), chi - __high2float(h));
-        *reinterpret_cast<uint2*>(smem + wr::kLutOff + (size_t)e * 8) = make_uint2(h2_as_u32(h), h2_as_u32(l));
-    }
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    if (base != (uint32_t)kDynBase) {  // the table address above assumes this window layout
-        if (tid == 0) atomicAdd(&g_wait_timeouts, 1u);
-        return;
-    }
-    const uint32_t bars = base + wr::kBarOff + (uint32_t)w * wr::kBarW;  // full[s] at 8 s, q_full at 24
-    if (lane == 0) {
-        for (int s = 0; s < wr::kNs; s++) mbar_init(bars + 8u * s, 1);
-        mbar_init(bars + 24u, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    }
-    __syncthreads();
-    if (P.rot != nullptr) {
-        // fused query rotation (cooperative launch, one CTA per SM)
-        rotate_share<1, wr::kThreads>(P, smem, tid);
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();  // this CTA's rows, before its arrival
-            const uint32_t seen = atomicAdd(&g_rot_barrier, blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u);
-            sts32(base + wr::kSeenOff, seen);
-        }
-        __syncthreads();
-    }
-
-    // ---- this warp's walk over the items (b, s, KV head; head fastest) -----
-    uint32_t walk[3];
-    tile_walk<1>(P, w, wr::kWarps, (uint32_t)P.num_items, walk, lane);
-    const uint32_t it_end = walk[1], it_stride = walk[2];
-
-    const int g = lane >> 2, c = lane & 3;
-    const uint32_t lut_sel_src = (uint32_t)(lane % kLutCopies) * 8u | ((uint32_t)(kLutAddr >> 16) << 8);
-    const int tau = 8 * (g >> 2) + 2 * ((g >> 1) & 1) + 4 * (g & 1);
-    const uint32_t ringw = base + (uint32_t)wr::ring(w);
-    const uint32_t metaw = base + (uint32_t)wr::kMetaOff + (uint32_t)w * kMetaSlot;  // stage s: + s * kCol
-    const uint32_t qarea = base + (uint32_t)wr::kQOff + (uint32_t)w * wr::kQW;
-    const uint32_t stg = base + (uint32_t)wr::kStgOff + (uint32_t)w * kStgBytes;
-    LaneSmem o;
-    {
-        auto sw = [](int t, int chunk) { return (uint32_t)(t * kDataBytes + ((chunk ^ (t & 7)) << 4)); };
-        o.k0 = ringw + sw(tau, c);
-        o.k1 = ringw + sw(tau + 1, c);
-        o.v0 = ringw + sw(2 * c, 4 + (g >> 1)) + 8u * (g & 1);
-        o.v1 = ringw + sw(2 * c + 1, 4 + (g >> 1)) + 8u * (g & 1);
-        o.meta = metaw + 2u * tau;  // stage s's metadata sits s * kCol after stage 0's, as its codes do
-        o.row = 0;
-    }
-    const int src_a = 4 * (((c & 1) << 1) | (c >> 1)) + (g >> 1);
-    const uint32_t nblocks = (P.num_blocks > 0 && P.num_blocks < 0x7fffffff) ? (uint32_t)P.num_blocks : 0x7fffffffu;
-    const uint64_t stream_policy = l2_evict_first_policy();
-    const uint32_t tok_bytes = (uint32_t)P.Hk * kDataBytes;
-
-    // Current item (consumed) and the next one (its description in shared
-    // memory at bars + 32: b, s, KV head, start, end, pages; pages 0 = none).
-    ItemInfo cur;
-    uint32_t it = next_item(P, walk[0], it_end, it_stride, cur);
-    if (it >= it_end) return;  // no work for this warp
-    auto pages_of = [](const ItemInfo& x) { return (x.end - 1) / kBlockSize - x.start / kBlockSize + 1; };
-    auto put_next = [&](const ItemInfo& x, int np) {
-        if (lane == 0) {
-            sts32(bars + 32u, (uint32_t)x.b);
-            sts32(bars + 36u, (uint32_t)x.s);
-            sts32(bars + 40u, (uint32_t)x.kvh);
-            sts32(bars + 44u, (uint32_t)x.start);
-            sts32(bars + 48u, (uint32_t)x.end);
-            sts32(bars + 52u, (uint32_t)np);
-        }
-        __syncwarp();
-    };
-    // Query rows of an item into this warp's query area, after its previous
-    // rows were read (the caller orders those reads before this with
-    // __syncwarp; the proxy fence orders them before the async copy).
-    auto issue_query = [&](int b, int kvh) {
-        if (lane == 0) {
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            mbar_arrive_tx(bars + 24u, (uint32_t)P.G * kQRowBytes);
-            tma_load_3d(qarea, &M.query, 0, kvh * P.G, b, bars + 24u);
-        }
-    };
-    int cur_np = pages_of(cur);
-    {
-        ItemInfo nx;
-        const uint32_t itn = next_item(P, it + it_stride, it_end, it_stride, nx);
-        put_next(nx, itn < it_end ? pages_of(nx) : 0);
-        it = itn;
-    }
-
-    // Issue pointer: the page after the last one issued, in the current item
-    // (iss_next == 0) or the next one (1), or past the next one (2: waits
-    // until the current item is done).  iss_pos indexes P.bt.
-    int iss_next = 0, iss_left = cur_np, iss_kvh = cur.kvh;
-    int iss_pos = cur.b * (int)P.bt_stride + cur.start / kBlockSize;  // B * bt_stride < 2^31 (host check)
-    int next_id = __ldg(P.bt + iss_pos);
-    uint32_t s_iss = 0, s_con = 0, vbits = 0, cbits = 0;
-    int in_flight = 0;
-    // Copies the page at the issue pointer into slot s_iss and advances.
-    auto issue_page = [&]() {
-        const bool ok = (uint32_t)next_id < nblocks;
-        const uint32_t id = ok ? (uint32_t)next_id : 0u;  // a masked page copies block 0
-        const uint32_t full = bars + 8u * s_iss;
-        if (lane == 0) {
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            mbar_arrive_tx(full, (uint32_t)(wr::kCol + kMetaSlot));
-            tma_load_4d(ringw + s_iss * (uint32_t)wr::kCol, &M.page[3], 0, 0, iss_kvh, (int)id, full, stream_policy);
-            bulk_g2s(metaw + s_iss * (uint32_t)wr::kCol,
-                     P.cache + (uint64_t)id * (uint64_t)P.block_bytes + kBlockSize * tok_bytes +
-                         (uint32_t)iss_kvh * kMetaSlot,
-                     kMetaSlot, full, stream_policy);
-        }
-        vbits = ok ? (vbits | (1u << s_iss)) : (vbits & ~(1u << s_iss));
-        s_iss = s_iss == wr::kNs - 1 ? 0u : s_iss + 1u;
-        in_flight++;
-        iss_pos++;
-        if (--iss_left == 0) {
-            // into the next item, when it is known
-            const int nnp = iss_next == 0 ? (int)lds32(bars + 52u) : 0;
-            if (nnp > 0) {
-                iss_next = 1;
-                iss_left = nnp;
-                iss_kvh = (int)lds32(bars + 40u);
-                iss_pos = (int)lds32(bars + 32u) * (int)P.bt_stride + (int)lds32(bars + 44u) / kBlockSize;
-            } else {
-                iss_next = 2;
-            }
-        }
-        next_id = iss_left > 0 ? __ldg(P.bt + iss_pos) : 0;  // lands while this page is computed
-    };
-    while (in_flight < wr::kNs && iss_left > 0) issue_page();
-    if (P.rot != nullptr && !rot_barrier_wait(lds32(base + wr::kSeenOff), lane)) {
-        // drain this warp's copies, then leave
-        for (int s = 0; s < in_flight; s++) mbar_wait(bars + 8u * s, 0u);
-        return;
-    }
-    __syncwarp();
-    issue_query(cur.b, cur.kvh);
-    bool q_pending = true;
-    uint32_t tq = 0;
-
-    for (;;) {
-        // ---- query fragments of the current item -------------------------
-        if (!mbar_wait(bars + 24u, tq & 1u)) break;
-        tq++;
-        q_pending = false;
-        ItemState<1> st;
-        {
-            const bool odd = g & 1;
-            const int hl = g >> 1;
-            float qv[16];
-            float amax = 0.0f;
-            if (hl < P.G) {
-                const uint32_t qa = qarea + (uint32_t)hl * kQRowBytes + 128u * c + (odd ? 64u : 0u);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float4 f = lds_f4(qa + 16u * j);
-                    qv[4 * j] = f.x; qv[4 * j + 1] = f.y; qv[4 * j + 2] = f.z; qv[4 * j + 3] = f.w;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(qv[j]));
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; j++) qv[j] = 0.0f;
-            }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-            amax = warp_max_xor(amax, 1, 2);
-            const int eq = fp16_scale_exp(amax);
-            const float qscale = exp2i(eq);
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
-                const __half2 h = __floats2half2_rn(x0, x1);
-                const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-                const uint32_t keep = odd ? h2_as_u32(l) : h2_as_u32(h);
-                const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? h2_as_u32(h) : h2_as_u32(l), 4);
-                st.qf[0][j] = odd ? got : keep;
-                st.qf[0][8 + j] = odd ? keep : got;
-            }
-            const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
-            st.kfac[0] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
-            st.m_run[0] = -INFINITY;
-            st.l_part[0] = 0.0f;
-            st.z_part[0] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-#pragma unroll
-                for (int k = 0; k < 4; k++) st.acc[0][i][k] = 0.0f;
-        }
-        // the query area is free: the next item's rows go out now
-        const int nxt_np = (int)lds32(bars + 52u);
-        __syncwarp();
-        if (nxt_np > 0) {
-            issue_query((int)lds32(bars + 32u), (int)lds32(bars + 40u));
-            q_pending = true;
-        }
-
-        // ---- pages of the current item -------------------------------------
-        const int tok_first = (cur.start / kBlockSize) * kBlockSize + tau;
-        bool fail = false;
-        for (int k = 0; k < cur_np; k++) {
-            const uint32_t slot = s_con;
-            if (!mbar_wait(bars + 8u * slot, (cbits >> slot) & 1u)) { fail = true; break; }
-            cbits ^= 1u << slot;
-            const bool page_ok = (vbits >> slot) & 1u;
-            // the slot is refilled right after this warp's reads of it
-            auto refill = [&]() {
-                in_flight--;
-                s_con = s_con == wr::kNs - 1 ? 0u : s_con + 1u;
-                __syncwarp();
-                if (iss_left > 0) issue_page();
-            };
-            const int tok0 = tok_first + k * kBlockSize;
-            if (slot == 0)
-                page_math<1, LAYOUT>(st, 0u, o, page_ok, tok0, cur.start, cur.end, lut_sel_src, g, c, src_a, refill,
-                                     1.0f);
-            else if (slot == 1)
-                page_math<1, LAYOUT>(st, (uint32_t)wr::kCol, o, page_ok, tok0, cur.start, cur.end, lut_sel_src, g, c,
-                                     src_a, refill, 1.0f);
-            else
-                page_math<1, LAYOUT>(st, 2u * wr::kCol, o, page_ok, tok0, cur.start, cur.end, lut_sel_src, g, c, src_a,
-                                     refill, 1.0f);
-        }
-        if (fail) break;
-        epilogue<1>(P, st, stg, cur.b, cur.s, cur.kvh, g, c, lane);
-
-        // ---- advance: the next item becomes current -------------------------
-        if (nxt_np == 0) break;  // walk done (nothing in flight: every issued page was consumed)
-        cur.b = (int)lds32(bars + 32u);
-        cur.s = (int)lds32(bars + 36u);
-        cur.kvh = (int)lds32(bars + 40u);
-        cur.start = (int)lds32(bars + 44u);
-        cur.end = (int)lds32(bars + 48u);
-        cur_np = nxt_np;
-        ItemInfo nx;
-        const uint32_t itn = next_item(P, it + it_stride, it_end, it_stride, nx);
-        put_next(nx, itn < it_end ? pages_of(nx) : 0);
-        it = itn;
-        if (iss_next == 1) {
-            iss_next = 0;  // the issue pointer was in the item now current
-        } else if (iss_next == 2) {
-            // it had reached the end of the item now current: on into the new next one
-            const int nnp = (int)lds32(bars + 52u);
-            if (nnp > 0) {
-                iss_next = 1;
-                iss_left = nnp;
-                iss_kvh = (int)lds32(bars + 40u);
-                iss_pos = (int)lds32(bars + 32u) * (int)P.bt_stride + (int)lds32(bars + 44u) / kBlockSize;
-                next_id = __ldg(P.bt + iss_pos);
-            }
-        }
-        while (in_flight < wr::kNs && iss_left > 0) issue_page();
-    }
-    // Normally nothing is in flight here (every page issued was consumed,
-    // no query copy is pending); after a wait gave up, let this warp's copies
-    // land before it leaves.
-    for (int i = 0; i < in_flight; i++) {
-        const uint32_t slot = (s_con + (uint32_t)i) % wr::kNs;
-        if (!mbar_wait(bars + 8u * slot, (cbits >> slot) & 1u)) break;
-        cbits ^= 1u << slot;
-    }
-    if (q_pending) mbar_wait(bars + 24u, tq & 1u);
 }
 
 // True when the compiled kernel launches with enough registers per thread
@@ -1837,49 +1495,6 @@ int launch_ring_t(const Stage1Params& P, const RingMaps& M, cudaStream_t stream,
     return report_launch(launch_pdl(kern, dim3((unsigned)grid), dim3(C::kThreads), C::kSmem, stream, P, M));
 }
 
-// The per-warp-ring kernel (SoA, GQA <= 4); the fused rotation launches it
-// cooperatively with one CTA per SM, like the group ring.
-int launch_wring(const Stage1Params& P, const RingMaps& M, cudaStream_t stream, int num_sms) {
-    auto kern = stage1_wring_kernel<TQB_LAYOUT_SOA>;
-    static thread_local int configured_dev = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured_dev != dev) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, wr::kSmem) != cudaSuccess)
-            return report_launch(cudaGetLastError());
-        configured_dev = dev;
-    }
-    if (P.rot != nullptr) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)num_sms);
-        cfg.blockDim = dim3(wr::kThreads);
-        cfg.dynamicSmemBytes = wr::kSmem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P, M);
-        if (e == cudaErrorCooperativeLaunchTooLarge) {
-            cudaGetLastError();
-            return TQB_ERR_UNSUPPORTED;  // the caller rotates in a kernel of its own
-        }
-        return report_launch(e);
-    }
-    const int64_t need = (P.num_items + wr::kWarps - 1) / wr::kWarps;
-    const int64_t grid = need < num_sms ? need : num_sms;
-    if (grid <= 0) return TQB_OK;
-    return report_launch(launch_pdl(kern, dim3((unsigned)grid), dim3(wr::kThreads), wr::kSmem, stream, P, M));
-}
-
-// TQB_STAGE1_KERNEL selects among the SoA kernels for GQA <= 4: "warp" the
-// per-warp rings, "group" the group ring (the default); read on every call.
-bool warp_rings_selected() {
-    const char* v = getenv("TQB_STAGE1_KERNEL");
-    return v != nullptr && strcmp(v, "warp") == 0;
-}
-
 }  // namespace
 
 bool stage1_ring_supported(const Stage1Params& P) {
@@ -1922,9 +1537,6 @@ bool stage1_ring_supported(const Stage1Params& P) {
 int launch_stage1_ring(const Stage1Params& P, cudaStream_t stream, int num_sms) {
     RingMaps M;
     if (!encode_maps(P, M)) return TQB_ERR_UNSUPPORTED;
-    if (P.layout == TQB_LAYOUT_SOA && P.G <= 4 && warp_rings_selected() &&
-        (int64_t)P.B * P.bt_stride < (int64_t(1) << 31))
-        return launch_wring(P, M, stream, num_sms);
     if (P.layout == TQB_LAYOUT_SOA)
         return P.G <= 4 ? launch_ring_t<1, TQB_LAYOUT_SOA>(P, M, stream, num_sms)
                         : launch_ring_t<2, TQB_LAYOUT_SOA>(P, M, stream, num_sms);
