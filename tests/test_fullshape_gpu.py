@@ -10,7 +10,8 @@ tiles as it does in the bench:
 * c3  B256 x 8192, Hq64/Hk8 (GQA-8, the ring kernel's two-item-per-warp
       instance), 32 splits.
 * c2  B128 ragged, seq_lens U[512, 16384] (seeded), per-sequence splits
-      min(32, ceil(len / 512)), fully shuffled block pool.
+      min(32, ceil(len / 512)), fully shuffled block pool; on one GPU, and
+      as the 8 data-parallel ranks' shares, each decoded on its own.
 * c4  B4 x 131072 over 8 sequence-parallel ranks emulated on one GPU, 74
       local splits per rank; one rank's partials against the oracle on its
       share, and every rank's merged result (peer-memory exchange kernels)
@@ -199,15 +200,46 @@ def test_c3_gqa8_decode(cuda_device):
     _check(got, _decode_oracle(h, 32), w["lens"], 32, what="c3")
 
 
-def test_c2_ragged_decode(cuda_device):
-    """Full c2: B128, seq_lens U[512, 16384], splits min(32, ceil(len/512)),
-    the block pool shuffled with spare blocks."""
+@pytest.fixture(scope="module")
+def c2_ragged(cuda_device):
+    """The c2 batch (B128, seq_lens U[512, 16384], splits min(32,
+    ceil(len/512)), shuffled pool with spare blocks) and its oracle decode."""
     lens = np.random.default_rng(20261201).integers(512, 16384 + 1, size=128).tolist()
     nsp = [min(32, math.ceil(n / 512)) for n in lens]
     w = _build(cuda_device, 14, lens, 32, 8, "soa", pool_extra=64)
     h = _host(w)
+    return w, nsp, _decode_oracle(h, 32, nsp=nsp)
+
+
+def test_c2_ragged_decode(c2_ragged):
+    """Full c2 on one GPU."""
+    w, nsp, ref = c2_ragged
     got = _decode_gpu(w, 32, nsp=nsp)
-    _check(got, _decode_oracle(h, 32, nsp=nsp), lens, 32, nsp=nsp, what="c2")
+    _check(got, ref, w["lens"], 32, nsp=nsp, what="c2")
+
+
+def test_c2_data_parallel_rank_shares(c2_ragged):
+    """c2 split over 8 data-parallel ranks as the 8-GPU bench splits it
+    (sharding.plan_batch): each rank's share of 16 sequences is decoded on
+    its own, as one rank does.  A share has so few non-empty tiles that the
+    Stage1 tile walk cuts it by item count (at most two tiles per group),
+    the cut none of the one-GPU shapes reach."""
+    w, nsp, ref = c2_ragged
+    lens = w["lens"]
+    B, Hq = len(lens), w["Hq"]
+    mid = np.full((B, Hq, 32, D + 1), SENTINEL, np.float32)
+    out = np.empty((B, Hq, D), np.float32)
+    lse = np.empty((B, Hq), np.float32)
+    plan = sharding.plan_batch(lens, 8)
+    assert sorted(i for r in plan for i in r) == list(range(B))
+    dev = w["q"].device
+    for idx in plan:
+        it = torch.tensor(idx, dtype=torch.long, device=dev)
+        part = dict(w, q=w["q"][it].contiguous(), bt=w["bt"][it].contiguous(), sl=w["sl"][it].contiguous(),
+                    lens=[lens[i] for i in idx])
+        m, o, l = _decode_gpu(part, 32, nsp=[nsp[i] for i in idx])
+        mid[idx], out[idx], lse[idx] = m, o, l
+    _check((mid, out, lse), ref, lens, 32, nsp=nsp, what="c2 rank shares")
 
 
 def test_c4_sequence_parallel_8_ranks(cuda_device):
