@@ -1069,10 +1069,14 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
         l = l > 0.0f ? l : 1.0f;  // safe_l (reference/soa_decode_v1.py:311)
         const float z = warp_sum_xor(st.z_part[nt], 4, 16);
         const float inv = rcp_approx(l);
-        auto val = [&](int i, int hi) {
-            return (((hi ? st.acc[nt][i][2] + st.acc[nt][i][3] : st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale +
-                     z) * inv);
-        };
+        // the lane's 16 outputs, formed once (not inside the per-pass branch,
+        // which the warp issues twice)
+        float val[8][2];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            val[i][0] = ((st.acc[nt][i][0] + st.acc[nt][i][1]) * kCodeScale + z) * inv;
+            val[i][1] = ((st.acc[nt][i][2] + st.acc[nt][i][3]) * kCodeScale + z) * inv;
+        }
         const int heads = min(4, P.G - 4 * nt);
 #pragma unroll
         for (int pass = 0; pass < 2; pass++) {
@@ -1082,8 +1086,8 @@ __device__ __forceinline__ void epilogue(const Stage1Params& P, const ItemState<
                 for (int j = 0; j < 4; j++)  // dims 16g + 4j .. 16g + 4j + 3
                     asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(
                                      col + (uint32_t)r * 512u + ((uint32_t)((4 * g + j) ^ r) << 4)),
-                                 "f"(val(2 * j, 0)), "f"(val(2 * j, 1)), "f"(val(2 * j + 1, 0)),
-                                 "f"(val(2 * j + 1, 1))
+                                 "f"(val[2 * j][0]), "f"(val[2 * j][1]), "f"(val[2 * j + 1][0]),
+                                 "f"(val[2 * j + 1][1])
                                  : "memory");
             }
             __syncwarp();
