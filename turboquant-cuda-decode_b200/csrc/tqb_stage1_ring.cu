@@ -395,8 +395,10 @@ __device__ __forceinline__ uint32_t cut_tile(const Stage1Params& P, const SeqSpl
 }
 // Tile walk of group gi of this CTA: tiles first, first + stride, ... below
 // end, in res[0..2].  A batch whose sequences all have the same length and
-// split count takes the round-robin walk (already balanced); any other
-// batch the contiguous ranges of the weight cut.  One warp (compact loops:
+// split count is cut into equal contiguous tile ranges (already balanced;
+// consecutive tiles are consecutive splits of one sequence, so the compute
+// warps keep their query fragments across them); any other batch takes the
+// contiguous ranges of the weight cut.  One warp (compact loops:
 // this code runs once, cold, ahead of every other warp's first tile).
 __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uint32_t num_tiles, uint32_t (&res)[3],
                           int lane) {
@@ -422,9 +424,11 @@ __device__ void tile_walk(const Stage1Params& P, int gi, int groups_per_cta, uin
     cnt = warp_sum_ll(cnt);
     if (__reduce_min_sync(0xffffffffu, lmin) == __reduce_max_sync(0xffffffffu, lmax) &&
         __reduce_min_sync(0xffffffffu, nmin) == __reduce_max_sync(0xffffffffu, nmax)) {
-        res[0] = g;
-        res[1] = num_tiles;
-        res[2] = cuts;
+        // contiguous ranges: consecutive tiles of a group are consecutive
+        // splits of one sequence, so its warps keep their query fragments
+        res[0] = (uint32_t)((uint64_t)g * num_tiles / cuts);
+        res[1] = (uint32_t)((uint64_t)(g + 1) * num_tiles / cuts);
+        res[2] = 1u;
         return;
     }
     res[2] = 1u;
@@ -1211,6 +1215,10 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     const int src_a = 4 * (((c & 1) << 1) | (c >> 1)) + (g >> 1);
     uint32_t tq = 0;     // tiles done (query-barrier phase)
     uint32_t cbits = 0;  // bit s: parity of the pages slot s has delivered
+    // The query fragments (and score factors) stay from one tile to the
+    // next while the item's sequence and KV head do not change.
+    ItemState<NT> st;
+    int prev_b = -1, prev_kvh = -1;
 
     for (uint32_t t = t_first; t < t_end; t += t_stride) {
         ItemInfo ir;
@@ -1226,9 +1234,12 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 
         // ---- query fragments from the tile's query rows ---------------------
         if (!mbar_wait(gs.q_full<NS>(), tq & 1u)) return;
-        ItemState<NT> st;
+        const bool reuse = b == prev_b && kvh == prev_kvh;
+        prev_b = my_np > 0 ? b : -1;
+        prev_kvh = kvh;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
+          if (!reuse) {
             // Lanes g and g^1 share a head and dims 32c .. 32c+31 but keep the
             // hi (even g) or lo (odd g) parts: each converts 16 of the 32
             // floats and the pair swaps the halves the other keeps.
@@ -1266,6 +1277,7 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
             }
             const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
             st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
+          }
             st.m_run[nt] = -INFINITY;
             st.l_part[nt] = 0.0f;
             st.z_part[nt] = 0.0f;
