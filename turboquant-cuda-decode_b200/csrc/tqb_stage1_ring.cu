@@ -646,7 +646,13 @@ __device__ __forceinline__ void produce(const Stage1Params& P, const RingMaps& M
         ItemInfo irn;
         int npn = 0, np_tile_n = 0;
         const uint32_t tn = next_tile(t + t_stride, irn, npn, np_tile_n);
-        bool next_query_sent = tn >= t_end;
+        // When every item of the next tile keeps its sequence and KV head,
+        // the query area already holds its rows (the compute warps keep
+        // their fragments): no copy, and no handoff on the query barriers.
+        const bool same_rows =
+            tn < t_end && __all_sync(0xffffffffu, lane >= kGroupWarps || (np > 0 && npn > 0 && irn.b == ir.b &&
+                                                                           irn.kvh == ir.kvh));
+        bool next_query_sent = tn >= t_end || same_rows;
         // Runs of consecutive items sharing one (b, s): their head slices are
         // adjacent in every token row, so one copy per row serves a run.
         const int key = np > 0 ? ir.b * P.S + ir.s : -1 - lane;
@@ -1219,6 +1225,9 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
     // next while the item's sequence and KV head do not change.
     ItemState<NT> st;
     int prev_b = -1, prev_kvh = -1;
+    // lanes 0-7: (b, KV head) of item `lane` of the previous non-empty tile
+    // (b = -1: none or empty), the test the producer makes for the rows
+    int lane_b = -1, lane_kvh = -1;
 
     for (uint32_t t = t_first; t < t_end; t += t_stride) {
         ItemInfo ir;
@@ -1233,7 +1242,11 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         const int my_np = __shfl_sync(0xffffffffu, np, w);
 
         // ---- query fragments from the tile's query rows ---------------------
-        if (!mbar_wait(gs.q_full<NS>(), tq & 1u)) return;
+        const bool same_rows = __all_sync(0xffffffffu, lane >= kGroupWarps || (np > 0 && lane_b >= 0 &&
+                                                                              ir.b == lane_b && ir.kvh == lane_kvh));
+        lane_b = np > 0 ? ir.b : -1;
+        lane_kvh = ir.kvh;
+        if (!same_rows && !mbar_wait(gs.q_full<NS>(), tq & 1u)) return;
         const bool reuse = b == prev_b && kvh == prev_kvh;
         prev_b = my_np > 0 ? b : -1;
         prev_kvh = kvh;
@@ -1286,8 +1299,10 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
 #pragma unroll
                 for (int k = 0; k < 4; k++) st.acc[nt][i][k] = 0.0f;
         }
-        mbar_arrive(gs.q_empty<NS>());  // all 32 lanes
-        tq++;
+        if (!same_rows) {
+            mbar_arrive(gs.q_empty<NS>());  // all 32 lanes
+            tq++;
+        }
 
         // ---- pages: slot S of the ring holds pages k = S (mod NS) ------------
         const int tok_first = (start / kBlockSize) * kBlockSize + tau;
