@@ -1242,6 +1242,9 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         const int my_np = __shfl_sync(0xffffffffu, np, w);
 
         // ---- query fragments from the tile's query rows ---------------------
+        // Every item keeps its sequence and KV head: the producer copied no
+        // rows and neither side uses the query barriers (its own test, on the
+        // same items).  One warp's item keeping them: its fragments stay.
         const bool same_rows = __all_sync(0xffffffffu, lane >= kGroupWarps || (np > 0 && lane_b >= 0 &&
                                                                               ir.b == lane_b && ir.kvh == lane_kvh));
         lane_b = np > 0 ? ir.b : -1;
@@ -1252,45 +1255,45 @@ __device__ __forceinline__ void consume(const Stage1Params& P, const GroupSmem& 
         prev_kvh = kvh;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-          if (!reuse) {
-            // Lanes g and g^1 share a head and dims 32c .. 32c+31 but keep the
-            // hi (even g) or lo (odd g) parts: each converts 16 of the 32
-            // floats and the pair swaps the halves the other keeps.
-            const int hl = (g >> 1) + 4 * nt;
-            const bool odd = g & 1;
-            float qv[16];
-            float amax = 0.0f;
-            if (my_np > 0 && hl < P.G) {
-                const uint32_t qa = gs.qarea + (uint32_t)(w * C::kHeadsPerWarp + hl) * kQRowBytes + 128u * c +
-                                    (odd ? 64u : 0u);
+            if (!reuse) {
+                // Lanes g and g^1 share a head and dims 32c .. 32c+31 but keep the
+                // hi (even g) or lo (odd g) parts: each converts 16 of the 32
+                // floats and the pair swaps the halves the other keeps.
+                const int hl = (g >> 1) + 4 * nt;
+                const bool odd = g & 1;
+                float qv[16];
+                float amax = 0.0f;
+                if (my_np > 0 && hl < P.G) {
+                    const uint32_t qa = gs.qarea + (uint32_t)(w * C::kHeadsPerWarp + hl) * kQRowBytes + 128u * c +
+                                        (odd ? 64u : 0u);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float4 f = lds_f4(qa + 16u * j);
-                    qv[4 * j] = f.x; qv[4 * j + 1] = f.y; qv[4 * j + 2] = f.z; qv[4 * j + 3] = f.w;
+                    for (int j = 0; j < 4; j++) {
+                        const float4 f = lds_f4(qa + 16u * j);
+                        qv[4 * j] = f.x; qv[4 * j + 1] = f.y; qv[4 * j + 2] = f.z; qv[4 * j + 3] = f.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(qv[j]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) qv[j] = 0.0f;
                 }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+                amax = warp_max_xor(amax, 1, 2);
+                const int eq = fp16_scale_exp(amax);
+                const float qscale = exp2i(eq);
 #pragma unroll
-                for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(qv[j]));
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; j++) qv[j] = 0.0f;
+                for (int j = 0; j < 8; j++) {
+                    const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
+                    const __half2 h = __floats2half2_rn(x0, x1);
+                    const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+                    const uint32_t keep = odd ? h2_as_u32(l) : h2_as_u32(h);
+                    const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? h2_as_u32(h) : h2_as_u32(l), 4);
+                    st.qf[nt][j] = odd ? got : keep;      // fragments 0-7: floats of the even lane
+                    st.qf[nt][8 + j] = odd ? keep : got;  // fragments 8-15: floats of the odd lane
+                }
+                const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
+                st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
             }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-            amax = warp_max_xor(amax, 1, 2);
-            const int eq = fp16_scale_exp(amax);
-            const float qscale = exp2i(eq);
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float x0 = qv[2 * j] * qscale, x1 = qv[2 * j + 1] * qscale;
-                const __half2 h = __floats2half2_rn(x0, x1);
-                const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-                const uint32_t keep = odd ? h2_as_u32(l) : h2_as_u32(h);
-                const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? h2_as_u32(h) : h2_as_u32(l), 4);
-                st.qf[nt][j] = odd ? got : keep;      // fragments 0-7: floats of the even lane
-                st.qf[nt][8 + j] = odd ? keep : got;  // fragments 8-15: floats of the odd lane
-            }
-            const int eq_head = __shfl_sync(0xffffffffu, eq, 8 * c);
-            st.kfac[nt] = P.attn_scale * kLog2e * exp2i(-eq_head) * exp2i(-ec);
-          }
             st.m_run[nt] = -INFINITY;
             st.l_part[nt] = 0.0f;
             st.z_part[nt] = 0.0f;
